@@ -1,0 +1,227 @@
+"""CPU ORACLE — test infrastructure only.
+
+ctypes wrappers over
+
+* ``oracle/_ref/liboracle.so`` — the plain-C restatement of the reference
+  algorithms (``oracle/kvm_oracle.c``), and
+* ``oracle/_ref/libkvref.so`` — the reference's own CPU selection code compiled
+  from its sources (``oracle/Makefile`` target ``ref``; present only where the
+  reference sources were available when it was built).
+
+Only tests, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference
+arm may import this module. The product package ``kvmem_b200`` never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "_ref")
+REFERENCE_SRC = os.environ.get("KVM_REFERENCE_SRC", "/root/reference")
+
+F32, F16, BF16, Q8_0, Q4_0, Q5_0 = 0, 1, 2, 3, 4, 5
+OK, ERR_INVALID, ERR_RUNTIME = 0, 1, 2
+
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+
+
+def build(ref: bool = False) -> None:
+    """Compile the C restatement and, with ref=True (and the reference sources
+    present), the reference's own CPU selection library."""
+    subprocess.check_call(["make", "-s", "-C", HERE], stdout=subprocess.DEVNULL)
+    if ref and os.path.isdir(os.path.join(REFERENCE_SRC, "kvmem", "src", "host")):
+        subprocess.check_call(["make", "-s", "-j8", "-C", HERE, "ref", f"REF={REFERENCE_SRC}"],
+                              stdout=subprocess.DEVNULL)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(REF_DIR, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.kvo_page_mass.argtypes = [
+            C.c_void_p, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64,
+            C.c_void_p, C.c_int, C.c_uint64, C.c_uint64, C.c_uint64,
+            C.c_void_p, C.c_uint64,
+            C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+            C.c_uint64, C.c_uint32, C.c_double, C.c_double, C.c_uint32, _f64p]
+        L.kvo_recall_fp16.argtypes = [C.c_float, C.POINTER(C.c_float)]
+        L.kvo_meank_scores.argtypes = [_f32p, _f32p, _u32p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                       C.c_uint32, C.c_uint32, C.c_uint32, _u8p, C.c_int, C.c_double, _f64p]
+        L.kvo_query_score_frame.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                            _u32p, C.c_uint32, C.c_uint64, _u64p, _u32p, _u8p, _u8p,
+                                            C.POINTER(C.c_uint64)]
+        L.kvo_pick_scored.argtypes = [C.c_uint32, _u32p, _f64p, C.c_uint32, _u32p, C.c_uint32, C.c_uint32,
+                                      C.c_int, C.c_uint32, _u32p, C.c_uint32, _u32p, C.POINTER(C.c_uint32)]
+        L.kvo_plan_residency.argtypes = [_u64p, C.c_uint32, _u64p, C.c_uint32, C.c_int,
+                                         _u64p, C.POINTER(C.c_uint32), _u64p, C.POINTER(C.c_uint32),
+                                         _u64p, C.POINTER(C.c_uint32)]
+        L.kvo_decode.argtypes = [C.c_int, C.c_void_p, C.c_uint32]
+        L.kvo_decode.restype = C.c_double
+        L.kvo_row_bytes.argtypes = [C.c_int, C.c_uint32]
+        L.kvo_row_bytes.restype = C.c_uint64
+        _lib = L
+    return _lib
+
+
+def ref():
+    """The reference's compiled CPU selection library, or None when absent."""
+    global _ref
+    if _ref is None:
+        path = os.path.join(REF_DIR, "libkvref.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        L.kvref_query_score_frame.argtypes = lib().kvo_query_score_frame.argtypes
+        L.kvref_page_softmax_scores.argtypes = [
+            _f32p, _u32p, _f32p, _u32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+            C.c_uint32, C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, _u32p, C.c_uint32, C.c_int,
+            C.c_float, _f64p, C.c_uint64]
+        L.kvref_recall_fp16.argtypes = [C.c_float, C.POINTER(C.c_float)]
+        L.kvref_pick_scored.argtypes = lib().kvo_pick_scored.argtypes
+        L.kvref_plan_residency.argtypes = lib().kvo_plan_residency.argtypes
+        _ref = L
+    return _ref
+
+
+def row_bytes(ktype: int, dim: int) -> int:
+    return int(lib().kvo_row_bytes(ktype, dim))
+
+
+def page_mass(q: np.ndarray, q_type: int, k: np.ndarray, k_type: int, *, layers: int, rows: int,
+              heads: int, kv_heads: int, dim: int, tokens: int, page_tokens: int, scale: float,
+              softcap: float = 0.0, groups: int = 1, mask: np.ndarray | None = None,
+              q_strides=None, k_strides=None) -> np.ndarray:
+    """FP64 per-token page mass [layers, groups, rows, pages].
+
+    q: bytes of [layers][rows][heads][dim] elements of q_type (dense unless
+    q_strides=(layer, row, head) byte strides are given).
+    k: bytes of [layers][tokens_alloc][kv_heads] rows of k_type (dense unless
+    k_strides=(layer, token, head) byte strides are given).
+    mask: optional f32 [rows][>=tokens] bias.
+    """
+    esz = {F32: 4, F16: 2, BF16: 2}[q_type]
+    if q_strides is None:
+        q_strides = (rows * heads * dim * esz, heads * dim * esz, dim * esz)
+    rb = row_bytes(k_type, dim)
+    pages = -(-tokens // page_tokens)
+    if k_strides is None:
+        k_strides = (pages * page_tokens * kv_heads * rb, kv_heads * rb, rb)
+    qb = np.ascontiguousarray(q).view(np.uint8)
+    kb = np.ascontiguousarray(k).view(np.uint8)
+    out = np.zeros(layers * groups * rows * pages, np.float64)
+    mptr, mrow = None, 0
+    if mask is not None:
+        mask = np.ascontiguousarray(mask, np.float32)
+        mptr, mrow = mask.ctypes.data, mask.shape[1]
+    rc = lib().kvo_page_mass(qb.ctypes.data, q_type, *q_strides, kb.ctypes.data, k_type, *k_strides,
+                             mptr, mrow, layers, rows, heads, kv_heads, dim, tokens, page_tokens,
+                             scale, softcap, groups, out)
+    if rc:
+        raise ValueError(f"oracle page_mass rejected its geometry (rc={rc})")
+    return out.reshape(layers, groups, rows, pages)
+
+
+def recall_fp16(value: float, use_ref: bool = False) -> float:
+    out = C.c_float()
+    fn = ref().kvref_recall_fp16 if use_ref else lib().kvo_recall_fp16
+    rc = fn(value, C.byref(out))
+    if rc:
+        raise ValueError("recall operand rejected")
+    return out.value
+
+
+def meank_scores(means: np.ndarray, q: np.ndarray, layer_rows, *, heads: int, kv_heads: int, dim: int,
+                 score_mask, aggregation: int = 0, scale: float = 0.0) -> np.ndarray:
+    """FP64 Mean-K page softmax. means [L][P][Hkv*D] f32, q [L][R][Hq*D] f32."""
+    means = np.ascontiguousarray(means, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    L, P, _ = means.shape
+    R = q.shape[1]
+    out = np.zeros(P, np.float64)
+    rc = lib().kvo_meank_scores(means.reshape(-1), q.reshape(-1), np.ascontiguousarray(layer_rows, np.uint32),
+                                L, R, heads, kv_heads, dim, P, np.ascontiguousarray(score_mask, np.uint8),
+                                aggregation, scale, out)
+    if rc:
+        raise ValueError(f"oracle meank rejected its operands (rc={rc})")
+    return out
+
+
+def query_score_frame(accepted, block, budget, sink, recent, fixed=(), use_ref=False):
+    n_cap = accepted // block + 2
+    starts = np.zeros(n_cap, np.uint64)
+    counts = np.zeros(n_cap, np.uint32)
+    sm = np.zeros(n_cap, np.uint8)
+    tm = np.zeros(n_cap, np.uint8)
+    n = C.c_uint64()
+    fx = np.ascontiguousarray(list(fixed) or [0], np.uint32)
+    fn = ref().kvref_query_score_frame if use_ref else lib().kvo_query_score_frame
+    rc = fn(accepted, block, budget, sink, recent, fx, len(fixed), n_cap, starts, counts, sm, tm, C.byref(n))
+    if rc:
+        raise ValueError(f"query_score_frame rejected (rc={rc})")
+    k = n.value
+    return dict(starts=starts[:k], counts=counts[:k], score_mask=sm[:k], transport_mask=tm[:k],
+                accepted_through=accepted)
+
+
+def pick_scored(n, candidates, scores, mandatory, budget, signed=False, block_tokens=1, ranges=(),
+                use_ref=False):
+    """Returns (status, ascending ids or None)."""
+    cand = np.ascontiguousarray(candidates, np.uint32)
+    sc = np.ascontiguousarray(scores, np.float64)
+    mand = np.ascontiguousarray(list(mandatory) or [0], np.uint32)
+    rg = np.ascontiguousarray(np.asarray(ranges, np.uint32).reshape(-1) if len(ranges) else [0, 0], np.uint32)
+    out = np.zeros(max(n, 1), np.uint32)
+    cnt = C.c_uint32()
+    fn = ref().kvref_pick_scored if use_ref else lib().kvo_pick_scored
+    rc = fn(n, cand if len(cand) else np.zeros(1, np.uint32), sc if len(sc) else np.zeros(1),
+            len(cand), mand, len(mandatory), budget, int(signed), block_tokens, rg, len(ranges), out,
+            C.byref(cnt))
+    return rc, (out[:cnt.value].copy() if rc == 0 else None)
+
+
+def plan_residency(resident, selected, force_reload=False, use_ref=False):
+    a = np.ascontiguousarray(list(resident) or [0], np.uint64)
+    b = np.ascontiguousarray(list(selected) or [0], np.uint64)
+    na, nb = len(resident), len(selected)
+    ev = np.zeros(max(na, 1), np.uint64)
+    rt = np.zeros(max(na, 1), np.uint64)
+    rs = np.zeros(max(nb, 1), np.uint64)
+    ne, nr, ns = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    fn = ref().kvref_plan_residency if use_ref else lib().kvo_plan_residency
+    rc = fn(a, na, b, nb, int(force_reload), ev, C.byref(ne), rt, C.byref(nr), rs, C.byref(ns))
+    if rc:
+        return rc, None
+    return 0, dict(evict=ev[:ne.value].copy(), retain=rt[:nr.value].copy(), restore=rs[:ns.value].copy())
+
+
+def ref_page_softmax_scores(sums, counts, q, layer_rows, *, heads, kv_heads, dim, block, accepted, budget,
+                            sink, recent, fixed=(), aggregation=0, scale=0.0):
+    """The reference's own page_softmax_scores over a RawKvStore built from K sums."""
+    sums = np.ascontiguousarray(sums, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    L, P, _ = sums.shape
+    R = q.shape[1]
+    out = np.zeros(P + 1, np.float64)
+    fx = np.ascontiguousarray(list(fixed) or [0], np.uint32)
+    rc = ref().kvref_page_softmax_scores(sums.reshape(-1), np.ascontiguousarray(counts, np.uint32),
+                                         q.reshape(-1), np.ascontiguousarray(layer_rows, np.uint32), L, R,
+                                         heads, kv_heads, dim, block, accepted, budget, sink, recent, fx,
+                                         len(fixed), aggregation, scale, out, P)
+    if rc:
+        raise ValueError(f"reference page_softmax_scores rejected (rc={rc})")
+    return out[:P]
