@@ -1,0 +1,279 @@
+/*
+ * kvm_recall.h — C ABI of the B200 history-recall path.
+ *
+ * The path scores every page of a paged KV history against the current
+ * queries (page-softmax mass under GQA), selects the top-k pages with pinned
+ * keep-pages, plans the residency delta, and stages the selected pages' K/V
+ * bytes from mapped pinned host memory into a device paged cache.
+ *
+ * Conventions
+ *  - Plain C: opaque handles, plain pointers and sizes, no exceptions.
+ *  - Every entry point returns a kvm_status. Work is enqueued on the
+ *    caller's CUDA stream (`stream` is a cudaStream_t; NULL = legacy default).
+ *  - Device-side failures (a non-finite score, a bounded wait that ran out)
+ *    are recorded in the context and reported by kvm_ctx_status().
+ *  - One context per execution state; a context is never used by two host
+ *    threads at once (the reference rule, src/adapter/llama-kvmem-hooks.h:54-57).
+ *  - Device pointers must belong to the context's device.
+ */
+#ifndef KVM_RECALL_H
+#define KVM_RECALL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 1..8 follow kvmem::MemoryErrorCode in order
+ * (kvmem/include/kvmem/memory_contract.hpp:14-17); the rest stand for the
+ * reference's std::invalid_argument / std::length_error / CUDA runtime_error. */
+typedef enum kvm_status {
+    KVM_OK = 0,
+    KVM_ERR_INVALID_PLAN = 1,
+    KVM_ERR_UNSUPPORTED = 2,
+    KVM_ERR_BUDGET_EXCEEDED = 3,
+    KVM_ERR_STALE = 4,
+    KVM_ERR_PENDING = 5,
+    KVM_ERR_TRANSFER_FAILED = 6,
+    KVM_ERR_DISCONNECTED = 7,
+    KVM_ERR_INVALID_SESSION = 8,
+    KVM_ERR_INVALID_ARGUMENT = 9, /* geometry / operand rejected (std::invalid_argument) */
+    KVM_ERR_LENGTH = 10,          /* exceeds workspace or launch range (std::length_error) */
+    KVM_ERR_CUDA = 11,            /* CUDA runtime failure (std::runtime_error) */
+    KVM_ERR_TIMEOUT = 12,         /* a bounded wait ran out */
+    KVM_ERR_NONFINITE = 13        /* non-finite / negative score or non-finite FP16 operand
+                                     (the reference's std::invalid_argument for those) */
+} kvm_status;
+
+/* Element / block encodings. */
+typedef enum kvm_type {
+    KVM_F32 = 0,
+    KVM_F16 = 1,
+    KVM_BF16 = 2,
+    KVM_Q8_0 = 3, /* GGUF block of 32: {fp16 d; int8 qs[32]}              34 B */
+    KVM_Q4_0 = 4, /* GGUF block of 32: {fp16 d; uint8 qs[16]} (nibble-8)  18 B */
+    KVM_Q5_0 = 5  /* GGUF block of 32: {fp16 d; uint8 qh[4]; uint8 qs[16]} 22 B */
+} kvm_type;
+
+typedef struct kvm_ctx kvm_ctx;
+typedef struct kvm_pool kvm_pool;
+
+/* Current-step queries: element (l, r, h, d) at
+ * data + l*layer_stride + r*row_stride + h*head_stride + d*sizeof(type).
+ * type F32, F16 or BF16; device memory. */
+typedef struct kvm_query {
+    const void* data;
+    int32_t type;
+    uint32_t rows;
+    uint64_t layer_stride, row_stride, head_stride;
+} kvm_query;
+
+/* K history in HBM, token-major rows as in the engine's K cache view
+ * [D, T, Hkv] (src/adapter/llama-kvmem-attention-cuda.cu:76): row (l, t, kvh)
+ * at data + l*layer_stride + t*token_stride + kvh*head_stride.
+ * The scorer needs the dense layout
+ *   head_stride = row_bytes(type, D), token_stride = kv_heads * head_stride,
+ * whole pages allocated (capacity_tokens >= pages * page_tokens) and 16-byte
+ * aligned layer bases; anything else returns KVM_ERR_UNSUPPORTED, as the
+ * reference's score() returns false for inputs it does not handle. */
+typedef struct kvm_kcache {
+    const void* data;
+    int32_t type;
+    uint32_t reserved;
+    uint64_t layer_stride, token_stride, head_stride;
+    uint64_t capacity_tokens;
+} kvm_kcache;
+
+/* One scoring problem. */
+typedef struct kvm_score_desc {
+    uint32_t layers, q_heads, kv_heads, head_dim;
+    uint64_t tokens;      /* visible history: token t takes part iff t < tokens */
+    uint32_t page_tokens; /* tokens per page ("block") */
+    uint32_t groups;      /* 1: mass averaged over all query heads (reference `average`);
+                             kv_heads: averaged over the query heads of each KV head */
+    float scale;          /* logit scale; 0 selects 1/sqrt(head_dim) */
+    float softcap;        /* > 0: logit = softcap * tanh(logit / softcap) */
+    const void* mask;     /* optional device bias per (row, token), type mask_type (F32/F16);
+                             a non-finite bias hides the token */
+    int32_t mask_type;
+    uint32_t reserved;
+    uint64_t mask_row_stride; /* bytes between rows of the mask */
+} kvm_score_desc;
+
+/* ---------------------------------------------------------------- context */
+
+/* Replaces the lazily created device/stream state of llama_kvmem_attention_cuda
+ * (src/adapter/llama-kvmem-attention-cuda.cu:131-156) and of PageSoftmaxCuda
+ * (kvmem/src/cuda/page_softmax.cu:156-175). */
+int kvm_ctx_create(int device, kvm_ctx** out);
+int kvm_ctx_destroy(kvm_ctx* ctx);
+int kvm_ctx_device(const kvm_ctx* ctx);
+
+/* Reads and clears the device-side status word (synchronises `stream`).
+ * Replaces the exceptions the reference throws from inside score()/pick. */
+int kvm_ctx_status(kvm_ctx* ctx, void* stream);
+
+/* Workspace: bytes of device scratch kvm_score_pages needs for `rows` query
+ * rows; the context grows its own allocation on demand unless a workspace has
+ * been bound. Binding mirrors PageSoftmaxCuda's borrowed-workspace constructor
+ * (kvmem/include/kvmem/page_softmax_cuda.hpp:13-15): the pointer must be
+ * 256-byte aligned device memory of the context's device, and a later call
+ * that would need more returns KVM_ERR_LENGTH before any launch
+ * (kvmem/src/cuda/page_softmax.cu:34). */
+size_t kvm_score_workspace_bytes(const kvm_score_desc* desc, uint32_t rows);
+int kvm_ctx_bind_workspace(kvm_ctx* ctx, void* workspace, size_t bytes);
+size_t kvm_ctx_device_bytes(const kvm_ctx* ctx);
+
+/* ------------------------------------------------------------ page scoring */
+
+/* Per-token page mass. Replaces llama_kvmem_attention_cuda::score
+ * (src/adapter/llama-kvmem-attention-cuda.cu:146-193; kernels page_lse /
+ * normalize / average at :59-121):
+ *   lse[l,r,h,p]   = log sum_{t in p, t < tokens} exp(scale*<q_lrh, K_l,t,h/G> [softcap] + bias_rt)
+ *   prob[l,r,h,p]  = exp(lse - M_lrh) / Z_lrh,  M, Z over all pages of layer l
+ *   mass_rows[l,g,r,p] = mean over the query heads h of group g of prob[l,r,h,p]
+ *   mass_mean[l,g,p]   = mean over r of mass_rows[l,g,r,p]
+ * Outputs are device f32 arrays (either may be NULL):
+ *   mass_rows [layers][groups][rows][pages], mass_mean [layers][groups][pages].
+ * q8_0 / q4_0 / q5_0 keys are dequantised in registers. */
+int kvm_score_pages(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                    float* mass_rows, float* mass_mean, void* stream);
+
+/* ------------------------------------------------------------------ top-k */
+
+/* Budgeted top-k with keep pages, one selection per score row. Replaces
+ * KvMemStore::pick_scored_blocks (kvmem/src/host/kvmem_store.cpp:418-451)
+ * for candidates = all pages of the row and no media groups:
+ *   keep pages first (an out-of-range keep is KVM_ERR_INVALID_ARGUMENT, more
+ *   distinct keeps than `budget` is KVM_ERR_BUDGET_EXCEEDED, both before any
+ *   launch), then pages by (score desc, page id desc) until `budget` pages are
+ *   kept; output ascending.
+ * scores: device f32 [nrows][score_stride]; keep: host u32 [nkeep].
+ * out_ids: device u32 [nrows][out_stride], out_n: device u32 [nrows].
+ * A non-finite score, or a negative one without signed_scores, sets
+ * KVM_ERR_NONFINITE in the context status and that row's out_n to 0. */
+int kvm_select_topk(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
+                    const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
+                    uint32_t* out_ids, uint32_t* out_n, uint32_t out_stride, void* stream);
+
+/* -------------------------------------------------------- residency + stage-in */
+
+/* Device residency table for `rows` independent selections (one per layer or
+ * per (layer, KV head)), each over `pages` logical pages and `slots` cache
+ * slots. Holds the resident set that plan_residency consumes
+ * (kvmem/src/host/memory_contract.cpp:135-150). All slots start free. */
+int kvm_pool_create(kvm_ctx* ctx, uint32_t rows, uint32_t pages, uint32_t slots, kvm_pool** out);
+int kvm_pool_destroy(kvm_pool* pool);
+int kvm_pool_reset(kvm_pool* pool, void* stream);
+
+/* Stage-in geometry: page (row i, page p) of plane j (0 = K, 1 = V; `planes`
+ * of them) is `bytes[j]` contiguous bytes at host_base[j] + i*host_row_stride[j]
+ * + p*host_page_stride[j] in mapped pinned host memory (cudaHostAlloc /
+ * cudaHostRegister), written to dev_base[j] + i*dev_row_stride[j] +
+ * slot*dev_slot_stride[j] in device memory. Replaces write_block_to_gpu's
+ * destination arithmetic (src/adapter/llama-memory-kvmem.cpp:4475-4486). */
+typedef struct kvm_stage_layout {
+    uint32_t planes;
+    uint32_t reserved;
+    const void* host_base[2];
+    uint64_t host_row_stride[2], host_page_stride[2];
+    void* dev_base[2];
+    uint64_t dev_row_stride[2], dev_slot_stride[2];
+    uint64_t bytes[2];
+} kvm_stage_layout;
+
+/* Residency delta on the device for every row: evict = resident \ selected,
+ * retain = resident ∩ selected, restore = selected \ resident (all resident /
+ * all selected when force_reload), the plan_residency rule
+ * (kvmem/src/host/memory_contract.cpp:135-150). Restored pages take the freed
+ * slots in ascending page / slot order; the table is updated in place and the
+ * restore list is kept for kvm_stagein_pool. sel_ids / sel_n are the outputs
+ * of kvm_select_topk (device). Optional device outputs (may be NULL):
+ * n_restore[rows], n_evict[rows]. */
+int kvm_plan_residency(kvm_ctx* ctx, kvm_pool* pool, const uint32_t* sel_ids, const uint32_t* sel_n,
+                       uint32_t sel_stride, int force_reload, uint32_t* n_restore, uint32_t* n_evict,
+                       void* stream);
+
+/* Device-initiated gather of every planned restore from mapped pinned host
+ * memory into the device cache (replaces kvmem_stagein_enqueue_v +
+ * kvmem_stagein_flush, src/adapter/llama-kvmem-stagein.cu:673-881, without
+ * the pinned slab and the per-item D2D copies). `ctas` bounds the SMs the
+ * gather occupies (0 = default). Asynchronous on `stream`. */
+int kvm_stagein_pool(kvm_ctx* ctx, kvm_pool* pool, const kvm_stage_layout* layout, uint32_t ctas, void* stream);
+
+/* Explicit copy list (the form of kvmem_stagein_enqueue_v / kvmem_d2d_batched,
+ * src/adapter/llama-kvmem-stagein.cu:861,1006): n host ops {src, dst, bytes};
+ * src may be mapped pinned host or device memory, dst device memory. */
+typedef struct kvm_copy {
+    const void* src;
+    void* dst;
+    uint64_t bytes;
+} kvm_copy;
+int kvm_stagein_copies(kvm_ctx* ctx, const kvm_copy* ops, uint32_t n, uint32_t ctas, void* stream);
+
+/* Bounded host wait for everything enqueued on `stream`; returns
+ * KVM_ERR_TIMEOUT after timeout_us, else the context status
+ * (replaces kvmem_stagein_sync_checked, src/adapter/llama-kvmem-stagein.cu:656). */
+int kvm_stagein_wait(kvm_ctx* ctx, void* stream, uint64_t timeout_us);
+
+/* Pool introspection (tests): copies the device tables to host arrays
+ * slot_of[rows][pages] (-1 = not resident) and page_of[rows][slots]. */
+int kvm_pool_read(kvm_pool* pool, int32_t* slot_of, int32_t* page_of, void* stream);
+
+/* -------------------------------------------------------------- Mean-K path */
+
+/* Mean-K page softmax over device-resident per-page K sums. Replaces
+ * PageSoftmaxCuda::score (kvmem/src/cuda/page_softmax.cu:202-280):
+ *   mean[l,p]  = fp16(sum[l,p] * (1/count[p]))           (raw_kv_store.cpp:606-614, recall_fp16)
+ *   logit      = scale * <fp16(q_lrh), mean[l,p,h/G]>    over pages with score_mask[p]
+ *   Mean:  out[p] += prob / (active_layers * Hq)          (page_softmax.cu:88-96)
+ *   Max:   out[p] += (max_{h in group} prob) / mass / (active_layers * Hkv)  (:100-133)
+ * sums: device f32 [layers][pages][kv_heads*head_dim]; counts: device u32 [pages];
+ * q: device f32 [layers][rows][q_heads*head_dim]; layer_rows: host u32 [layers]
+ * (0 = absent layer); score_mask: host u8 [pages]; out: device f32 [pages]
+ * (overwritten; disabled pages get 0). A non-finite or FP16-overflowing
+ * operand returns KVM_ERR_NONFINITE (this call synchronises `stream` to read
+ * the operand flag, as the reference does at page_softmax.cu:372-375). */
+int kvm_meank_score(kvm_ctx* ctx, const float* sums, const uint32_t* counts, const float* q,
+                    const uint32_t* layer_rows, uint32_t layers, uint32_t rows, uint32_t q_heads,
+                    uint32_t kv_heads, uint32_t head_dim, uint32_t pages, const uint8_t* score_mask,
+                    int aggregation, float scale, float* out, void* stream);
+
+/* ------------------------------------------------------------ fused step */
+
+/* One decode-step recall: score -> per-row top-k -> residency plan -> stage-in,
+ * pipelined over layer chunks so the stage-in of chunk i (side stream, PCIe)
+ * overlaps the scoring of chunk i+1 (HBM). Selection rows are (layer, group)
+ * pairs; the keep list applies to every row.
+ *   mass_mean: device f32 [layers*groups][pages]
+ *   sel_ids: device u32 [layers*groups][budget], sel_n: device u32 [layers*groups]
+ *   pool: residency table with rows = layers*groups (NULL: select only)
+ *   layout: stage-in geometry for the pool (NULL: plan without copying)
+ * Returns after enqueueing; completion is ordered on `stream`. */
+typedef struct kvm_step_desc {
+    const kvm_score_desc* score;
+    const kvm_query* q;
+    const kvm_kcache* k;
+    const uint32_t* keep;
+    uint32_t nkeep;
+    uint32_t budget;
+    uint32_t chunks;     /* layer chunks (0 = 4) */
+    uint32_t stage_ctas; /* CTAs of each gather launch (0 = 32) */
+    int force_reload;    /* stage every selected page (cold worst case) */
+    int reserved;
+} kvm_step_desc;
+int kvm_recall_step(kvm_ctx* ctx, const kvm_step_desc* step, kvm_pool* pool, const kvm_stage_layout* layout,
+                    float* mass_mean, uint32_t* sel_ids, uint32_t* sel_n, void* stream);
+
+/* Bytes of one D-element row of `type` (0 for an unknown type). */
+uint64_t kvm_row_bytes(int type, uint32_t dim);
+
+/* Kernel launches this context has issued (for launch accounting). */
+uint64_t kvm_ctx_launches(const kvm_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

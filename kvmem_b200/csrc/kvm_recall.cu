@@ -1,0 +1,672 @@
+// C ABI of the B200 history-recall path (declarations: include/kvm_recall.h).
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "lse_launch.cuh"
+#include "meank.cuh"
+#include "page_norm.cuh"
+#include "select.cuh"
+#include "stagein.cuh"
+
+using namespace kvmb;
+
+struct kvm_pool {
+    kvm_ctx* ctx = nullptr;
+    PoolView view{};
+    void* mem = nullptr;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int previous = -1;
+    bool ok = false;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&previous) != cudaSuccess) return;
+        ok = cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (previous >= 0) cudaSetDevice(previous);
+    }
+};
+
+#define KVM_CUDA(call)               \
+    do {                             \
+        if ((call) != cudaSuccess) { \
+            cudaGetLastError();      \
+            return KVM_ERR_CUDA;     \
+        }                            \
+    } while (0)
+
+#define KVM_TRY(call)                  \
+    do {                               \
+        const int rc_ = (call);        \
+        if (rc_ != KVM_OK) return rc_; \
+    } while (0)
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+int ensure_ws(kvm_ctx* c, size_t bytes) {
+    if (bytes <= c->ws_bytes) return KVM_OK;
+    if (c->ws_borrowed) return KVM_ERR_LENGTH;
+    if (c->ws) {
+        cudaDeviceSynchronize();
+        cudaFree(c->ws);
+        c->ws = nullptr;
+        c->ws_bytes = 0;
+    }
+    KVM_CUDA(cudaMalloc(&c->ws, bytes));
+    c->ws_bytes = bytes;
+    return KVM_OK;
+}
+
+int ensure_small(kvm_ctx* c, size_t bytes) {
+    if (bytes <= c->small_bytes) return KVM_OK;
+    if (c->small) {
+        cudaDeviceSynchronize();
+        cudaFree(c->small);
+        c->small = nullptr;
+        c->small_bytes = 0;
+        c->keep_valid = false;
+    }
+    const size_t want = std::max<size_t>(bytes, 1 << 16);
+    KVM_CUDA(cudaMalloc(&c->small, want));
+    c->small_bytes = want;
+    return KVM_OK;
+}
+
+// The keep list lives at the start of the small scratch (first 4 KiB + list);
+// it is re-uploaded only when it changes, by a synchronous copy, so the host
+// array may be reused as soon as the call returns.
+size_t keep_area(const kvm_ctx* c) { return align256(4096 + c->keep_cached.size() * 4); }
+
+int upload_keep(kvm_ctx* c, const uint32_t* keep, uint32_t nkeep) {
+    if (c->keep_valid && c->keep_cached.size() == nkeep &&
+        (nkeep == 0 || std::memcmp(c->keep_cached.data(), keep, size_t(nkeep) * 4) == 0))
+        return KVM_OK;
+    KVM_TRY(ensure_small(c, align256(4096 + size_t(nkeep) * 4)));
+    if (nkeep) {
+        cudaDeviceSynchronize();  // no launch may still read the previous list
+        KVM_CUDA(cudaMemcpy(c->small, keep, size_t(nkeep) * 4, cudaMemcpyHostToDevice));
+    }
+    c->keep_cached.assign(keep, keep + nkeep);
+    c->keep_valid = true;
+    return KVM_OK;
+}
+
+struct LseConfig {
+    uint32_t lpr = 0, tpc = 0, chunk_bytes = 0, chunks = 0, row_bytes = 0, stage_stride = 0;
+    size_t smem = 0;
+};
+
+bool supported_type(int t) { return t >= KVM_F32 && t <= KVM_Q5_0; }
+
+int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, LseConfig* cfg) {
+    if (!d || !q || !k || !q->data || !k->data) return KVM_ERR_INVALID_ARGUMENT;
+    if (!d->layers || !d->q_heads || !d->kv_heads || !d->head_dim || !d->page_tokens || !q->rows ||
+        d->q_heads % d->kv_heads)
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (d->groups != 1 && d->groups != d->kv_heads) return KVM_ERR_INVALID_ARGUMENT;
+    if (q->type != KVM_F32 && q->type != KVM_F16 && q->type != KVM_BF16) return KVM_ERR_UNSUPPORTED;
+    if (!supported_type(k->type)) return KVM_ERR_UNSUPPORTED;
+    if (d->mask && d->mask_type != KVM_F32 && d->mask_type != KVM_F16) return KVM_ERR_UNSUPPORTED;
+    const uint32_t D = d->head_dim;
+    if (D != 64 && D != 128 && D != 256) return KVM_ERR_UNSUPPORTED;
+    const uint32_t lpr = D / 8;
+    const uint32_t ng = kLseConsumerWarps * 32 / lpr;
+    if (ng % d->kv_heads) return KVM_ERR_UNSUPPORTED;
+    const uint64_t rb = row_bytes_of(k->type, D);
+    if (k->head_stride != rb || k->token_stride != rb * d->kv_heads) return KVM_ERR_UNSUPPORTED;
+    const uint64_t pages = (d->tokens + d->page_tokens - 1) / d->page_tokens;
+    if (!pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (k->capacity_tokens < pages * d->page_tokens) return KVM_ERR_UNSUPPORTED;
+    const uint64_t page_bytes = uint64_t(d->page_tokens) * k->token_stride;
+    if ((reinterpret_cast<uintptr_t>(k->data) & 15) || (k->layer_stride & 15) || (page_bytes & 15))
+        return KVM_ERR_UNSUPPORTED;
+    if (d->layers > 1 && k->layer_stride < pages * page_bytes) return KVM_ERR_INVALID_ARGUMENT;
+    if (pages > 0x7fffffffull || uint64_t(d->layers) * pages > 0x7fffffffull) return KVM_ERR_LENGTH;
+    if (q->rows * uint64_t(d->q_heads / d->kv_heads) > 0x7fffffffull) return KVM_ERR_LENGTH;
+    // Tokens per ring chunk: the largest power of two dividing page_tokens whose
+    // chunk is a multiple of 16 bytes and stays within 16 KiB (32 KiB when a
+    // single token row set is that large).
+    uint32_t tpc = 0;
+    for (uint32_t t = 1; t <= d->page_tokens; t <<= 1) {
+        if (d->page_tokens % t) break;
+        const uint64_t cb = uint64_t(t) * k->token_stride;
+        if (cb > 32768) break;
+        if (cb % 16 == 0 && (tpc == 0 || cb <= 16384)) tpc = t;
+    }
+    if (!tpc) return KVM_ERR_UNSUPPORTED;
+    cfg->lpr = lpr;
+    cfg->tpc = tpc;
+    cfg->chunk_bytes = uint32_t(uint64_t(tpc) * k->token_stride);
+    cfg->chunks = d->page_tokens / tpc;
+    cfg->row_bytes = uint32_t(rb);
+    cfg->stage_stride = uint32_t((cfg->chunk_bytes + 16 + 127) / 128 * 128);
+    cfg->smem = size_t(kLseStages) * cfg->stage_stride + 2 * kLseStages * sizeof(uint64_t) +
+                2 * 2 * size_t(ng) * 8 * sizeof(float) + 16;
+    return KVM_OK;
+}
+
+size_t lse_bytes(const kvm_score_desc* d, uint32_t layers, uint32_t rows) {
+    const uint64_t pages = (d->tokens + d->page_tokens - 1) / d->page_tokens;
+    return align256(size_t(layers) * rows * d->q_heads * pages * sizeof(float));
+}
+
+int launch_lse(kvm_ctx* c, int kt, const LseParams& p, int lpr, int vp, size_t smem, cudaStream_t s) {
+    switch (kt) {
+        case KVM_F32: return launch_lse_kt<KVM_F32>(c, p, lpr, vp, smem, s);
+        case KVM_F16: return launch_lse_kt<KVM_F16>(c, p, lpr, vp, smem, s);
+        case KVM_BF16: return launch_lse_kt<KVM_BF16>(c, p, lpr, vp, smem, s);
+        case KVM_Q8_0: return launch_lse_kt<KVM_Q8_0>(c, p, lpr, vp, smem, s);
+        case KVM_Q4_0: return launch_lse_kt<KVM_Q4_0>(c, p, lpr, vp, smem, s);
+        default: return launch_lse_kt<KVM_Q5_0>(c, p, lpr, vp, smem, s);
+    }
+}
+
+// Scores layers [l0, l0+nl) into mass rows / means whose layer index starts at
+// l0 (absolute), using `lse` ([nl][rows][Hq][pages]) as scratch.
+int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, const LseConfig& cfg,
+                 uint32_t l0, uint32_t nl, float* lse, float* mass_rows, float* mass_mean, cudaStream_t s) {
+    const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
+    const uint32_t G = d->q_heads / d->kv_heads;
+    const uint32_t nvt = q->rows * G;
+    int vp = 1;
+    while (vp < int(nvt) && vp < 8) vp <<= 1;
+    LseParams p{};
+    p.k = static_cast<const uint8_t*>(k->data) + uint64_t(l0) * k->layer_stride;
+    p.k_layer = k->layer_stride;
+    p.page_bytes = uint64_t(d->page_tokens) * k->token_stride;
+    p.chunk_bytes = cfg.chunk_bytes;
+    p.chunks = cfg.chunks;
+    p.tpc = cfg.tpc;
+    p.kv_heads = d->kv_heads;
+    p.row_bytes = cfg.row_bytes;
+    p.pages = pages;
+    p.layers = nl;
+    p.page_tokens = d->page_tokens;
+    p.tokens = d->tokens;
+    p.q = static_cast<const uint8_t*>(q->data) + uint64_t(l0) * q->layer_stride;
+    p.q_type = q->type;
+    p.rows = q->rows;
+    p.q_layer = q->layer_stride;
+    p.q_row = q->row_stride;
+    p.q_head = q->head_stride;
+    p.group = G;
+    p.q_heads = d->q_heads;
+    p.scale = d->scale > 0.f ? d->scale : 1.f / std::sqrt(float(d->head_dim));
+    p.softcap = d->softcap;
+    p.mask = static_cast<const uint8_t*>(d->mask);
+    p.mask_type = d->mask_type;
+    p.mask_row = d->mask_row_stride;
+    p.lse = lse;
+    p.status = c->status;
+    p.stage_stride = cfg.stage_stride;
+    for (uint32_t v0 = 0; v0 < nvt; v0 += vp) {
+        p.v0 = v0;
+        p.nv = std::min<uint32_t>(vp, nvt - v0);
+        KVM_TRY(launch_lse(c, k->type, p, int(cfg.lpr), vp, cfg.smem, s));
+    }
+    const uint32_t heads_per = d->groups == 1 ? d->q_heads : G;
+    const size_t nsmem = size_t(q->rows) * heads_per * sizeof(float2);
+    if (nsmem > 200 * 1024) return KVM_ERR_LENGTH;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(page_mass_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    page_mass_normalize_kernel<<<nl * d->groups, 256, nsmem, s>>>(lse, q->rows, d->q_heads, G, d->groups, pages,
+                                                                 mass_rows, mass_mean, l0);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
+                const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores, uint32_t* out_ids,
+                uint32_t* out_n, uint32_t out_stride, cudaStream_t s) {
+    if (!scores || !out_ids || !out_n || !nrows || !pages || !budget) return KVM_ERR_INVALID_ARGUMENT;
+    if (nkeep && !keep) return KVM_ERR_INVALID_ARGUMENT;
+    if (pages > 196608) return KVM_ERR_LENGTH;
+    if (score_stride < pages || out_stride < std::min(budget, pages)) return KVM_ERR_INVALID_ARGUMENT;
+    std::vector<uint8_t> seen(pages, 0);
+    uint32_t distinct = 0;
+    for (uint32_t i = 0; i < nkeep; ++i) {
+        if (keep[i] >= pages) return KVM_ERR_INVALID_ARGUMENT;
+        distinct += !seen[keep[i]];
+        seen[keep[i]] = 1;
+    }
+    if (distinct > budget) return KVM_ERR_BUDGET_EXCEEDED;
+    KVM_TRY(upload_keep(c, keep, nkeep));
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    select_topk_kernel<<<nrows, kSelectThreads, pages, s>>>(scores, pages, score_stride,
+                                                             static_cast<const uint32_t*>(c->small), nkeep, budget,
+                                                             signed_scores, out_ids, out_n, out_stride, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int plan_rows(kvm_ctx* c, kvm_pool* pool, uint32_t row0, uint32_t nrows, const uint32_t* sel_ids,
+              const uint32_t* sel_n, uint32_t sel_stride, int force, uint32_t* n_restore, uint32_t* n_evict,
+              cudaStream_t s) {
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(plan_residency_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    plan_residency_kernel<<<nrows, kPlanThreads, pool->view.pages, s>>>(pool->view, row0, sel_ids, sel_n, sel_stride,
+                                                                         force, n_restore, n_evict, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int gather_layout(const kvm_stage_layout* L, GatherLayout* g) {
+    if (!L || L->planes < 1 || L->planes > 2) return KVM_ERR_INVALID_ARGUMENT;
+    g->planes = L->planes;
+    for (uint32_t j = 0; j < 2; ++j) {
+        g->host_base[j] = static_cast<const uint8_t*>(L->host_base[j]);
+        g->host_row_stride[j] = L->host_row_stride[j];
+        g->host_page_stride[j] = L->host_page_stride[j];
+        g->dev_base[j] = static_cast<uint8_t*>(L->dev_base[j]);
+        g->dev_row_stride[j] = L->dev_row_stride[j];
+        g->dev_slot_stride[j] = L->dev_slot_stride[j];
+        g->bytes[j] = L->bytes[j];
+        if (j < L->planes) {
+            if (!L->host_base[j] || !L->dev_base[j] || !L->bytes[j]) return KVM_ERR_INVALID_ARGUMENT;
+            if (L->host_page_stride[j] < L->bytes[j] || L->dev_slot_stride[j] < L->bytes[j])
+                return KVM_ERR_INVALID_ARGUMENT;
+        }
+    }
+    return KVM_OK;
+}
+
+int gather_rows(kvm_ctx* c, kvm_pool* pool, uint32_t row0, uint32_t nrows, const GatherLayout& g, uint32_t ctas,
+                cudaStream_t s) {
+    const uint32_t grid = ctas ? ctas : 32;
+    stagein_gather_kernel<<<grid, kGatherThreads, 0, s>>>(pool->view, row0, nrows, g);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t kvm_row_bytes(int type, uint32_t dim) { return supported_type(type) ? row_bytes_of(type, dim) : 0; }
+
+int kvm_ctx_create(int device, kvm_ctx** out) {
+    if (!out) return KVM_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    int count = 0;
+    KVM_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(device);
+    if (!guard.ok) return KVM_ERR_CUDA;
+    auto* c = new (std::nothrow) kvm_ctx;
+    if (!c) return KVM_ERR_CUDA;
+    c->device = device;
+    cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->side_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&c->status, sizeof(DeviceStatus)) != cudaSuccess ||
+        cudaMallocHost(&c->status_host, sizeof(DeviceStatus)) != cudaSuccess ||
+        cudaMemset(c->status, 0, sizeof(DeviceStatus)) != cudaSuccess) {
+        cudaGetLastError();
+        kvm_ctx_destroy(c);
+        return KVM_ERR_CUDA;
+    }
+    *out = c;
+    return KVM_OK;
+}
+
+int kvm_ctx_destroy(kvm_ctx* c) {
+    if (!c) return KVM_OK;
+    DeviceGuard guard(c->device);
+    cudaDeviceSynchronize();
+    for (auto e : c->events) cudaEventDestroy(e);
+    if (c->side_done) cudaEventDestroy(c->side_done);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->status) cudaFree(c->status);
+    if (c->status_host) cudaFreeHost(c->status_host);
+    if (c->ws && !c->ws_borrowed) cudaFree(c->ws);
+    if (c->small) cudaFree(c->small);
+    delete c;
+    return KVM_OK;
+}
+
+int kvm_ctx_device(const kvm_ctx* c) { return c ? c->device : -1; }
+uint64_t kvm_ctx_launches(const kvm_ctx* c) { return c ? c->launches : 0; }
+
+int kvm_ctx_status(kvm_ctx* c, void* stream) {
+    if (!c) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_CUDA(cudaMemcpyAsync(c->status_host, c->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, s));
+    KVM_CUDA(cudaStreamSynchronize(s));
+    const int code = c->status_host->code;
+    if (code) {
+        KVM_CUDA(cudaMemsetAsync(c->status, 0, sizeof(DeviceStatus), s));
+        KVM_CUDA(cudaStreamSynchronize(s));
+    }
+    return code;
+}
+
+size_t kvm_score_workspace_bytes(const kvm_score_desc* d, uint32_t rows) {
+    if (!d || !d->page_tokens) return 0;
+    return lse_bytes(d, d->layers, rows);
+}
+
+int kvm_ctx_bind_workspace(kvm_ctx* c, void* ws, size_t bytes) {
+    if (!c || !ws || (reinterpret_cast<uintptr_t>(ws) & 255)) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ws) != cudaSuccess) {
+        cudaGetLastError();
+        return KVM_ERR_INVALID_ARGUMENT;
+    }
+    if (a.type != cudaMemoryTypeDevice || a.device != c->device) return KVM_ERR_INVALID_ARGUMENT;
+    if (c->ws && !c->ws_borrowed) {
+        cudaDeviceSynchronize();
+        cudaFree(c->ws);
+    }
+    c->ws = ws;
+    c->ws_bytes = bytes;
+    c->ws_borrowed = true;
+    return KVM_OK;
+}
+
+size_t kvm_ctx_device_bytes(const kvm_ctx* c) {
+    return c ? (c->ws_borrowed ? 0 : c->ws_bytes) + c->small_bytes : 0;
+}
+
+int kvm_score_pages(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, float* mass_rows,
+                    float* mass_mean, void* stream) {
+    if (!c) return KVM_ERR_INVALID_ARGUMENT;
+    LseConfig cfg;
+    KVM_TRY(validate_score(d, q, k, &cfg));
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_TRY(ensure_ws(c, lse_bytes(d, d->layers, q->rows)));
+    return score_layers(c, d, q, k, cfg, 0, d->layers, static_cast<float*>(c->ws), mass_rows, mass_mean, s);
+}
+
+int kvm_select_topk(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
+                    const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores, uint32_t* out_ids,
+                    uint32_t* out_n, uint32_t out_stride, void* stream) {
+    if (!c) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    return select_rows(c, scores, nrows, pages, score_stride, keep, nkeep, budget, signed_scores, out_ids, out_n,
+                       out_stride, static_cast<cudaStream_t>(stream));
+}
+
+int kvm_pool_create(kvm_ctx* c, uint32_t rows, uint32_t pages, uint32_t slots, kvm_pool** out) {
+    if (!c || !out || !rows || !pages || !slots || pages > 196608) return KVM_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    DeviceGuard guard(c->device);
+    auto* p = new (std::nothrow) kvm_pool;
+    if (!p) return KVM_ERR_CUDA;
+    p->ctx = c;
+    const size_t a = align256(size_t(rows) * pages * 4), b = align256(size_t(rows) * slots * 4),
+                 n = align256(size_t(rows) * 4);
+    if (cudaMalloc(&p->mem, a + 3 * b + n) != cudaSuccess) {
+        cudaGetLastError();
+        delete p;
+        return KVM_ERR_CUDA;
+    }
+    auto* base = static_cast<uint8_t*>(p->mem);
+    p->view.slot_of = reinterpret_cast<int32_t*>(base);
+    p->view.page_of = reinterpret_cast<int32_t*>(base + a);
+    p->view.restore = reinterpret_cast<uint32_t*>(base + a + b);
+    p->view.restore_slot = reinterpret_cast<uint32_t*>(base + a + 2 * b);
+    p->view.n_restore = reinterpret_cast<uint32_t*>(base + a + 3 * b);
+    p->view.rows = rows;
+    p->view.pages = pages;
+    p->view.slots = slots;
+    int rc = kvm_pool_reset(p, nullptr);
+    if (rc == KVM_OK && cudaDeviceSynchronize() != cudaSuccess) rc = KVM_ERR_CUDA;
+    if (rc != KVM_OK) {
+        kvm_pool_destroy(p);
+        return rc;
+    }
+    *out = p;
+    return KVM_OK;
+}
+
+int kvm_pool_destroy(kvm_pool* p) {
+    if (!p) return KVM_OK;
+    DeviceGuard guard(p->ctx->device);
+    cudaDeviceSynchronize();
+    if (p->mem) cudaFree(p->mem);
+    delete p;
+    return KVM_OK;
+}
+
+int kvm_pool_reset(kvm_pool* p, void* stream) {
+    if (!p) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(p->ctx->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const auto& v = p->view;
+    KVM_CUDA(cudaMemsetAsync(v.slot_of, 0xff, size_t(v.rows) * v.pages * 4, s));
+    KVM_CUDA(cudaMemsetAsync(v.page_of, 0xff, size_t(v.rows) * v.slots * 4, s));
+    KVM_CUDA(cudaMemsetAsync(v.n_restore, 0, size_t(v.rows) * 4, s));
+    return KVM_OK;
+}
+
+int kvm_pool_read(kvm_pool* p, int32_t* slot_of, int32_t* page_of, void* stream) {
+    if (!p) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(p->ctx->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const auto& v = p->view;
+    if (slot_of)
+        KVM_CUDA(cudaMemcpyAsync(slot_of, v.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToHost, s));
+    if (page_of)
+        KVM_CUDA(cudaMemcpyAsync(page_of, v.page_of, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToHost, s));
+    KVM_CUDA(cudaStreamSynchronize(s));
+    return KVM_OK;
+}
+
+int kvm_plan_residency(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, const uint32_t* sel_n, uint32_t sel_stride,
+                       int force_reload, uint32_t* n_restore, uint32_t* n_evict, void* stream) {
+    if (!c || !pool || !sel_ids || !sel_n || pool->ctx != c) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    return plan_rows(c, pool, 0, pool->view.rows, sel_ids, sel_n, sel_stride, force_reload, n_restore, n_evict,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int kvm_stagein_pool(kvm_ctx* c, kvm_pool* pool, const kvm_stage_layout* layout, uint32_t ctas, void* stream) {
+    if (!c || !pool || pool->ctx != c) return KVM_ERR_INVALID_ARGUMENT;
+    GatherLayout g{};
+    KVM_TRY(gather_layout(layout, &g));
+    DeviceGuard guard(c->device);
+    return gather_rows(c, pool, 0, pool->view.rows, g, ctas, static_cast<cudaStream_t>(stream));
+}
+
+int kvm_stagein_copies(kvm_ctx* c, const kvm_copy* ops, uint32_t n, uint32_t ctas, void* stream) {
+    if (!c || (n && !ops)) return KVM_ERR_INVALID_ARGUMENT;
+    if (!n) return KVM_OK;
+    for (uint32_t i = 0; i < n; ++i)
+        if (!ops[i].src || !ops[i].dst || !ops[i].bytes) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const size_t off = keep_area(c);
+    KVM_TRY(ensure_small(c, off + size_t(n) * sizeof(CopyOp)));
+    auto* dev_ops = reinterpret_cast<CopyOp*>(static_cast<uint8_t*>(c->small) + off);
+    static_assert(sizeof(CopyOp) == sizeof(kvm_copy), "copy op layout");
+    // The previous list may still be read by a launch in flight; the upload is
+    // synchronous so the caller's host list may be reused on return.
+    KVM_CUDA(cudaDeviceSynchronize());
+    KVM_CUDA(cudaMemcpy(dev_ops, ops, size_t(n) * sizeof(CopyOp), cudaMemcpyHostToDevice));
+    const uint32_t grid = std::min<uint32_t>(n, ctas ? ctas : 64);
+    copy_ops_kernel<<<grid, kGatherThreads, 0, s>>>(dev_ops, n);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_stagein_wait(kvm_ctx* c, void* stream, uint64_t timeout_us) {
+    if (!c) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) {
+            cudaGetLastError();
+            return KVM_ERR_CUDA;
+        }
+        const auto us =
+            std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (uint64_t(us) >= timeout_us) return KVM_ERR_TIMEOUT;
+    }
+    return kvm_ctx_status(c, stream);
+}
+
+int kvm_meank_score(kvm_ctx* c, const float* sums, const uint32_t* counts, const float* q, const uint32_t* layer_rows,
+                    uint32_t layers, uint32_t rows, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                    uint32_t pages, const uint8_t* score_mask, int aggregation, float scale, float* out,
+                    void* stream) {
+    if (!c || !sums || !counts || !q || !layer_rows || !score_mask || !out) return KVM_ERR_INVALID_ARGUMENT;
+    if (aggregation != 0 && aggregation != 1) return KVM_ERR_INVALID_ARGUMENT;
+    if (!layers || !rows || !q_heads || !kv_heads || !head_dim || q_heads % kv_heads || !pages)
+        return KVM_ERR_INVALID_ARGUMENT;
+    std::vector<uint32_t> enabled, active, pairs, pair_slot;
+    for (uint32_t p = 0; p < pages; ++p)
+        if (score_mask[p]) enabled.push_back(p);
+    for (uint32_t l = 0; l < layers; ++l) {
+        if (layer_rows[l] > rows) return KVM_ERR_INVALID_ARGUMENT;
+        if (!layer_rows[l]) continue;
+        for (uint32_t r = 0; r < layer_rows[l]; ++r) {
+            pairs.push_back(l);
+            pairs.push_back(r);
+            pair_slot.push_back(uint32_t(active.size()));
+        }
+        active.push_back(l);
+    }
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_CUDA(cudaMemsetAsync(out, 0, size_t(pages) * 4, s));
+    if (enabled.empty() || active.empty()) return KVM_OK;
+    const uint32_t n = uint32_t(enabled.size()), nact = uint32_t(active.size());
+    const uint32_t npairs = uint32_t(pair_slot.size());
+    const uint64_t kw = uint64_t(kv_heads) * head_dim, qw = uint64_t(q_heads) * head_dim;
+    const uint64_t dists = uint64_t(npairs) * q_heads;
+    if (dists > 65535) return KVM_ERR_LENGTH;  // grid.y of the logits launch
+    const uint32_t group = q_heads / kv_heads;
+    // Workspace: means_h | qh | logits | norms | group_inv | bad
+    const size_t b_means = align256(size_t(nact) * n * kw * 2), b_q = align256(size_t(npairs) * qw * 2),
+                 b_logits = align256(size_t(dists) * n * 4), b_norms = align256(size_t(dists) * 8),
+                 b_group = align256(size_t(dists / group) * 4), b_bad = 256;
+    KVM_TRY(ensure_ws(c, b_means + b_q + b_logits + b_norms + b_group + b_bad));
+    auto* w = static_cast<uint8_t*>(c->ws);
+    auto* means_h = reinterpret_cast<__half*>(w);
+    auto* qh = reinterpret_cast<__half*>(w + b_means);
+    auto* logits = reinterpret_cast<float*>(w + b_means + b_q);
+    auto* norms = reinterpret_cast<float2*>(w + b_means + b_q + b_logits);
+    auto* ginv = reinterpret_cast<float*>(w + b_means + b_q + b_logits + b_norms);
+    auto* bad = reinterpret_cast<uint32_t*>(w + b_means + b_q + b_logits + b_norms + b_group);
+    // Host tables: enabled | active | pairs | pair_slot
+    std::vector<uint32_t> host;
+    host.insert(host.end(), enabled.begin(), enabled.end());
+    host.insert(host.end(), active.begin(), active.end());
+    host.insert(host.end(), pairs.begin(), pairs.end());
+    host.insert(host.end(), pair_slot.begin(), pair_slot.end());
+    const size_t tbl = host.size() * 4;
+    const size_t off = keep_area(c);
+    KVM_TRY(ensure_small(c, off + tbl));
+    auto* t = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(c->small) + off);
+    KVM_CUDA(cudaDeviceSynchronize());
+    KVM_CUDA(cudaMemcpy(t, host.data(), tbl, cudaMemcpyHostToDevice));
+    const uint32_t* d_enabled = t;
+    const uint32_t* d_active = t + enabled.size();
+    const uint32_t* d_pairs = d_active + active.size();
+    const uint32_t* d_slot = d_pairs + pairs.size();
+    KVM_CUDA(cudaMemsetAsync(bad, 0, 4, s));
+    const uint32_t pack_grid = uint32_t(std::max(1, c->num_sms * 4));
+    meank_pack_means_kernel<<<pack_grid, 256, 0, s>>>(sums, counts, d_enabled, d_active, nact, pages, n, uint32_t(kw),
+                                                      means_h, bad);
+    meank_pack_query_kernel<<<pack_grid, 256, 0, s>>>(q, d_pairs, npairs, rows, uint32_t(qw), qh, bad);
+    c->launches += 2;
+    KVM_CUDA(cudaGetLastError());
+    KVM_CUDA(cudaMemcpyAsync(c->status_host, bad, 4, cudaMemcpyDeviceToHost, s));
+    KVM_CUDA(cudaStreamSynchronize(s));
+    if (c->status_host->code) return KVM_ERR_NONFINITE;
+    const float sc = scale > 0.f ? scale : 1.f / std::sqrt(float(head_dim));
+    meank_logits_kernel<<<dim3((n + 7) / 8, uint32_t(dists)), 256, 0, s>>>(qh, means_h, d_slot, q_heads, kv_heads,
+                                                                           head_dim, n, sc, logits);
+    meank_normalize_kernel<<<uint32_t((dists + 7) / 8), 256, 0, s>>>(logits, n, uint32_t(dists), norms);
+    c->launches += 2;
+    if (aggregation == 1) {
+        const uint32_t ngroups = uint32_t(dists / group);
+        meank_group_mass_kernel<<<(ngroups + 7) / 8, 256, 0, s>>>(logits, norms, n, group, ngroups, ginv);
+        ++c->launches;
+    }
+    const float weight = aggregation == 0 ? 1.f / (float(nact) * q_heads) : 1.f / (float(nact) * kv_heads);
+    meank_accumulate_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, norms, ginv, d_enabled, n, uint32_t(dists), group,
+                                                            aggregation, weight, out);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_recall_step(kvm_ctx* c, const kvm_step_desc* st, kvm_pool* pool, const kvm_stage_layout* layout,
+                    float* mass_mean, uint32_t* sel_ids, uint32_t* sel_n, void* stream) {
+    if (!c || !st || !st->score || !mass_mean || !sel_ids || !sel_n || !st->budget) return KVM_ERR_INVALID_ARGUMENT;
+    const kvm_score_desc* d = st->score;
+    LseConfig cfg;
+    KVM_TRY(validate_score(d, st->q, st->k, &cfg));
+    const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
+    const uint32_t srows = d->layers * d->groups;
+    GatherLayout g{};
+    if (pool) {
+        if (pool->ctx != c || pool->view.rows != srows || pool->view.pages != pages) return KVM_ERR_INVALID_ARGUMENT;
+        if (pool->view.slots < std::min(st->budget, pages)) return KVM_ERR_BUDGET_EXCEEDED;
+        if (layout) KVM_TRY(gather_layout(layout, &g));
+    }
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const uint32_t chunks = std::max<uint32_t>(1, std::min(st->chunks ? st->chunks : 4u, d->layers));
+    const uint32_t per = (d->layers + chunks - 1) / chunks;
+    KVM_TRY(ensure_ws(c, lse_bytes(d, per, st->q->rows)));
+    while (c->events.size() < chunks) {
+        cudaEvent_t e;
+        KVM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        c->events.push_back(e);
+    }
+    const uint32_t out_stride = st->budget;
+    bool staged = false;
+    for (uint32_t ci = 0; ci < chunks; ++ci) {
+        const uint32_t l0 = ci * per;
+        if (l0 >= d->layers) break;
+        const uint32_t nl = std::min(per, d->layers - l0);
+        KVM_TRY(score_layers(c, d, st->q, st->k, cfg, l0, nl, static_cast<float*>(c->ws), nullptr, mass_mean, s));
+        const uint32_t r0 = l0 * d->groups, nr = nl * d->groups;
+        KVM_TRY(select_rows(c, mass_mean + size_t(r0) * pages, nr, pages, pages, st->keep, st->nkeep, st->budget, 0,
+                            sel_ids + size_t(r0) * out_stride, sel_n + r0, out_stride, s));
+        if (!pool) continue;
+        KVM_TRY(plan_rows(c, pool, r0, nr, sel_ids + size_t(r0) * out_stride, sel_n + r0, out_stride,
+                          st->force_reload, nullptr, nullptr, s));
+        if (!layout) continue;
+        KVM_CUDA(cudaEventRecord(c->events[ci], s));
+        KVM_CUDA(cudaStreamWaitEvent(c->side, c->events[ci], 0));
+        KVM_TRY(gather_rows(c, pool, r0, nr, g, st->stage_ctas, c->side));
+        staged = true;
+    }
+    if (staged) {
+        KVM_CUDA(cudaEventRecord(c->side_done, c->side));
+        KVM_CUDA(cudaStreamWaitEvent(s, c->side_done, 0));
+    }
+    return KVM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+// Context definition shared by the library's translation units, and the
+// templated launcher of the page log-sum-exp kernel (instantiated once per key
+// type in lse_<type>.cu so the variants compile in parallel).
+#pragma once
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "page_mass.cuh"
+
+struct kvm_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t side = nullptr;  // stage-in stream of kvm_recall_step
+    std::vector<cudaEvent_t> events;
+    cudaEvent_t side_done = nullptr;
+    kvmb::DeviceStatus* status = nullptr;       // device
+    kvmb::DeviceStatus* status_host = nullptr;  // pinned
+    void* ws = nullptr;                         // scoring workspace
+    size_t ws_bytes = 0;
+    bool ws_borrowed = false;
+    void* small = nullptr;  // device copy of short host-built tables
+    size_t small_bytes = 0;
+    std::vector<uint32_t> keep_cached;
+    bool keep_valid = false;
+    uint64_t launches = 0;
+};
+
+namespace kvmb {
+
+template <int KT, int LPR, int VP, bool MASK>
+int launch_lse_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
+    auto fn = page_lse_kernel<KT, LPR, VP, MASK>;
+    static std::once_flag once;  // one attribute set per instantiation
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLseThreads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return KVM_ERR_CUDA;
+    }
+    if (per_sm < 1) return KVM_ERR_UNSUPPORTED;
+    const uint32_t units = p.layers * p.pages;
+    const uint32_t grid = std::min<uint32_t>(units, uint32_t(c->num_sms * per_sm));
+    fn<<<grid, kLseThreads, smem, s>>>(p);
+    ++c->launches;
+    if (cudaGetLastError() != cudaSuccess) return KVM_ERR_CUDA;
+    return KVM_OK;
+}
+
+template <int KT, int LPR, int VP>
+int launch_lse_m(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
+    return p.mask ? launch_lse_t<KT, LPR, VP, true>(c, p, smem, s) : launch_lse_t<KT, LPR, VP, false>(c, p, smem, s);
+}
+
+template <int KT, int LPR>
+int launch_lse_v(kvm_ctx* c, const LseParams& p, int vp, size_t smem, cudaStream_t s) {
+    switch (vp) {
+        case 1: return launch_lse_m<KT, LPR, 1>(c, p, smem, s);
+        case 2: return launch_lse_m<KT, LPR, 2>(c, p, smem, s);
+        case 4: return launch_lse_m<KT, LPR, 4>(c, p, smem, s);
+        default: return launch_lse_m<KT, LPR, 8>(c, p, smem, s);
+    }
+}
+
+template <int KT>
+int launch_lse_kt(kvm_ctx* c, const LseParams& p, int lpr, int vp, size_t smem, cudaStream_t s) {
+    switch (lpr) {
+        case 8: return launch_lse_v<KT, 8>(c, p, vp, smem, s);
+        case 16: return launch_lse_v<KT, 16>(c, p, vp, smem, s);
+        default: return launch_lse_v<KT, 32>(c, p, vp, smem, s);
+    }
+}
+
+// Instantiated once each in lse_<type>.cu.
+extern template int launch_lse_kt<KVM_F32>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_kt<KVM_F16>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_kt<KVM_BF16>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_kt<KVM_Q8_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_kt<KVM_Q4_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_kt<KVM_Q5_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+
+}  // namespace kvmb

@@ -1,0 +1,6 @@
+// Page log-sum-exp launchers for q5_0 keys (one translation unit per key type).
+#include "lse_launch.cuh"
+
+namespace kvmb {
+template int launch_lse_kt<KVM_Q5_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+}  // namespace kvmb
