@@ -1,0 +1,366 @@
+"""Host-side API over the C ABI (``include/kvm_recall.h``).
+
+Two layers:
+
+* ``RecallContext`` / ``ResidencyPool`` — direct wrappers of the C entry
+  points, taking device tensors (torch is used only to own device memory and
+  streams) and returning device tensors;
+* ``AttentionCuda``, ``PageSoftmaxCuda`` and ``pick_scored_blocks`` — mirrors
+  of the reference's interfaces for this path, with the same argument meaning
+  and error behaviour, so callers and tests read like the reference's own:
+  ``llama_kvmem_attention_cuda::score`` (src/adapter/llama-kvmem-attention-cuda.h:9-18),
+  ``kvmem::PageSoftmaxCuda`` (kvmem/include/kvmem/page_softmax_cuda.hpp:10-31) and
+  ``KvMemStore::pick_scored_blocks`` (kvmem/src/host/kvmem_store.cpp:418-451).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _abi as A
+
+_TORCH_QTYPE = {torch.float32: A.F32, torch.float16: A.F16, torch.bfloat16: A.BF16}
+
+
+def _stream_ptr(stream) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream
+
+
+def row_bytes(ktype: int, dim: int) -> int:
+    return int(A.load().kvm_row_bytes(ktype, dim))
+
+
+class RecallContext:
+    """One kvm_ctx: device, status word, scoring workspace, stage-in stream."""
+
+    def __init__(self, device: int = 0):
+        self.lib = A.load()
+        self.device = device
+        h = C.c_void_p()
+        A.check(self.lib.kvm_ctx_create(device, C.byref(h)), "kvm_ctx_create")
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.kvm_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- status / workspace ------------------------------------------------
+    def status(self, stream=None) -> int:
+        return int(self.lib.kvm_ctx_status(self.h, _stream_ptr(stream)))
+
+    def check_status(self, where: str = "device", stream=None) -> None:
+        A.check(self.status(stream), where)
+
+    @property
+    def launches(self) -> int:
+        return int(self.lib.kvm_ctx_launches(self.h))
+
+    def bind_workspace(self, tensor: torch.Tensor) -> None:
+        A.check(self.lib.kvm_ctx_bind_workspace(self.h, tensor.data_ptr(), tensor.numel() * tensor.element_size()),
+                "kvm_ctx_bind_workspace")
+
+    def device_bytes(self) -> int:
+        return int(self.lib.kvm_ctx_device_bytes(self.h))
+
+    # -- descriptors -------------------------------------------------------
+    @staticmethod
+    def make_desc(*, layers, q_heads, kv_heads, head_dim, tokens, page_tokens, groups=1, scale=0.0, softcap=0.0,
+                  mask: Optional[torch.Tensor] = None, mask_row_stride: int = 0) -> A.ScoreDesc:
+        d = A.ScoreDesc()
+        d.layers, d.q_heads, d.kv_heads, d.head_dim = layers, q_heads, kv_heads, head_dim
+        d.tokens, d.page_tokens, d.groups = tokens, page_tokens, groups
+        d.scale, d.softcap = scale, softcap
+        if mask is not None:
+            d.mask = mask.data_ptr()
+            d.mask_type = _TORCH_QTYPE[mask.dtype]
+            d.mask_row_stride = mask_row_stride or mask.stride(0) * mask.element_size()
+        return d
+
+    @staticmethod
+    def make_query(q: torch.Tensor, rows: int, *, strides=None, data_ptr: Optional[int] = None) -> A.Query:
+        """q dense [layers][rows][heads][dim] unless strides=(layer, row, head) bytes."""
+        qq = A.Query()
+        qq.data = data_ptr if data_ptr is not None else q.data_ptr()
+        qq.type = _TORCH_QTYPE[q.dtype]
+        qq.rows = rows
+        es = q.element_size()
+        if strides is None:
+            L, R, H, D = q.shape
+            strides = (R * H * D * es, H * D * es, D * es)
+        qq.layer_stride, qq.row_stride, qq.head_stride = strides
+        return qq
+
+    @staticmethod
+    def make_kcache(k: torch.Tensor, ktype: int, *, kv_heads: int, head_dim: int, capacity_tokens: int,
+                    layer_stride: Optional[int] = None, data_ptr: Optional[int] = None) -> A.KCache:
+        """k: device bytes holding [layers][capacity_tokens][kv_heads] rows of ktype."""
+        kc = A.KCache()
+        kc.data = data_ptr if data_ptr is not None else k.data_ptr()
+        kc.type = ktype
+        rb = row_bytes(ktype, head_dim)
+        kc.head_stride = rb
+        kc.token_stride = rb * kv_heads
+        kc.layer_stride = layer_stride if layer_stride is not None else rb * kv_heads * capacity_tokens
+        kc.capacity_tokens = capacity_tokens
+        return kc
+
+    # -- entry points ------------------------------------------------------
+    def score_pages(self, desc: A.ScoreDesc, q: A.Query, k: A.KCache, *, want_rows=True, want_mean=True,
+                    out_rows: Optional[torch.Tensor] = None, out_mean: Optional[torch.Tensor] = None, stream=None):
+        pages = -(-desc.tokens // desc.page_tokens)
+        dev = torch.device("cuda", self.device)
+        if want_rows and out_rows is None:
+            out_rows = torch.empty((desc.layers, desc.groups, q.rows, pages), dtype=torch.float32, device=dev)
+        if want_mean and out_mean is None:
+            out_mean = torch.empty((desc.layers, desc.groups, pages), dtype=torch.float32, device=dev)
+        rc = self.lib.kvm_score_pages(self.h, C.byref(desc), C.byref(q), C.byref(k),
+                                      out_rows.data_ptr() if out_rows is not None else None,
+                                      out_mean.data_ptr() if out_mean is not None else None, _stream_ptr(stream))
+        A.check(rc, "kvm_score_pages")
+        return out_rows, out_mean
+
+    def select_topk(self, scores: torch.Tensor, keep: Sequence[int], budget: int, *, signed: bool = False,
+                    out_ids: Optional[torch.Tensor] = None, out_n: Optional[torch.Tensor] = None, stream=None):
+        """scores [nrows][pages] f32 on the device -> (ids [nrows][min(budget,pages)], n [nrows])."""
+        assert scores.dtype == torch.float32 and scores.dim() == 2
+        nrows, pages = scores.shape
+        width = min(budget, pages)
+        if out_ids is None:
+            out_ids = torch.zeros((nrows, width), dtype=torch.int32, device=scores.device)
+        if out_n is None:
+            out_n = torch.zeros((nrows,), dtype=torch.int32, device=scores.device)
+        kp = (C.c_uint32 * max(1, len(keep)))(*keep)
+        rc = self.lib.kvm_select_topk(self.h, scores.data_ptr(), nrows, pages, scores.stride(0), kp, len(keep),
+                                      budget, int(signed), out_ids.data_ptr(), out_n.data_ptr(), out_ids.stride(0),
+                                      _stream_ptr(stream))
+        A.check(rc, "kvm_select_topk")
+        return out_ids, out_n
+
+    def meank_score(self, sums: torch.Tensor, counts: torch.Tensor, q: torch.Tensor, layer_rows: Sequence[int],
+                    score_mask: Sequence[int], *, q_heads: int, kv_heads: int, head_dim: int, aggregation: int = 0,
+                    scale: float = 0.0, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """sums [L][P][Hkv*D] f32, counts [P] u32 (int32 tensor), q [L][R][Hq*D] f32 -> out [P] f32."""
+        L, P, _ = sums.shape
+        R = q.shape[1]
+        if out is None:
+            out = torch.empty((P,), dtype=torch.float32, device=sums.device)
+        lr = (C.c_uint32 * L)(*layer_rows)
+        sm = (C.c_uint8 * P)(*[1 if x else 0 for x in score_mask])
+        rc = self.lib.kvm_meank_score(self.h, sums.data_ptr(), counts.data_ptr(), q.data_ptr(), lr, L, R, q_heads,
+                                      kv_heads, head_dim, P, sm, aggregation, scale, out.data_ptr(),
+                                      _stream_ptr(stream))
+        A.check(rc, "kvm_meank_score")
+        return out
+
+    def stagein_copies(self, ops: Sequence[tuple], ctas: int = 0, stream=None) -> None:
+        arr = (A.Copy * max(1, len(ops)))()
+        for i, (src, dst, nbytes) in enumerate(ops):
+            arr[i].src, arr[i].dst, arr[i].bytes = src, dst, nbytes
+        A.check(self.lib.kvm_stagein_copies(self.h, arr, len(ops), ctas, _stream_ptr(stream)), "kvm_stagein_copies")
+
+    def wait(self, timeout_s: float = 30.0, stream=None) -> None:
+        A.check(self.lib.kvm_stagein_wait(self.h, _stream_ptr(stream), int(timeout_s * 1e6)), "kvm_stagein_wait")
+
+    def recall_step(self, desc: A.ScoreDesc, q: A.Query, k: A.KCache, keep: Sequence[int], budget: int, *,
+                    mass_mean: torch.Tensor, sel_ids: torch.Tensor, sel_n: torch.Tensor,
+                    pool: Optional["ResidencyPool"] = None, layout: Optional[A.StageLayout] = None,
+                    chunks: int = 0, stage_ctas: int = 0, force_reload: bool = False, stream=None) -> None:
+        st = A.StepDesc()
+        st.score = C.pointer(desc)
+        st.q = C.pointer(q)
+        st.k = C.pointer(k)
+        kp = (C.c_uint32 * max(1, len(keep)))(*keep)
+        st.keep = C.cast(kp, C.POINTER(C.c_uint32))
+        st.nkeep, st.budget, st.chunks, st.stage_ctas = len(keep), budget, chunks, stage_ctas
+        st.force_reload = int(force_reload)
+        rc = self.lib.kvm_recall_step(self.h, C.byref(st), pool.h if pool is not None else None,
+                                      C.byref(layout) if layout is not None else None, mass_mean.data_ptr(),
+                                      sel_ids.data_ptr(), sel_n.data_ptr(), _stream_ptr(stream))
+        A.check(rc, "kvm_recall_step")
+
+
+class ResidencyPool:
+    """Device residency table (kvm_pool) for `rows` selections over `pages` pages and `slots` slots."""
+
+    def __init__(self, ctx: RecallContext, rows: int, pages: int, slots: int):
+        self.ctx, self.rows, self.pages, self.slots = ctx, rows, pages, slots
+        h = C.c_void_p()
+        A.check(ctx.lib.kvm_pool_create(ctx.h, rows, pages, slots, C.byref(h)), "kvm_pool_create")
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.ctx.lib.kvm_pool_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self, stream=None) -> None:
+        A.check(self.ctx.lib.kvm_pool_reset(self.h, _stream_ptr(stream)), "kvm_pool_reset")
+
+    def plan(self, sel_ids: torch.Tensor, sel_n: torch.Tensor, *, force_reload=False, stream=None):
+        n_restore = torch.zeros((self.rows,), dtype=torch.int32, device=sel_ids.device)
+        n_evict = torch.zeros((self.rows,), dtype=torch.int32, device=sel_ids.device)
+        rc = self.ctx.lib.kvm_plan_residency(self.ctx.h, self.h, sel_ids.data_ptr(), sel_n.data_ptr(),
+                                             sel_ids.stride(0), int(force_reload), n_restore.data_ptr(),
+                                             n_evict.data_ptr(), _stream_ptr(stream))
+        A.check(rc, "kvm_plan_residency")
+        return n_restore, n_evict
+
+    def stage_in(self, layout: A.StageLayout, ctas: int = 0, stream=None) -> None:
+        A.check(self.ctx.lib.kvm_stagein_pool(self.ctx.h, self.h, C.byref(layout), ctas, _stream_ptr(stream)),
+                "kvm_stagein_pool")
+
+    def read(self, stream=None):
+        import numpy as np
+        slot_of = np.empty((self.rows, self.pages), np.int32)
+        page_of = np.empty((self.rows, self.slots), np.int32)
+        rc = self.ctx.lib.kvm_pool_read(self.h, slot_of.ctypes.data, page_of.ctypes.data, _stream_ptr(stream))
+        A.check(rc, "kvm_pool_read")
+        return slot_of, page_of
+
+
+def stage_layout(planes: Sequence[dict]) -> A.StageLayout:
+    """planes: up to two dicts with host_base, host_row_stride, host_page_stride,
+    dev_base, dev_row_stride, dev_slot_stride, bytes."""
+    L = A.StageLayout()
+    L.planes = len(planes)
+    for j, p in enumerate(planes):
+        L.host_base[j] = p["host_base"]
+        L.host_row_stride[j] = p["host_row_stride"]
+        L.host_page_stride[j] = p["host_page_stride"]
+        L.dev_base[j] = p["dev_base"]
+        L.dev_row_stride[j] = p["dev_row_stride"]
+        L.dev_slot_stride[j] = p["dev_slot_stride"]
+        L.bytes[j] = p["bytes"]
+    return L
+
+
+# ----------------------------------------------------------------------------
+# Mirrors of the reference interfaces for this path.
+# ----------------------------------------------------------------------------
+
+@dataclass
+class TensorView:
+    """The parts of a ggml tensor the reference scorer reads: `data` (device
+    tensor owning the bytes), element / block `type`, ne[0..2] and byte strides
+    nb[1..2] (ggml order: ne0 = head_dim, ne1 = rows or tokens, ne2 = heads)."""
+    data: torch.Tensor
+    type: int
+    ne: tuple
+    nb: tuple
+
+
+class AttentionCuda:
+    """Mirror of llama_kvmem_attention_cuda (src/adapter/llama-kvmem-attention-cuda.h:9-18).
+
+    score(q, k, mask, scale, softcap, block, rows) returns masses[len(rows)][pages]
+    (mean over all query heads of the page-softmax mass), or None when the
+    inputs are outside what the kernel handles (the reference's `false`,
+    after which the caller builds its fallback graph). CUDA failures raise.
+    """
+
+    def __init__(self, device: int = 0):
+        self.ctx = RecallContext(device)
+
+    def score(self, q: TensorView, k: TensorView, mask: Optional[TensorView], scale: float, softcap: float,
+              block: int, rows: Sequence[int]):
+        D, _, Hq = q.ne[0], q.ne[1], q.ne[2]
+        T, Hkv = k.ne[1], k.ne[2]
+        if q.type not in (A.F32, A.F16, A.BF16) or D > 256 or D % 32:
+            return None
+        pages = -(-T // block)
+        desc = RecallContext.make_desc(layers=1, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=block,
+                                       groups=1, scale=scale, softcap=softcap)
+        kc = A.KCache()
+        kc.data, kc.type = k.data.data_ptr(), k.type
+        kc.layer_stride, kc.token_stride, kc.head_stride = 0, k.nb[1], k.nb[2]
+        kc.capacity_tokens = T
+        out = []
+        for r in rows:
+            qq = A.Query()
+            qq.data = q.data.data_ptr() + r * q.nb[1]
+            qq.type, qq.rows = q.type, 1
+            qq.layer_stride, qq.row_stride, qq.head_stride = 0, q.nb[1], q.nb[2]
+            if mask is not None:
+                desc.mask = mask.data.data_ptr() + r * mask.nb[1]
+                desc.mask_type = mask.type
+                desc.mask_row_stride = mask.nb[1]
+            _, mean = None, None
+            try:
+                _, mean = self.ctx.score_pages(desc, qq, kc, want_rows=False)
+            except A.KvmError as e:
+                if e.code == A.ERR_UNSUPPORTED:
+                    return None
+                raise
+            out.append(mean.view(pages).tolist())
+        self.ctx.check_status("llama_kvmem_attention_cuda::score")
+        return out
+
+
+class PageSoftmaxCuda:
+    """Mirror of kvmem::PageSoftmaxCuda (kvmem/include/kvmem/page_softmax_cuda.hpp:10-31)
+    over device-resident per-page K sums.
+
+    score(sums, counts, q, layer_rows, frame, aggregation) -> list of doubles
+    over frame pages; frame is the dict form of QueryScoreFrame (score_mask
+    selects the softmax domain). Geometry errors raise ValueError
+    (std::invalid_argument), a non-finite / FP16-overflowing operand raises
+    ValueError, CUDA failures raise RuntimeError.
+    """
+
+    def __init__(self, device: int = 0, workspace: Optional[torch.Tensor] = None):
+        self.ctx = RecallContext(device)
+        if workspace is not None:
+            if workspace.data_ptr() % 256:
+                raise ValueError("page softmax borrowed workspace is missing, unaligned or too small")
+            self.ctx.bind_workspace(workspace)
+
+    def score(self, sums: torch.Tensor, counts: torch.Tensor, q: torch.Tensor, layer_rows: Sequence[int],
+              frame: dict, aggregation: int = 0, *, q_heads: int, kv_heads: int, head_dim: int,
+              scale: float = 0.0) -> list:
+        try:
+            out = self.ctx.meank_score(sums, counts, q, layer_rows, frame["score_mask"], q_heads=q_heads,
+                                       kv_heads=kv_heads, head_dim=head_dim, aggregation=aggregation, scale=scale)
+        except A.KvmError as e:
+            if e.code in (A.ERR_INVALID_ARGUMENT, A.ERR_NONFINITE):
+                raise ValueError(str(e)) from e
+            if e.code == A.ERR_LENGTH:
+                raise OverflowError(str(e)) from e
+            raise
+        return [float(x) for x in out.cpu().double()]
+
+    def device_bytes(self) -> int:
+        return self.ctx.device_bytes()
+
+
+def pick_scored_blocks(ctx: RecallContext, scores: torch.Tensor, mandatory: Sequence[int], budget: int,
+                       signed_scores: bool = False) -> list:
+    """Mirror of KvMemStore::pick_scored_blocks with candidates = every page of
+    the (device f32) score row and no media groups. Raises ValueError for an
+    invalid candidate or mandatory page (std::invalid_argument) and
+    RuntimeError when mandatory pages exceed the budget (std::runtime_error)."""
+    try:
+        ids, n = ctx.select_topk(scores.view(1, -1), mandatory, budget, signed=signed_scores)
+        ctx.check_status("pick_scored_blocks")
+    except A.KvmError as e:
+        if e.code in (A.ERR_INVALID_ARGUMENT, A.ERR_NONFINITE):
+            raise ValueError(str(e)) from e
+        raise RuntimeError(str(e)) from e
+    return ids[0, : int(n[0])].tolist()

@@ -1,0 +1,276 @@
+"""CPU tests: the oracle against the reference's own known answers and golden vectors.
+
+The known answers restate kvmem/tests/graph_recall_test.cpp:22-106,242-253.
+The golden vectors (tests/golden/reference_cases.json) were produced by the
+reference's CPU code compiled from its sources (tests/golden/make_golden.py).
+"""
+import base64
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests import util as U
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_cases.json")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    with open(GOLDEN) as f:
+        return json.load(f)
+
+
+def means_from_sums(sums, counts):
+    inv = (np.float32(1.0) / np.asarray(counts, np.float32)).astype(np.float32)
+    return (sums * inv[None, :, None]).astype(np.float32)
+
+
+# ---------------------------------------------------------------- known answers
+
+def test_frames_known_answers():
+    f = O.query_score_frame(12, 4, 2, 0, 0, [2])
+    assert f["score_mask"].tolist() == [1, 1, 1] and f["transport_mask"].tolist() == [1, 1, 0]
+    s = O.query_score_frame(11, 4, 4, 1, 1, [0, 2])
+    assert s["score_mask"].tolist() == [1, 1, 1] and s["transport_mask"].tolist() == [0, 0, 0]
+    assert s["counts"][-1] == 3
+    c = O.query_score_frame(12, 4, 2, 1, 1, [0, 2])
+    assert c["score_mask"].tolist() == [0, 1, 0]
+
+
+def test_page_softmax_known_answer():
+    # graph_recall_test.cpp:32-56: keys {8,0},{0,4},{40,0} summed over 4 tokens.
+    frame = O.query_score_frame(12, 4, 2, 0, 0, [2])
+    means = means_from_sums(np.array([[[8, 0], [0, 4], [40, 0]]], np.float32), [4, 4, 4])
+    q = np.array([[[2, 0], [0, 2]]], np.float32)  # one layer, two rows, one head
+    res = O.meank_scores(means, q, [2], heads=1, kv_heads=1, dim=2, score_mask=frame["score_mask"])
+    logits = [[4 / math.sqrt(2), 0, 20 / math.sqrt(2)], [0, 2 / math.sqrt(2), 0]]
+    exp = [0.0, 0.0, 0.0]
+    for line in logits:
+        den = sum(math.exp(v) for v in line)
+        for i in range(3):
+            exp[i] += math.exp(line[i]) / den
+    np.testing.assert_allclose(res, exp, atol=1e-12)
+    assert abs(res.sum() - 2) < 1e-12
+    assert res[1] > res[0]
+    sm = frame["score_mask"].copy()
+    sm[2] = 0
+    wrong = O.meank_scores(means, q, [2], heads=1, kv_heads=1, dim=2, score_mask=sm)
+    assert wrong[0] > wrong[1]
+    empty = O.meank_scores(means, q, [2], heads=1, kv_heads=1, dim=2, score_mask=[0, 0, 0])
+    assert empty.sum() == 0
+
+
+def test_recall_fp16_known_answers():
+    assert O.recall_fp16(1.00048828125) == 1.0
+    assert O.recall_fp16(1.00146484375) == 1.001953125
+    assert O.recall_fp16(2.0 ** -24) == 2.0 ** -24
+    assert O.recall_fp16(2.0 ** -25) == 0.0
+    with pytest.raises(ValueError):
+        O.recall_fp16(65536.0)
+
+
+def test_gqa_and_large_domain():
+    # graph_recall_test.cpp:63-84
+    means = np.array([[[1.0], [-1.0]], [[1.0], [-1.0]]], np.float32)
+    frame = O.query_score_frame(2, 1, 1, 0, 0)
+    q = np.array([[[1, -1]], [[2, -2]]], np.float32)
+    res = O.meank_scores(means, q, [1, 1], heads=2, kv_heads=1, dim=1, score_mask=frame["score_mask"])
+    np.testing.assert_allclose(res, [0.5, 0.5], atol=1e-12)
+    for n in (8192, 8193, 32768, 32769):
+        f = O.query_score_frame(n, 1, 1, 0, 0)
+        s = O.meank_scores(np.ones((1, n, 1), np.float32), np.ones((1, 1, 1), np.float32), [1], heads=1,
+                           kv_heads=1, dim=1, score_mask=f["score_mask"])
+        assert abs(s[0] - 1 / n) < 1e-12 and abs(s[-1] - 1 / n) < 1e-12
+        assert abs(s.sum() - 1) < 2e-12
+
+
+def test_max_aggregation_and_signed_picker():
+    # graph_recall_test.cpp:85-105
+    means = np.array([[[1, 0], [0, 1], [-1, -1]]], np.float32)
+    q = np.array([[[2, 0, 0, 2], [2, 0, 0, 2]]], np.float32)
+    frame = O.query_score_frame(3, 1, 2, 0, 0)
+    a, b, c = math.exp(math.sqrt(2)), 1.0, math.exp(-math.sqrt(2))
+    mx, neg = a / (a + b + c), c / (a + b + c)
+    mass = 2 * mx + neg
+    s = O.meank_scores(means, q, [2], heads=2, kv_heads=1, dim=2, score_mask=frame["score_mask"], aggregation=1)
+    np.testing.assert_allclose(s, [2 * mx / mass, 2 * mx / mass, 2 * neg / mass], atol=1e-12)
+    rc, ids = O.pick_scored(3, [0, 1, 2], [-.8, -.2, -.5], [], 2, signed=True)
+    assert rc == 0 and ids.tolist() == [1, 2]
+    rc, _ = O.pick_scored(3, [0, 1, 2], [-.8, -.2, -.5], [], 2)
+    assert rc == O.ERR_INVALID
+
+
+def test_fixed_picker_media_rejects():
+    # graph_recall_test.cpp:250-252
+    rc, _ = O.pick_scored(6, [0, 3, 4, 5], [0, 1, 9, 8], [0, 3], 4, block_tokens=4, ranges=[(4, 9), (9, 13)])
+    assert rc == O.ERR_RUNTIME
+
+
+# ---------------------------------------------------------------- golden vectors
+
+def test_golden_frames(golden):
+    for c in golden["frames"]:
+        f = O.query_score_frame(*c["args"], c["fixed"])
+        assert f["score_mask"].tolist() == c["score_mask"]
+        assert f["transport_mask"].tolist() == c["transport_mask"]
+        assert f["counts"].tolist() == c["counts"]
+
+
+def test_golden_recall_fp16(golden):
+    for v, expected in golden["recall_fp16"]:
+        value = float(v)
+        if expected is None:
+            with pytest.raises(ValueError):
+                O.recall_fp16(value)
+        else:
+            assert O.recall_fp16(value) == expected, v
+
+
+def test_golden_page_softmax(golden):
+    for c in golden["page_softmax"]:
+        L, P, R, D, Hq, Hkv = c["L"], c["P"], c["R"], c["D"], c["Hq"], c["Hkv"]
+        sums = np.frombuffer(base64.b64decode(c["sums_f32_b64"]), np.float32).reshape(L, P, Hkv * D)
+        q = np.frombuffer(base64.b64decode(c["q_f32_b64"]), np.float32).reshape(L, R, Hq * D)
+        accepted = (P - 1) * c["block"] + c["counts"][-1]
+        frame = O.query_score_frame(accepted, c["block"], c["budget"], c["sink"], c["recent"], c["fixed"])
+        means = means_from_sums(sums, c["counts"])
+        for agg, key in ((0, "expected_mean"), (1, "expected_max")):
+            got = O.meank_scores(means, q, c["layer_rows"], heads=Hq, kv_heads=Hkv, dim=D,
+                                 score_mask=frame["score_mask"], aggregation=agg)
+            np.testing.assert_allclose(got, c[key], rtol=1e-12, atol=1e-15)
+
+
+def test_golden_pick(golden):
+    for c in golden["pick"]:
+        rc, ids = O.pick_scored(c["n"], list(range(c["n"])), c["scores"], c["mandatory"], c["budget"],
+                                signed=c["signed"])
+        assert rc == c["rc"]
+        if rc == 0:
+            assert ids.tolist() == c["ids"]
+    for c in golden["media_pick"]:
+        rc, ids = O.pick_scored(6, c["cand"], c["scores"], c["mandatory"], c["budget"], block_tokens=4,
+                                ranges=[(4, 9), (9, 13)])
+        assert rc == c["rc"]
+        if rc == 0:
+            assert ids.tolist() == c["ids"]
+
+
+def test_golden_residency(golden):
+    for c in golden["residency"]:
+        rc, d = O.plan_residency(c["resident"], c["selected"], c["force"])
+        assert rc == c["rc"]
+        if rc == 0:
+            assert d["evict"].tolist() == c["evict"]
+            assert d["retain"].tolist() == c["retain"]
+            assert d["restore"].tolist() == c["restore"]
+
+
+# ---------------------------------------------------------------- live reference (when built here)
+
+@pytest.mark.skipif(O.ref() is None, reason="reference library not built (needs the reference sources)")
+def test_live_reference_random_picks():
+    rng = np.random.default_rng(3)
+    for i in range(200):
+        n = int(rng.integers(1, 600))
+        scores = rng.random(n).astype(np.float32).astype(np.float64)
+        if i % 2:
+            scores = np.round(scores * 3) / 3
+        budget = int(rng.integers(1, n + 2))
+        mand = sorted(set(int(x) for x in rng.integers(0, n, int(rng.integers(0, 3)))))
+        a = O.pick_scored(n, list(range(n)), scores, mand, budget)
+        b = O.pick_scored(n, list(range(n)), scores, mand, budget, use_ref=True)
+        assert a[0] == b[0]
+        if a[0] == 0:
+            assert a[1].tolist() == b[1].tolist()
+
+
+# ---------------------------------------------------------------- per-token page mass oracle
+
+def dense_page_mass(qv, kv, tokens, page, scale, softcap=0.0, bias=None):
+    """Independent numpy restatement for one (layer, row): qv [Hq, D] f64, kv [T, Hkv, D] f64."""
+    Hq, Hkv = qv.shape[0], kv.shape[1]
+    G = Hq // Hkv
+    pages = -(-tokens // page)
+    out = np.zeros(pages)
+    for h in range(Hq):
+        lg = kv[:tokens, h // G, :] @ qv[h] * scale
+        if softcap > 0:
+            lg = softcap * np.tanh(lg / softcap)
+        if bias is not None:
+            lg = lg + bias[:tokens]
+        p = np.exp(lg - lg.max())
+        p /= p.sum()
+        np.add.at(out, np.arange(tokens) // page, p / Hq)
+    return out
+
+
+@pytest.mark.parametrize("ktype", [U.F32, U.F16, U.BF16])
+def test_page_mass_float_types_against_numpy(ktype):
+    rng = np.random.default_rng(ktype)
+    L, R, Hq, Hkv, D, T, page = 2, 2, 4, 2, 32, 50, 8
+    kb = U.make_k(rng, ktype, L, 56, Hkv, D)
+    qb = U.make_q(rng, U.F32, L, R, Hq, D)
+    m = O.page_mass(qb, U.F32, kb, ktype, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                    page_tokens=page, scale=0.3, softcap=2.0 if ktype == U.F16 else 0.0)
+    qv = qb.view(np.float32).reshape(L, R, Hq, D).astype(np.float64)
+    if ktype == U.F32:
+        kv = kb.view(np.float32)
+    elif ktype == U.F16:
+        kv = kb.view(np.float16).astype(np.float32)
+    else:
+        kv = (kb.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    kv = kv.reshape(L, 56, Hkv, D).astype(np.float64)
+    for l in range(L):
+        for r in range(R):
+            exp = dense_page_mass(qv[l, r], kv[l], T, page, 0.3, 2.0 if ktype == U.F16 else 0.0)
+            np.testing.assert_allclose(m[l, 0, r], exp, rtol=1e-12, atol=1e-15)
+            assert abs(m[l, 0, r].sum() - 1) < 1e-12
+
+
+def decode_blocks(raw, ktype, D):
+    """Independent numpy decode of GGUF q8_0 / q4_0 / q5_0 rows."""
+    nb = D // 32
+    bb = U.BLOCK_BYTES[ktype]
+    blk = raw.reshape(-1, nb, bb)
+    d = blk[:, :, 0:2].copy().view(np.float16).astype(np.float64)[..., 0]
+    if ktype == U.Q8_0:
+        codes = blk[:, :, 2:].view(np.int8).astype(np.float64)
+    elif ktype == U.Q4_0:
+        qs = blk[:, :, 2:18]
+        codes = np.concatenate([qs & 15, qs >> 4], axis=2).astype(np.float64) - 8
+    else:
+        qh = blk[:, :, 2:6].copy().view(np.uint32)[..., 0]
+        qs = blk[:, :, 6:22]
+        low = np.concatenate([qs & 15, qs >> 4], axis=2).astype(np.int64)
+        high = (qh[..., None] >> np.arange(32)) & 1
+        codes = (low | (high << 4)).astype(np.float64) - 16
+    return (codes * d[..., None]).reshape(-1, D)
+
+
+@pytest.mark.parametrize("ktype", [U.Q8_0, U.Q4_0, U.Q5_0])
+def test_quant_decode_against_numpy(ktype):
+    rng = np.random.default_rng(ktype + 10)
+    D = 64
+    raw = U.make_quant_rows(rng, ktype, 5, D)
+    lib = O.lib()
+    got = np.array([[lib.kvo_decode(ktype, raw[i].ctypes.data, d) for d in range(D)] for i in range(5)])
+    np.testing.assert_array_equal(got, decode_blocks(raw, ktype, D))
+
+
+def test_page_mass_groups_mask_and_empty_rows():
+    rng = np.random.default_rng(2)
+    L, R, Hq, Hkv, D, T, page = 1, 2, 4, 2, 32, 24, 8
+    kb = U.make_k(rng, U.F16, L, T, Hkv, D)
+    qb = U.make_q(rng, U.F16, L, R, Hq, D)
+    mask = np.zeros((R, T), np.float32)
+    mask[0, 5:9] = -np.inf
+    mask[1, :] = -np.inf  # row 1 sees nothing -> NaN, as the reference's normaliser
+    m = O.page_mass(qb, U.F16, kb, U.F16, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                    page_tokens=page, scale=0.2, groups=Hkv, mask=mask)
+    assert m.shape == (1, 2, 2, 3)
+    np.testing.assert_allclose(m[0, :, 0].sum(axis=1), [1, 1], atol=1e-12)
+    assert np.isnan(m[0, :, 1]).all()

@@ -1,0 +1,76 @@
+"""Seeded synthetic inputs for the tests (host numpy; uploaded as raw bytes)."""
+from __future__ import annotations
+
+import numpy as np
+
+F32, F16, BF16, Q8_0, Q4_0, Q5_0 = 0, 1, 2, 3, 4, 5
+BLOCK_BYTES = {Q8_0: 34, Q4_0: 18, Q5_0: 22}
+
+
+def row_bytes(ktype: int, dim: int) -> int:
+    if ktype == F32:
+        return 4 * dim
+    if ktype in (F16, BF16):
+        return 2 * dim
+    return dim // 32 * BLOCK_BYTES[ktype]
+
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def encode(vals: np.ndarray, ktype: int) -> np.ndarray:
+    """f32 values [..., D] -> bytes [..., row_bytes] of ktype (float types only)."""
+    if ktype == F32:
+        return np.ascontiguousarray(vals, np.float32).view(np.uint8)
+    if ktype == F16:
+        return np.ascontiguousarray(vals.astype(np.float16)).view(np.uint8)
+    if ktype == BF16:
+        return to_bf16_bits(vals).view(np.uint8)
+    raise ValueError(ktype)
+
+
+def make_quant_rows(rng, ktype: int, nrows: int, dim: int) -> np.ndarray:
+    """Random GGUF blocks: q8_0 codes round(N(0,1)*40) clamped to +-127, scales U(0.005,0.03)."""
+    nb = dim // 32
+    out = np.zeros((nrows, nb, BLOCK_BYTES[ktype]), np.uint8)
+    d = rng.uniform(0.005, 0.03, (nrows, nb)).astype(np.float16)
+    out[:, :, 0:2] = d.view(np.uint8).reshape(nrows, nb, 2)
+    if ktype == Q8_0:
+        qs = np.clip(np.round(rng.standard_normal((nrows, nb, 32)) * 40), -127, 127).astype(np.int8)
+        out[:, :, 2:] = qs.view(np.uint8)
+    elif ktype == Q4_0:
+        out[:, :, 2:] = rng.integers(0, 256, (nrows, nb, 16), dtype=np.uint8)
+    else:
+        out[:, :, 2:] = rng.integers(0, 256, (nrows, nb, 20), dtype=np.uint8)
+    return out.reshape(nrows, nb * BLOCK_BYTES[ktype])
+
+
+def make_k(rng, ktype: int, layers: int, tokens: int, kv_heads: int, dim: int, needle_pages=(), page=64,
+           q_dir=None) -> np.ndarray:
+    """K history bytes [layers, tokens, kv_heads, row_bytes]."""
+    if ktype in (Q8_0, Q4_0, Q5_0):
+        raw = make_quant_rows(rng, ktype, layers * tokens * kv_heads, dim)
+        return raw.reshape(layers, tokens, kv_heads, -1)
+    vals = rng.standard_normal((layers, tokens, kv_heads, dim)).astype(np.float32)
+    if q_dir is not None:
+        for p in needle_pages:
+            sl = slice(p * page, (p + 1) * page)
+            vals[:, sl] = 0.8 * q_dir[:, None, :, :] * np.sqrt(dim) + 0.6 * vals[:, sl]
+    return encode(vals, ktype).reshape(layers, tokens, kv_heads, -1)
+
+
+def make_q(rng, qtype: int, layers: int, rows: int, heads: int, dim: int) -> np.ndarray:
+    """Query bytes [layers, rows, heads, dim*esize]."""
+    vals = rng.standard_normal((layers, rows, heads, dim)).astype(np.float32)
+    return encode(vals, qtype).reshape(layers, rows, heads, -1)
+
+
+def close(actual, expected, rel=1e-3, abs_=1e-6):
+    actual = np.asarray(actual, np.float64)
+    expected = np.asarray(expected, np.float64)
+    err = np.abs(actual - expected)
+    bound = abs_ + rel * np.abs(expected)
+    bad = ~(err <= bound)
+    return not bad.any(), float(err.max(initial=0.0)), int(bad.sum())
