@@ -219,7 +219,9 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_kernel(const LseParam
             for (int i = 0; i < 8; ++i)
                 qv[v][i] = ok ? load_scalar(qp + (lig * 8 + i) * type_bytes(P.q_type), P.q_type) : 0.f;
         }
-        const uint32_t myr = (P.v0 + myv) / P.group;
+        // Row of this lane's query vector; lanes that own a padding vector
+        // (myv >= nv) read row 0 so their mask reads stay in bounds.
+        const uint32_t myr = myv < int(P.nv) ? (P.v0 + myv) / P.group : 0;
         float m = -INFINITY, ssum = 0.f;
         const uint64_t tok0 = uint64_t(p) * P.page_tokens;
 
