@@ -1,0 +1,461 @@
+"""Benchmark of the per-decode-step history recall (score -> top-k -> residency plan -> stage-in).
+
+Default workload: config 2 of the reference's headline (a 128K-token fp16
+history, 64 layers, 24/4 heads, head_dim 256, pages of 256 tokens, top-32 plus
+first/last page, stage-in of the selected pages' K and V from pinned host
+memory into a device paged cache). One step = one decode step's recall over
+all 64 layers, steady state: queries drift per step (seeded) and only pages
+not already resident are staged. Prints one JSON line (rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3] [--impl ours|reference]
+
+Multi-GPU (torchrun): every rank runs an independent decode lane (replica) of
+the workload; value = all ranks' token-layers / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import csv
+import ctypes as C
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "select+stage-in ms/decode step @128K; KV tokens scored/s; % HBM roofline"
+UNIT = "KV token-layers/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--chunks", type=int, default=4)
+    ap.add_argument("--stage-ctas", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# --------------------------------------------------------------------------- data
+
+def build_history(w, seed, device, need_host=True):
+    """K score mirror on the device, pinned host K/V pages, device paged cache."""
+    import torch
+    from kvmem_b200 import row_bytes, synth
+    rbk = row_bytes(w.k_type, w.head_dim)
+    rbv = row_bytes(w.v_type, w.head_dim)
+    T = w.pages * w.page_tokens
+    layer_k = T * w.kv_heads * rbk
+    layer_v = T * w.kv_heads * rbv
+    q_base, drift = synth.make_queries(w, seed, device, drift_steps=8)
+    k_dev = torch.empty(w.layers * layer_k, dtype=torch.uint8, device=device)
+    host_k = host_v = None
+    if need_host:
+        host_k = torch.empty(w.layers * layer_k, dtype=torch.uint8, pin_memory=True)
+        host_v = torch.empty(w.layers * layer_v, dtype=torch.uint8, pin_memory=True)
+    for l in range(w.layers):
+        if w.k_type == 1:
+            kl = synth.fp16_layer(w, seed, l, q_base, device).view(torch.uint8).reshape(-1)
+        else:
+            kl = synth.q8_0_layer(w, seed, l, q_base, device).reshape(-1)
+        k_dev[l * layer_k:(l + 1) * layer_k].copy_(kl)
+        if need_host:
+            host_k[l * layer_k:(l + 1) * layer_k].copy_(kl)
+            vl = (synth.fp16_v_layer(w, seed, l, device).view(torch.uint8).reshape(-1) if w.v_type == 1
+                  else synth.q4_0_v_layer(w, seed, l, device).reshape(-1))
+            host_v[l * layer_v:(l + 1) * layer_v].copy_(vl)
+        del kl
+    torch.cuda.synchronize()
+    return dict(q_base=q_base, drift=drift, k_dev=k_dev, host_k=host_k, host_v=host_v, layer_k=layer_k,
+                layer_v=layer_v, rbk=rbk, rbv=rbv)
+
+
+# --------------------------------------------------------------------------- our arm
+
+def run_ours(args, world, rank, local):
+    import torch
+    import kvmem_b200 as K
+    from kvmem_b200 import synth
+    w = synth.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    seed = args.seed + rank
+    h = build_history(w, seed, dev)
+    ctx = K.RecallContext(local)
+    P, L = w.pages, w.layers
+    srows = L * w.groups
+    page_k = w.page_tokens * w.kv_heads * h["rbk"]
+    page_v = w.page_tokens * w.kv_heads * h["rbv"]
+    slots = w.budget
+    cache_k = torch.zeros(srows * slots * page_k // w.groups, dtype=torch.uint8, device=dev)
+    cache_v = torch.zeros(srows * slots * page_v // w.groups, dtype=torch.uint8, device=dev)
+    assert w.groups == 1, "stage-in geometry of this bench is per-layer selection"
+    layout = K.stage_layout([
+        dict(host_base=h["host_k"].data_ptr(), host_row_stride=h["layer_k"], host_page_stride=page_k,
+             dev_base=cache_k.data_ptr(), dev_row_stride=slots * page_k, dev_slot_stride=page_k, bytes=page_k),
+        dict(host_base=h["host_v"].data_ptr(), host_row_stride=h["layer_v"], host_page_stride=page_v,
+             dev_base=cache_v.data_ptr(), dev_row_stride=slots * page_v, dev_slot_stride=page_v, bytes=page_v)])
+    pool = K.ResidencyPool(ctx, srows, P, slots)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=P * w.page_tokens)
+    qs = [h["q_base"]] + h["drift"]
+    qdescs = [K.RecallContext.make_query(q, w.rows) for q in qs]
+    mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
+    sel_ids = torch.empty((srows, w.budget), dtype=torch.int32, device=dev)
+    sel_n = torch.empty((srows,), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i, force=False, with_layout=True, qd=None):
+        ctx.recall_step(desc, qd or qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
+                        sel_n=sel_n, pool=pool, layout=layout if with_layout else None, chunks=args.chunks,
+                        stage_ctas=args.stage_ctas, force_reload=force)
+
+    # Warm-up, then the timed steady state.
+    for i in range(args.warmup):
+        step(i)
+    ctx.wait(120.0)
+    a0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.launches - a0
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    ctx.check_status("timed steps")
+
+    # Pages restored per steady step (replayed untimed, selection only).
+    restored = []
+    prev = None
+    for i in range(args.warmup, args.warmup + min(args.steps, 8)):
+        ctx.recall_step(desc, qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
+                        sel_n=sel_n, chunks=args.chunks)
+        ids, n = sel_ids.cpu().numpy(), sel_n.cpu().numpy()
+        cur = [set(ids[r, : n[r]].tolist()) for r in range(srows)]
+        if prev is not None:
+            restored.append(sum(len(c - p) for c, p in zip(cur, prev)))
+        prev = cur
+    restored_per_step = float(np.mean(restored)) if restored else 0.0
+
+    # Cold worst case: every selected page staged every step.
+    n_cold = max(3, min(10, args.steps))
+    step(0, force=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0.record(stream)
+    for i in range(n_cold):
+        step(i, force=True)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms_cold = max_over_ranks(ev0.elapsed_time(ev1) / n_cold, world)
+    cold_bytes = srows * w.budget * (page_k + page_v)
+
+    # Stage-in alone (the gather of a full cold plan) -> link GB/s.
+    pool.plan(sel_ids, sel_n, force_reload=True)
+    pool.stage_in(layout, ctas=args.stage_ctas)
+    torch.cuda.synchronize()
+    g_ms = []
+    for _ in range(3):
+        pool.plan(sel_ids, sel_n, force_reload=True)
+        ev0.record(stream)
+        pool.stage_in(layout, ctas=args.stage_ctas)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        g_ms.append(ev0.elapsed_time(ev1))
+    gather_ms = statistics.median(g_ms)
+
+    # Dominant kernel alone: the page log-sum-exp pass over all layers (+ its tiny normaliser).
+    kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
+    for _ in range(2):
+        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
+    torch.cuda.synchronize()
+    n_k = 10
+    ev0.record(stream)
+    for _ in range(n_k):
+        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = ev0.elapsed_time(ev1) / n_k
+    hbm_peak, peak_src = peaks()
+    achieved = kbytes / (kernel_ms * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get(f"page_lse_{args.config}")
+        except Exception:
+            traffic = None
+
+    # End to end through the C ABI with host buffers: H2D of the step's queries,
+    # the step, D2H of the selection.
+    q_host = [q.cpu().pin_memory() for q in qs]
+    q_dev = torch.empty_like(qs[0])
+    qd_e2e = K.RecallContext.make_query(q_dev, w.rows)
+    ids_host = torch.empty(sel_ids.shape, dtype=torch.int32, pin_memory=True)
+    n_host = torch.empty(sel_n.shape, dtype=torch.int32, pin_memory=True)
+    h2d = q_host[0].numel() * 4
+    d2h = ids_host.numel() * 4 + n_host.numel() * 4
+    for i in range(2):
+        q_dev.copy_(q_host[i % len(q_host)], non_blocking=True)
+        step(i, qd=qd_e2e)
+        ids_host.copy_(sel_ids, non_blocking=True)
+        n_host.copy_(sel_n, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0.record(stream)
+    for i in range(args.steps):
+        q_dev.copy_(q_host[i % len(q_host)], non_blocking=True)
+        step(args.warmup + i, qd=qd_e2e)
+        ids_host.copy_(sel_ids, non_blocking=True)
+        n_host.copy_(sel_n, non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+
+    token_layers = L * w.tokens
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_port(w, h)
+
+    pool.close()
+    ctx.close()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": world * token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if w.k_type == 1 else "q8_0",
+        "data": "synthetic: seeded on-device N(0,1) K/V with per-channel scale U(0.5,2) and planted needle pages",
+        "config": {"workload": w.name, "layers": L, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
+                   "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": w.page_tokens, "pages": P,
+                   "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
+                   "step": "score all pages -> top-k -> residency plan -> stage-in of non-resident pages "
+                           "(seeded query drift)"},
+        "restored_pages_per_step": restored_per_step,
+        "clocks": clk.summary(),
+        "e2e": {"value": world * token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "page_lse_kernel (+page_mass_normalize_kernel)",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "peak_source": peak_src, "traffic": traffic, "kernel_ms": kernel_ms,
+                     "algorithmic_bytes": kbytes},
+        "cold": {"ms_per_step": ms_cold, "stage_bytes_per_step": cold_bytes,
+                 "note": "every selected page staged every step (force_reload)"},
+        "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
+                    "ctas": args.stage_ctas, "link": "PCIe Gen5 x16 (mapped pinned host reads)"},
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_port(w, h):
+    """FP64 per-token page mass of the oracle port (single thread) on a bounded sample."""
+    from oracle import oracle as O
+    tokens = 32768 if w.tokens >= 32768 else w.tokens
+    rb = h["rbk"]
+    k0 = h["host_k"][: tokens * w.kv_heads * rb].numpy()
+    q0 = h["q_base"][0:1].cpu().numpy().astype(np.float32)
+    t0 = time.perf_counter()
+    O.page_mass(q0, O.F32, k0, w.k_type, layers=1, rows=w.rows, heads=w.q_heads, kv_heads=w.kv_heads,
+                dim=w.head_dim, tokens=tokens, page_tokens=w.page_tokens, scale=1 / np.sqrt(w.head_dim),
+                k_strides=(tokens * w.kv_heads * rb, w.kv_heads * rb, rb))
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"1 layer x {tokens} tokens x {w.q_heads} heads, FP64 oracle restatement "
+                      f"(AttentionSampler::qualify), {dt:.1f} s"}
+
+
+# --------------------------------------------------------------------------- reference arm
+
+def run_reference(args, world, rank, local):
+    """The reference's own CPU selection path on the host cores: per layer,
+    query_score_frame + page_softmax_scores (Mean-K over the pages' mean keys of the
+    same K) + pick_scored_blocks, from oracle/_ref (compiled from the reference's
+    sources); the C restatement stands in when that library is absent."""
+    if rank != 0:
+        return
+    import torch
+    from kvmem_b200 import synth
+    from oracle import oracle as O
+    w = synth.CONFIGS[args.config]
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    L, P, T = w.layers, w.pages, w.pages * w.page_tokens
+    q_base, drift = synth.make_queries(w, args.seed, dev, drift_steps=8)
+    sums = np.empty((L, P, w.kv_heads * w.head_dim), np.float32)
+    for l in range(L):
+        if w.k_type == 1:
+            kl = synth.fp16_layer(w, args.seed, l, q_base, dev).float()
+        else:
+            raw = synth.q8_0_layer(w, args.seed, l, q_base, dev).view(T, w.kv_heads, w.head_dim // 32, 34)
+            d = raw[..., 0:2].contiguous().view(torch.float16).float()
+            kl = (raw[..., 2:].contiguous().view(torch.int8).float() * d).view(T, w.kv_heads, w.head_dim)
+        sums[l] = kl.view(P, w.page_tokens, -1).sum(dim=1).cpu().numpy()
+    counts = np.full(P, w.page_tokens, np.uint32)
+    queries = [q.view(L, w.rows, -1).cpu().numpy() for q in [q_base] + drift]
+    use_ref = O.ref() is not None
+    threads = os.cpu_count() or 1
+
+    def layer_select(l, q):
+        ql = np.ascontiguousarray(q[l:l + 1])
+        rows = np.array([w.rows], np.uint32)
+        if use_ref:
+            s = O.ref_page_softmax_scores(sums[l:l + 1], counts, ql, rows, heads=w.q_heads, kv_heads=w.kv_heads,
+                                          dim=w.head_dim, block=w.page_tokens, accepted=w.tokens, budget=w.budget,
+                                          sink=1, recent=1, fixed=w.keep)
+        else:
+            f = O.query_score_frame(w.tokens, w.page_tokens, w.budget, 1, 1, w.keep)
+            means = sums[l:l + 1] * (np.float32(1) / counts.astype(np.float32))[None, :, None]
+            s = O.meank_scores(means, ql, rows, heads=w.q_heads, kv_heads=w.kv_heads, dim=w.head_dim,
+                               score_mask=f["score_mask"])
+        rc, ids = O.pick_scored(P, list(range(P)), s, w.keep, w.budget, use_ref=use_ref)
+        return ids
+
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+
+    def one_step(i):
+        q = queries[i % len(queries)]
+        list(pool.map(lambda l: layer_select(l, q), range(L)))
+
+    for i in range(args.warmup):
+        one_step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one_step(args.warmup + i)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = L * w.tokens / dt
+    kind = "reference" if use_ref else "port"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (same generator and seed as the GPU arm)",
+        "config": {"workload": w.name, "layers": L, "pages": P, "top_k": w.top_k, "selection": "per layer"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": "full step: every layer's Mean-K page softmax + pick_scored_blocks "
+                                   "(reference CPU selection path), layers spread over host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,128 @@
+"""Seeded synthetic workloads for the benchmark configurations, generated on the device.
+
+Config 2 (the headline): 64 layers, 24 query / 4 KV heads, head_dim 256,
+131,072-token history in pages of 256 (512 pages per layer), fp16 K and V
+~ N(0,1) times a per-channel scale ~ U(0.5, 2); 32 needle pages per layer whose
+K rows are 0.8 * q_dir + 0.6 * N(0,1) (times the channel scale), q_dir being the
+layer's mean query direction of the KV head's group normalised to unit RMS;
+one decode query per head ~ N(0,1); top-32 plus first / last page kept.
+
+Everything is produced by torch generators seeded per (seed, layer) so a rerun
+gives the same bytes; host copies (for stage-in) are pinned and mapped.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class Workload:
+    name: str
+    layers: int
+    q_heads: int
+    kv_heads: int
+    head_dim: int
+    tokens: int
+    page_tokens: int
+    top_k: int
+    needles: int
+    keep_first_last: bool = True
+    groups: int = 1          # 1: per-layer selection; kv_heads: per (layer, KV head)
+    rows: int = 1            # query rows per decode step (replay rows)
+    k_type: int = 1          # kvm_type of K (1 = F16, 3 = Q8_0)
+    v_type: int = 1          # kvm_type of V (1 = F16, 4 = Q4_0)
+
+    @property
+    def pages(self) -> int:
+        return -(-self.tokens // self.page_tokens)
+
+    @property
+    def budget(self) -> int:
+        return self.top_k + (2 if self.keep_first_last else 0)
+
+    @property
+    def keep(self):
+        return [0, self.pages - 1] if self.keep_first_last else []
+
+
+CONFIGS = {
+    "c1": Workload("c1_cpu16k", 4, 32, 8, 128, 16384, 64, 16, 8, groups=8),
+    "c2": Workload("c2_fp16_128k", 64, 24, 4, 256, 131072, 256, 32, 32),
+    "c3": Workload("c3_q8k_q4v_256k", 64, 24, 4, 256, 262144, 256, 64, 32, k_type=3, v_type=4),
+}
+
+
+def _gen(seed: int, layer: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + layer * 7919 + 17)
+    return g
+
+
+def make_queries(w: Workload, seed: int, device, drift_steps: int = 0, drift: float = 0.35):
+    """Base queries [L][R][Hq][D] f32 and `drift_steps` drifted copies (q + drift * N(0,1))."""
+    g = _gen(seed, 10_000, device)
+    q = torch.randn((w.layers, w.rows, w.q_heads, w.head_dim), generator=g, device=device)
+    drifted = [q + drift * torch.randn(q.shape, generator=g, device=device) for _ in range(drift_steps)]
+    return q, drifted
+
+
+def needle_pages(w: Workload, seed: int, layer: int, device) -> torch.Tensor:
+    g = _gen(seed, 20_000 + layer, device)
+    inner = torch.randperm(w.pages - 2, generator=g, device=device)[: w.needles] + 1
+    return torch.sort(inner).values
+
+
+def fp16_layer(w: Workload, seed: int, layer: int, q: torch.Tensor, device) -> torch.Tensor:
+    """K of one layer, fp16 [tokens_alloc][Hkv][D], with the layer's needle pages planted."""
+    g = _gen(seed, layer, device)
+    T = w.pages * w.page_tokens
+    scale = torch.rand((w.kv_heads, w.head_dim), generator=g, device=device) * 1.5 + 0.5
+    z = torch.randn((T, w.kv_heads, w.head_dim), generator=g, device=device)
+    G = w.q_heads // w.kv_heads
+    qd = q[layer].mean(dim=0).view(w.kv_heads, G, w.head_dim).mean(dim=1)  # [Hkv][D]
+    qd = qd / qd.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    pages = needle_pages(w, seed, layer, device)
+    zp = z.view(w.pages, w.page_tokens, w.kv_heads, w.head_dim)
+    zp[pages] = 0.8 * qd + 0.6 * zp[pages]
+    return (z * scale).to(torch.float16)
+
+
+def fp16_v_layer(w: Workload, seed: int, layer: int, device) -> torch.Tensor:
+    g = _gen(seed, 30_000 + layer, device)
+    T = w.pages * w.page_tokens
+    scale = torch.rand((w.kv_heads, w.head_dim), generator=g, device=device) * 1.5 + 0.5
+    return (torch.randn((T, w.kv_heads, w.head_dim), generator=g, device=device) * scale).to(torch.float16)
+
+
+def q8_0_layer(w: Workload, seed: int, layer: int, q: torch.Tensor, device) -> torch.Tensor:
+    """GGUF q8_0 K of one layer as bytes [tokens_alloc][Hkv][D/32*34]: codes
+    round(N(0,1)*40) clamped to +-127 (needle rows: round(40*(0.8 q_dir + 0.6 z))), scales U(0.005, 0.03)."""
+    g = _gen(seed, layer, device)
+    T = w.pages * w.page_tokens
+    nb = w.head_dim // 32
+    z = torch.randn((T, w.kv_heads, w.head_dim), generator=g, device=device)
+    G = w.q_heads // w.kv_heads
+    qd = q[layer].mean(dim=0).view(w.kv_heads, G, w.head_dim).mean(dim=1)
+    qd = qd / qd.pow(2).mean(dim=-1, keepdim=True).sqrt()
+    pages = needle_pages(w, seed, layer, device)
+    zp = z.view(w.pages, w.page_tokens, w.kv_heads, w.head_dim)
+    zp[pages] = 0.8 * qd + 0.6 * zp[pages]
+    codes = torch.clamp(torch.round(z * 40), -127, 127).to(torch.int8).view(T, w.kv_heads, nb, 32)
+    d = (torch.rand((T, w.kv_heads, nb), generator=g, device=device) * 0.025 + 0.005).to(torch.float16)
+    out = torch.empty((T, w.kv_heads, nb, 34), dtype=torch.uint8, device=device)
+    out[..., 0:2] = d.view(torch.uint8).view(T, w.kv_heads, nb, 2)
+    out[..., 2:] = codes.view(torch.uint8)
+    return out.view(T, w.kv_heads, nb * 34)
+
+
+def q4_0_v_layer(w: Workload, seed: int, layer: int, device) -> torch.Tensor:
+    g = _gen(seed, 30_000 + layer, device)
+    T = w.pages * w.page_tokens
+    nb = w.head_dim // 32
+    out = torch.empty((T, w.kv_heads, nb, 18), dtype=torch.uint8, device=device)
+    d = (torch.rand((T, w.kv_heads, nb), generator=g, device=device) * 0.025 + 0.005).to(torch.float16)
+    out[..., 0:2] = d.view(torch.uint8).view(T, w.kv_heads, nb, 2)
+    out[..., 2:] = torch.randint(0, 256, (T, w.kv_heads, nb, 16), generator=g, device=device, dtype=torch.uint8)
+    return out.view(T, w.kv_heads, nb * 18)
