@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--chunks", type=int, default=4)
     ap.add_argument("--stage-ctas", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the page scorer (no host history, no stage-in); for ncu captures")
     return ap.parse_args()
 
 
@@ -171,11 +174,53 @@ def build_history(w, seed, device, need_host=True):
 
 # --------------------------------------------------------------------------- our arm
 
+def workload(args):
+    import dataclasses
+    from kvmem_b200 import synth
+    w = synth.CONFIGS[args.config]
+    if args.layers:
+        w = dataclasses.replace(w, layers=args.layers)
+    return w
+
+
+def run_kernel_only(args, w, local):
+    """The page scorer alone over the workload (device-resident K), for profiling."""
+    import torch
+    import kvmem_b200 as K
+    dev = torch.device("cuda", local)
+    h = build_history(w, args.seed, dev, need_host=False)
+    ctx = K.RecallContext(local)
+    L, P = w.layers, w.pages
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=P * w.page_tokens)
+    qd = K.RecallContext.make_query(h["q_base"], w.rows)
+    mass = torch.empty((L, w.groups, P), dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        ctx.score_pages(desc, qd, kc, want_rows=False, out_mean=mass)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        ctx.score_pages(desc, qd, kc, want_rows=False, out_mean=mass)
+    ev1.record()
+    torch.cuda.synchronize()
+    ctx.check_status("kernel-only")
+    ms = ev0.elapsed_time(ev1) / args.steps
+    kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
+    peak, src = peaks()
+    print(json.dumps({"kernel_only": w.name, "layers": L, "ms": ms, "GB/s": kbytes / ms / 1e6,
+                      "frac": kbytes / ms / 1e6 / peak, "peak_source": src, "launches": ctx.launches}), flush=True)
+    ctx.close()
+
+
 def run_ours(args, world, rank, local):
     import torch
     import kvmem_b200 as K
-    from kvmem_b200 import synth
-    w = synth.CONFIGS[args.config]
+    w = workload(args)
+    if args.kernel_only:
+        return run_kernel_only(args, w, local)
     dev = torch.device("cuda", local)
     seed = args.seed + rank
     h = build_history(w, seed, dev)
@@ -383,7 +428,7 @@ def run_reference(args, world, rank, local):
     import torch
     from kvmem_b200 import synth
     from oracle import oracle as O
-    w = synth.CONFIGS[args.config]
+    w = workload(args)
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     L, P, T = w.layers, w.pages, w.pages * w.page_tokens
     q_base, drift = synth.make_queries(w, args.seed, dev, drift_steps=8)
