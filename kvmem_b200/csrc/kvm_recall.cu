@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -103,7 +104,42 @@ int upload_keep(kvm_ctx* c, const uint32_t* keep, uint32_t nkeep) {
 struct LseConfig {
     uint32_t lpr = 0, tpc = 0, chunk_bytes = 0, chunks = 0, row_bytes = 0, stage_stride = 0;
     size_t smem = 0;
+    // Tensor-core scorer (fp16 / q8_0 / q4_0 keys, 1/2/4/8 KV heads), when usable.
+    bool mma = false;
+    uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0;
+    size_t mma_smem = 0;
 };
+
+// Scorer selection: KVM_SCORER=simt forces the FP32 SIMT kernel (used by the
+// tests to check both kernels against the oracle); anything else picks the
+// tensor-core kernel wherever it applies.
+bool force_simt() {
+    const char* e = std::getenv("KVM_SCORER");
+    return e && std::strcmp(e, "simt") == 0;
+}
+
+void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
+    if (force_simt()) return;
+    if (k->type != KVM_F16 && k->type != KVM_Q8_0 && k->type != KVM_Q4_0) return;
+    if (8 % d->kv_heads) return;
+    const uint64_t row_all = k->token_stride;  // bytes of one token across KV heads
+    // Every consumer warp needs an octet of one KV head in every chunk.
+    uint32_t tpc = std::max<uint32_t>(8, 64 / d->kv_heads);
+    while (tpc <= d->page_tokens && (d->page_tokens % tpc || (uint64_t(tpc) * row_all) % 16)) tpc <<= 1;
+    if (tpc > d->page_tokens || d->page_tokens % tpc) return;
+    while (tpc * 2 <= d->page_tokens && d->page_tokens % (tpc * 2) == 0 && uint64_t(tpc) * 2 * row_all <= 16384)
+        tpc <<= 1;
+    const uint64_t cb = uint64_t(tpc) * row_all;
+    if (cb > 65536) return;
+    cfg->mma = true;
+    cfg->mma_tpc = tpc;
+    cfg->mma_chunk_bytes = uint32_t(cb);
+    cfg->mma_chunks = d->page_tokens / tpc;
+    cfg->mma_stage_stride = uint32_t((cb + 16 + 127) / 128 * 128);
+    cfg->mma_stages = uint32_t(std::max<uint64_t>(2, std::min<uint64_t>(kMmaMaxStages, (110 * 1024) / cfg->mma_stage_stride)));
+    cfg->mma_smem = size_t(cfg->mma_stages) * cfg->mma_stage_stride + 2 * kMmaMaxStages * sizeof(uint64_t) +
+                    2 * 2 * kLseConsumerWarps * 8 * sizeof(float) + 16;
+}
 
 bool supported_type(int t) { return t >= KVM_F32 && t <= KVM_Q5_0; }
 
@@ -151,12 +187,22 @@ int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache
     cfg->stage_stride = uint32_t((cfg->chunk_bytes + 16 + 127) / 128 * 128);
     cfg->smem = size_t(kLseStages) * cfg->stage_stride + 2 * kLseStages * sizeof(uint64_t) +
                 2 * 2 * size_t(ng) * 8 * sizeof(float) + 16;
+    plan_mma(d, k, cfg);
     return KVM_OK;
 }
 
 size_t lse_bytes(const kvm_score_desc* d, uint32_t layers, uint32_t rows) {
     const uint64_t pages = (d->tokens + d->page_tokens - 1) / d->page_tokens;
     return align256(size_t(layers) * rows * d->q_heads * pages * sizeof(float));
+}
+
+int launch_lse_mma(kvm_ctx* c, int kt, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
+    switch (kt) {
+        case KVM_F16: return launch_lse_mma_kt<KVM_F16>(c, p, kk, smem, s);
+        case KVM_Q8_0: return launch_lse_mma_kt<KVM_Q8_0>(c, p, kk, smem, s);
+        case KVM_Q4_0: return launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s);
+        default: return KVM_ERR_UNSUPPORTED;
+    }
 }
 
 int launch_lse(kvm_ctx* c, int kt, const LseParams& p, int lpr, int vp, size_t smem, cudaStream_t s) {
@@ -208,10 +254,25 @@ int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const 
     p.lse = lse;
     p.status = c->status;
     p.stage_stride = cfg.stage_stride;
-    for (uint32_t v0 = 0; v0 < nvt; v0 += vp) {
-        p.v0 = v0;
-        p.nv = std::min<uint32_t>(vp, nvt - v0);
-        KVM_TRY(launch_lse(c, k->type, p, int(cfg.lpr), vp, cfg.smem, s));
+    if (cfg.mma) {
+        // Passes of up to 8 query vectors (the 16 rows of the mma's A tile hold
+        // their fp16 hi and lo parts).
+        p.chunk_bytes = cfg.mma_chunk_bytes;
+        p.chunks = cfg.mma_chunks;
+        p.tpc = cfg.mma_tpc;
+        p.stage_stride = cfg.mma_stage_stride;
+        p.stages = cfg.mma_stages;
+        for (uint32_t v0 = 0; v0 < nvt; v0 += 8) {
+            p.v0 = v0;
+            p.nv = std::min<uint32_t>(8, nvt - v0);
+            KVM_TRY(launch_lse_mma(c, k->type, p, int(d->head_dim / 32), cfg.mma_smem, s));
+        }
+    } else {
+        for (uint32_t v0 = 0; v0 < nvt; v0 += vp) {
+            p.v0 = v0;
+            p.nv = std::min<uint32_t>(vp, nvt - v0);
+            KVM_TRY(launch_lse(c, k->type, p, int(cfg.lpr), vp, cfg.smem, s));
+        }
     }
     const uint32_t heads_per = d->groups == 1 ? d->q_heads : G;
     const size_t nsmem = size_t(q->rows) * heads_per * sizeof(float2);

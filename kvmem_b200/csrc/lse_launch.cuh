@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "page_mass.cuh"
+#include "page_mass_mma.cuh"
 
 struct kvm_ctx {
     int device = 0;
@@ -75,6 +76,43 @@ int launch_lse_kt(kvm_ctx* c, const LseParams& p, int lpr, int vp, size_t smem, 
     }
 }
 
+template <int KT, int KK, bool MASK>
+int launch_lse_mma_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
+    auto fn = page_lse_mma_kernel<KT, KK, MASK>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLseThreads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return KVM_ERR_CUDA;
+    }
+    if (per_sm < 1) return KVM_ERR_UNSUPPORTED;
+    const uint32_t units = p.layers * p.pages;
+    const uint32_t grid = std::min<uint32_t>(units, uint32_t(c->num_sms * per_sm));
+    fn<<<grid, kLseThreads, smem, s>>>(p);
+    ++c->launches;
+    if (cudaGetLastError() != cudaSuccess) return KVM_ERR_CUDA;
+    return KVM_OK;
+}
+
+// Tensor-core scorer for fp16 / q8_0 / q4_0 keys; kk = head_dim / 32.
+template <int KT>
+int launch_lse_mma_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
+    if constexpr (KT == KVM_F16 || KT == KVM_Q8_0 || KT == KVM_Q4_0) {
+        const bool m = p.mask != nullptr;
+        switch (kk) {
+            case 2: return m ? launch_lse_mma_t<KT, 2, true>(c, p, smem, s) : launch_lse_mma_t<KT, 2, false>(c, p, smem, s);
+            case 4: return m ? launch_lse_mma_t<KT, 4, true>(c, p, smem, s) : launch_lse_mma_t<KT, 4, false>(c, p, smem, s);
+            case 8: return m ? launch_lse_mma_t<KT, 8, true>(c, p, smem, s) : launch_lse_mma_t<KT, 8, false>(c, p, smem, s);
+        }
+    }
+    return KVM_ERR_UNSUPPORTED;
+}
+
 // Instantiated once each in lse_<type>.cu.
 extern template int launch_lse_kt<KVM_F32>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
 extern template int launch_lse_kt<KVM_F16>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
@@ -82,5 +120,8 @@ extern template int launch_lse_kt<KVM_BF16>(kvm_ctx*, const LseParams&, int, int
 extern template int launch_lse_kt<KVM_Q8_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
 extern template int launch_lse_kt<KVM_Q4_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
 extern template int launch_lse_kt<KVM_Q5_0>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
+extern template int launch_lse_mma_kt<KVM_F16>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
+extern template int launch_lse_mma_kt<KVM_Q8_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
+extern template int launch_lse_mma_kt<KVM_Q4_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
 
 }  // namespace kvmb

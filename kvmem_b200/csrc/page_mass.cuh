@@ -54,6 +54,7 @@ struct LseParams {
     float* lse;             // [layers][rows][q_heads][pages], natural log
     DeviceStatus* status;
     uint32_t stage_stride;  // bytes per ring stage in shared memory
+    uint32_t stages;        // ring stages (tensor-core kernel; the SIMT kernel uses kLseStages)
 };
 
 // Decode the lane's 8 consecutive elements of one K row held in shared

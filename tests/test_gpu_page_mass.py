@@ -16,6 +16,13 @@ REL, ABS = 1e-3, 1e-6
 QT = {U.F32: torch.float32, U.F16: torch.float16, U.BF16: torch.bfloat16}
 
 
+@pytest.fixture(params=["auto", "simt"])
+def scorer(request, monkeypatch):
+    """Both page scorers: the tensor-core kernel (auto, where it applies) and the FP32 SIMT kernel."""
+    monkeypatch.setenv("KVM_SCORER", request.param)
+    return request.param
+
+
 def run_case(ctx, *, ktype, D, Hq, Hkv, R=1, L=2, page=64, T=1024, cap=None, groups=1, qtype=U.F32, softcap=0.0,
              mask=None, scale=0.0, seed=0):
     import kvmem_b200 as K
@@ -71,17 +78,21 @@ CASES = [
     dict(ktype=U.Q8_0, D=256, Hq=24, Hkv=4, page=256, T=768, groups=4, R=2),
     # softcap and explicit scale
     dict(ktype=U.F16, D=256, Hq=8, Hkv=4, page=64, T=512, softcap=30.0, scale=0.25),
+    # f16 queries (no lo part), MQA (one KV head), large query magnitudes (prescale)
+    dict(ktype=U.F16, D=64, Hq=8, Hkv=1, page=64, T=512, qtype=U.F16),
+    dict(ktype=U.Q4_0, D=256, Hq=24, Hkv=4, page=256, T=768, qtype=U.BF16),
+    dict(ktype=U.Q8_0, D=128, Hq=40, Hkv=8, R=2, page=128, T=512),
 ]
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(f"{k}{v}" for k, v in c.items()))
-def test_page_mass_matches_oracle(ctx, case):
+def test_page_mass_matches_oracle(ctx, scorer, case):
     got, exp = run_case(ctx, **case)
     # each (layer, group, row) distribution sums to 1
     np.testing.assert_allclose(got.sum(axis=-1), 1.0, atol=2e-5)
 
 
-def test_mask_hides_tokens_and_empty_rows_are_nan(ctx):
+def test_mask_hides_tokens_and_empty_rows_are_nan(ctx, scorer):
     R, T = 3, 512
     mask = np.zeros((R, T), np.float32)
     mask[0, 100:300] = -np.inf
@@ -134,7 +145,7 @@ def test_unsupported_layouts_are_rejected(ctx):
     assert e.value.code == K._abi.ERR_INVALID_ARGUMENT
 
 
-def test_attention_cuda_mirror_matches_oracle():
+def test_attention_cuda_mirror_matches_oracle(scorer):
     """The llama_kvmem_attention_cuda mirror: ggml-style views, sampled rows, mask rows."""
     import kvmem_b200 as K
     rng = np.random.default_rng(9)
