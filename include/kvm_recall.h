@@ -141,6 +141,27 @@ size_t kvm_ctx_device_bytes(const kvm_ctx* ctx);
 int kvm_score_pages(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
                     float* mass_rows, float* mass_mean, void* stream);
 
+/* Page mass without allocating device memory. This entry point has no
+ * counterpart in the reference. It computes exactly what kvm_score_pages
+ * computes, but needs no context: its scratch (a status word and the page
+ * log-sum-exp buffer) is a fixed 8 MiB array that the CUDA driver reserves on
+ * each GPU that loads this library and keeps until the process exits. It is
+ * meant for callers that must not call cudaMalloc while they score, such as an
+ * engine whose device memory is all handed out up front by its own pool, or a
+ * plugin host that forbids new device allocations after start-up.
+ *  - Runs on the current device. The first call on a device looks up the
+ *    array's device address; make that first call before any stream capture.
+ *  - Needs layers * rows * q_heads * pages * 4 bytes (rounded up to 256) of
+ *    scratch, at most 8 MiB - 256 B; larger problems return KVM_ERR_LENGTH
+ *    before any launch.
+ *  - Every call uses the same array; the status word is cleared on each call,
+ *    the rest is fully rewritten. Calls that overlap on the GPU (two streams,
+ *    two threads) race on it: order them on one stream.
+ *  - A bounded device wait that runs out leaves the outputs undefined; this
+ *    variant has no status read-back. */
+int kvm_score_pages_noalloc(const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                            float* mass_rows, float* mass_mean, void* stream);
+
 /* ------------------------------------------------------------------ top-k */
 
 /* Budgeted top-k with keep pages, one selection per score row. Replaces

@@ -94,6 +94,7 @@ SIGNATURES = {
     "kvm_ctx_bind_workspace": ([_vp, _vp, C.c_size_t], _i),
     "kvm_ctx_device_bytes": ([_vp], C.c_size_t),
     "kvm_score_pages": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _vp, _vp, _vp], _i),
+    "kvm_score_pages_noalloc": ([C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _vp, _vp, _vp], _i),
     "kvm_select_topk": ([_vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _i, _vp, _vp, _u32, _vp],
                         _i),
     "kvm_pool_create": ([_vp, _u32, _u32, _u32, C.POINTER(C.c_void_p)], _i),

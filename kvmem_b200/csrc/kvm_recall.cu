@@ -731,3 +731,63 @@ int kvm_recall_step(kvm_ctx* c, const kvm_step_desc* st, kvm_pool* pool, const k
 }
 
 }  // extern "C"
+
+// ------------------------------------------------- scoring without device allocation
+//
+// kvm_score_pages needs a page log-sum-exp buffer that the context allocates
+// (or that the caller binds). kvm_score_pages_noalloc below is the same
+// computation for callers that cannot allocate device memory when they score:
+// its scratch is this fixed array, which the CUDA driver reserves on every GPU
+// that loads the library and keeps until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 256 B status word + page LSE buffer
+constexpr size_t kNoAllocStatusBytes = 256;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_base[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+// The host symbol is only a stand-in; the address is looked up once per device.
+int noalloc_scratch(int device, void** base) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_base[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            return KVM_ERR_CUDA;
+        }
+        g_noalloc_base[device] = p;
+    }
+    *base = g_noalloc_base[device];
+    return KVM_OK;
+}
+
+}  // namespace
+
+extern "C" int kvm_score_pages_noalloc(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k,
+                                       float* mass_rows, float* mass_mean, void* stream) {
+    LseConfig cfg;
+    KVM_TRY(validate_score(d, q, k, &cfg));
+    if (kNoAllocStatusBytes + lse_bytes(d, d->layers, q->rows) > kNoAllocScratchBytes) return KVM_ERR_LENGTH;
+    int device = -1;
+    KVM_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kNoAllocMaxDevices) return KVM_ERR_UNSUPPORTED;
+    void* base = nullptr;
+    KVM_TRY(noalloc_scratch(device, &base));
+    auto s = static_cast<cudaStream_t>(stream);
+    // A context on the stack: it carries the device, SM count and the status
+    // word (inside the fixed scratch); it owns no memory.
+    kvm_ctx c;
+    c.device = device;
+    KVM_CUDA(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
+    c.status = static_cast<DeviceStatus*>(base);
+    KVM_CUDA(cudaMemsetAsync(base, 0, sizeof(DeviceStatus), s));
+    return score_layers(&c, d, q, k, cfg, 0, d->layers,
+                        reinterpret_cast<float*>(static_cast<uint8_t*>(base) + kNoAllocStatusBytes), mass_rows,
+                        mass_mean, s);
+}
