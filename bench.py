@@ -201,11 +201,13 @@ def run_kernel_only(args, w, local):
         ctx.score_pages(desc, qd, kc, want_rows=False, out_mean=mass)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     ev0.record()
     for _ in range(args.steps):
         ctx.score_pages(desc, qd, kc, want_rows=False, out_mean=mass)
     ev1.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     ctx.check_status("kernel-only")
     ms = ev0.elapsed_time(ev1) / args.steps
     kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
@@ -263,11 +265,13 @@ def run_ours(args, world, rank, local):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
         ev1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     launches = ctx.launches - a0
     ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
     ctx.check_status("timed steps")
