@@ -153,14 +153,18 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_kernel(const LseParam
     }
     __syncthreads();
 
+    // Each CTA scores a contiguous range of (layer, page) units, so the query
+    // registers are reloaded only when its range crosses a layer.
     const uint32_t units = P.layers * P.pages;
+    const uint32_t per_cta = (units + gridDim.x - 1) / gridDim.x;
+    const uint32_t unit_begin = min(units, blockIdx.x * per_cta), unit_end = min(units, unit_begin + per_cta);
 
     if (warp == NW) {
         // Producer warp: one elected lane streams page chunks into the ring.
         if (lane == 0) {
             const uint64_t policy = policy_evict_first();
             uint32_t it = 0, issued = 0;  // issued chunks form a prefix of the sequence
-            for (uint32_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
+            for (uint32_t unit = unit_begin; unit < unit_end; ++unit) {
                 const uint32_t l = unit / P.pages, p = unit % P.pages;
                 const uint8_t* src = P.k + l * P.k_layer + uint64_t(p) * P.page_bytes;
                 for (uint32_t c = 0; c < P.chunks; ++c, ++it) {
@@ -206,10 +210,12 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_kernel(const LseParam
     const float scale_l2 = P.scale * kLog2e;
 
     float qv[VP][8];
-    uint32_t it = 0, ucount = 0;
-    for (uint32_t unit = blockIdx.x; unit < units; unit += gridDim.x, ++ucount) {
+    uint32_t it = 0, ucount = 0, qlayer = 0xffffffffu;
+    for (uint32_t unit = unit_begin; unit < unit_end; ++unit, ++ucount) {
         const uint32_t l = unit / P.pages, p = unit % P.pages;
         // Query vectors of this KV head for layer l, as f32 registers.
+        if (l != qlayer) {
+        qlayer = l;
 #pragma unroll
         for (int v = 0; v < VP; ++v) {
             const uint32_t vg = P.v0 + v;
@@ -219,6 +225,7 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_kernel(const LseParam
 #pragma unroll
             for (int i = 0; i < 8; ++i)
                 qv[v][i] = ok ? load_scalar(qp + (lig * 8 + i) * type_bytes(P.q_type), P.q_type) : 0.f;
+        }
         }
         // Row of this lane's query vector; lanes that own a padding vector
         // (myv >= nv) read row 0 so their mask reads stay in bounds.

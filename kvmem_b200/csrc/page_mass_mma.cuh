@@ -118,13 +118,17 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
         mbar_fence_init();
     }
     __syncthreads();
+    // Each CTA scores a contiguous range of (layer, page) units, so the query
+    // registers are reloaded only when its range crosses a layer.
     const uint32_t units = P.layers * P.pages;
+    const uint32_t per_cta = (units + gridDim.x - 1) / gridDim.x;
+    const uint32_t unit_begin = min(units, blockIdx.x * per_cta), unit_end = min(units, unit_begin + per_cta);
 
     if (warp == NW) {
         if (lane == 0) {
             const uint64_t policy = policy_evict_first();
             uint32_t it = 0, issued = 0;
-            for (uint32_t unit = blockIdx.x; unit < units; unit += gridDim.x) {
+            for (uint32_t unit = unit_begin; unit < unit_end; ++unit) {
                 const uint32_t l = unit / P.pages, p = unit % P.pages;
                 const uint8_t* src = P.k + l * P.k_layer + uint64_t(p) * P.page_bytes;
                 for (uint32_t c = 0; c < P.chunks; ++c, ++it) {
@@ -160,10 +164,11 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
 
     uint32_t qa[KK][2][4];  // A fragments: [chunk][k-step][a0..a3]
     float qinv = 1.f;       // 2^-shift of this lane's vector prescale
-    uint32_t it = 0, ucount = 0;
-    for (uint32_t unit = blockIdx.x; unit < units; unit += gridDim.x, ++ucount) {
+    uint32_t it = 0, ucount = 0, qlayer = 0xffffffffu;
+    for (uint32_t unit = unit_begin; unit < unit_end; ++unit, ++ucount) {
         const uint32_t l = unit / P.pages, p = unit % P.pages;
-        {
+        if (l != qlayer) {
+            qlayer = l;
             // Query vector g of this KV head (8 dims per chunk), prescaled by 2^shift.
             float qv[KK][8];
             float amax = 0.f;
