@@ -288,6 +288,43 @@ typedef struct kvm_step_desc {
 int kvm_recall_step(kvm_ctx* ctx, const kvm_step_desc* step, kvm_pool* pool, const kvm_stage_layout* layout,
                     float* mass_mean, uint32_t* sel_ids, uint32_t* sel_n, void* stream);
 
+/* --------------------------------------------------- page-range sharding */
+
+/* One history partitioned by contiguous page ranges over several GPUs (the
+ * reference has no multi-GPU selection): each rank scores its range and two
+ * all-gathers merge. Per decode step, on every rank:
+ *   1. kvm_shard_score_partial: page LSE of the rank's pages [page0, page0 +
+ *      local_pages) (k: that range's K, dense as in kvm_kcache; desc->tokens is
+ *      the GLOBAL visible token count) into the context workspace, and its
+ *      softmax statistics stats[layers][rows][q_heads] = {max, sum exp(lse-max)}
+ *      (device f32 pairs). All-gather stats over the ranks (rank order).
+ *   2. kvm_shard_merge_stats: gathered [ranks][count] pairs -> global
+ *      [count] {max, 1/sum}.
+ *   3. kvm_shard_score_finish: local page masses normalised by the global
+ *      statistics (outputs as kvm_score_pages, over local_pages). Nothing else
+ *      may score on the context between steps 1 and 3 (the LSE stays in its
+ *      workspace); KVM_ERR_STALE when no partial pass left one.
+ *   4. kvm_shard_candidates: per score row the top-k local pages that are not
+ *      keep pages (keep = GLOBAL page ids), as (score, global id) in
+ *      cand_scores / cand_ids [nrows][k], padded with (-inf, 0xffffffff).
+ *      All-gather both over the ranks.
+ *   5. kvm_shard_merge: gathered [ranks][nrows][k] candidates -> per row the
+ *      (budget - keeps) best by (score desc, id desc) plus the keep pages,
+ *      ascending ids (out_ids [nrows][out_stride], out_n [nrows]): the same set
+ *      as kvm_select_topk over the whole row when k >= budget - keeps. */
+int kvm_shard_score_partial(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                            uint32_t page0, uint32_t local_pages, float* stats, void* stream);
+int kvm_shard_merge_stats(kvm_ctx* ctx, const float* gathered, uint32_t ranks, uint32_t count, float* global_stats,
+                          void* stream);
+int kvm_shard_score_finish(kvm_ctx* ctx, const kvm_score_desc* desc, uint32_t rows, uint32_t local_pages,
+                           const float* global_stats, float* mass_rows, float* mass_mean, void* stream);
+int kvm_shard_candidates(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint32_t local_pages, uint32_t score_stride,
+                         uint32_t page0, const uint32_t* keep, uint32_t nkeep, uint32_t k, float* cand_scores,
+                         uint32_t* cand_ids, void* stream);
+int kvm_shard_merge(kvm_ctx* ctx, const float* cand_scores, const uint32_t* cand_ids, uint32_t ranks, uint32_t nrows,
+                    uint32_t k, const uint32_t* keep, uint32_t nkeep, uint32_t budget, uint32_t* out_ids,
+                    uint32_t* out_n, uint32_t out_stride, void* stream);
+
 /* Bytes of one D-element row of `type` (0 for an unknown type). */
 uint64_t kvm_row_bytes(int type, uint32_t dim);
 

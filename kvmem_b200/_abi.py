@@ -108,6 +108,14 @@ SIGNATURES = {
     "kvm_meank_score": ([_vp, _vp, _vp, _vp, C.POINTER(C.c_uint32), _u32, _u32, _u32, _u32, _u32, _u32,
                          C.POINTER(C.c_uint8), _i, C.c_float, _vp, _vp], _i),
     "kvm_recall_step": ([_vp, C.POINTER(StepDesc), _vp, C.POINTER(StageLayout), _vp, _vp, _vp, _vp], _i),
+    "kvm_shard_score_partial": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _u32, _u32, _vp,
+                                 _vp], _i),
+    "kvm_shard_merge_stats": ([_vp, _vp, _u32, _u32, _vp, _vp], _i),
+    "kvm_shard_score_finish": ([_vp, C.POINTER(ScoreDesc), _u32, _u32, _vp, _vp, _vp, _vp], _i),
+    "kvm_shard_candidates": ([_vp, _vp, _u32, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _vp, _vp, _vp],
+                             _i),
+    "kvm_shard_merge": ([_vp, _vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _vp, _vp, _u32, _vp],
+                        _i),
     "kvm_row_bytes": ([_i, _u32], _u64),
     "kvm_ctx_launches": ([_vp], _u64),
 }

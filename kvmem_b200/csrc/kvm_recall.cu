@@ -13,6 +13,7 @@
 #include "meank.cuh"
 #include "page_norm.cuh"
 #include "select.cuh"
+#include "shard.cuh"
 #include "stagein.cuh"
 
 using namespace kvmb;
@@ -216,11 +217,11 @@ int launch_lse(kvm_ctx* c, int kt, const LseParams& p, int lpr, int vp, size_t s
     }
 }
 
-// Scores layers [l0, l0+nl) into mass rows / means whose layer index starts at
-// l0 (absolute), using `lse` ([nl][rows][Hq][pages]) as scratch.
-int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, const LseConfig& cfg,
-                 uint32_t l0, uint32_t nl, float* lse, float* mass_rows, float* mass_mean, cudaStream_t s) {
-    const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
+// Page LSE of layers [l0, l0+nl) into `lse` ([nl][rows][Hq][pages]); token t
+// takes part iff t < visible (pages and visible are the caller's: the whole
+// history for kvm_score_pages, one rank's page range for sharded scoring).
+int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, const LseConfig& cfg,
+               uint32_t l0, uint32_t nl, uint32_t pages, uint64_t visible, float* lse, cudaStream_t s) {
     const uint32_t G = d->q_heads / d->kv_heads;
     const uint32_t nvt = q->rows * G;
     int vp = 1;
@@ -237,7 +238,7 @@ int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const 
     p.pages = pages;
     p.layers = nl;
     p.page_tokens = d->page_tokens;
-    p.tokens = d->tokens;
+    p.tokens = visible;
     p.q = static_cast<const uint8_t*>(q->data) + uint64_t(l0) * q->layer_stride;
     p.q_type = q->type;
     p.rows = q->rows;
@@ -274,18 +275,35 @@ int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const 
             KVM_TRY(launch_lse(c, k->type, p, int(cfg.lpr), vp, cfg.smem, s));
         }
     }
+    return KVM_OK;
+}
+
+// Softmax over pages and the head / row means of layers [l0, l0+nl), with the
+// statistics computed here or (`given`, sharded scoring) supplied.
+int normalize_layers(kvm_ctx* c, const kvm_score_desc* d, uint32_t rows, uint32_t l0, uint32_t nl, uint32_t pages,
+                     const float* lse, const float2* given, float* mass_rows, float* mass_mean, cudaStream_t s) {
+    const uint32_t G = d->q_heads / d->kv_heads;
     const uint32_t heads_per = d->groups == 1 ? d->q_heads : G;
-    const size_t nsmem = size_t(q->rows) * heads_per * sizeof(float2);
+    const size_t nsmem = size_t(rows) * heads_per * sizeof(float2);
     if (nsmem > 200 * 1024) return KVM_ERR_LENGTH;
     static std::once_flag once;
     std::call_once(once, [] {
         cudaFuncSetAttribute(page_mass_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     });
-    page_mass_normalize_kernel<<<nl * d->groups, 256, nsmem, s>>>(lse, q->rows, d->q_heads, G, d->groups, pages,
-                                                                 mass_rows, mass_mean, l0);
+    page_mass_normalize_kernel<<<nl * d->groups, 256, nsmem, s>>>(lse, rows, d->q_heads, G, d->groups, pages,
+                                                                 mass_rows, mass_mean, l0, given);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
     return KVM_OK;
+}
+
+// Scores layers [l0, l0+nl) into mass rows / means whose layer index starts at
+// l0 (absolute), using `lse` ([nl][rows][Hq][pages]) as scratch.
+int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, const LseConfig& cfg,
+                 uint32_t l0, uint32_t nl, float* lse, float* mass_rows, float* mass_mean, cudaStream_t s) {
+    const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
+    KVM_TRY(lse_layers(c, d, q, k, cfg, l0, nl, pages, d->tokens, lse, s));
+    return normalize_layers(c, d, q->rows, l0, nl, pages, lse, nullptr, mass_rows, mass_mean, s);
 }
 
 int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
@@ -791,3 +809,116 @@ extern "C" int kvm_score_pages_noalloc(const kvm_score_desc* d, const kvm_query*
                         reinterpret_cast<float*>(static_cast<uint8_t*>(base) + kNoAllocStatusBytes), mass_rows,
                         mass_mean, s);
 }
+
+// ------------------------------------------------------------- page-range sharding
+namespace {
+
+// Copies the keep list without duplicates into `out` (validation of range is the caller's).
+std::vector<uint32_t> distinct(const uint32_t* keep, uint32_t nkeep) {
+    std::vector<uint32_t> v(keep, keep + nkeep);
+    std::sort(v.begin(), v.end());
+    v.erase(std::unique(v.begin(), v.end()), v.end());
+    return v;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kvm_shard_score_partial(kvm_ctx* c, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                            uint32_t page0, uint32_t local_pages, float* stats, void* stream) {
+    if (!c || !desc || !q || !stats || !local_pages) return KVM_ERR_INVALID_ARGUMENT;
+    // Validate and plan with the local slice; visibility follows the global token count.
+    kvm_score_desc local = *desc;
+    local.tokens = uint64_t(local_pages) * desc->page_tokens;
+    LseConfig cfg;
+    KVM_TRY(validate_score(&local, q, k, &cfg));
+    const uint64_t first = uint64_t(page0) * desc->page_tokens;
+    const uint64_t visible = desc->tokens > first ? std::min<uint64_t>(desc->tokens - first, local.tokens) : 0;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_TRY(ensure_ws(c, lse_bytes(&local, local.layers, q->rows)));
+    float* lse = static_cast<float*>(c->ws);
+    KVM_TRY(lse_layers(c, &local, q, k, cfg, 0, local.layers, local_pages, visible, lse, s));
+    const uint32_t nrows = local.layers * q->rows * local.q_heads;
+    lse_stats_kernel<<<(nrows + 7) / 8, 256, 0, s>>>(lse, nrows, local_pages, reinterpret_cast<float2*>(stats));
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_shard_merge_stats(kvm_ctx* c, const float* gathered, uint32_t ranks, uint32_t count, float* global_stats,
+                          void* stream) {
+    if (!c || !gathered || !global_stats || !ranks || !count) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    stats_merge_kernel<<<(count + 255) / 256, 256, 0, s>>>(reinterpret_cast<const float2*>(gathered), ranks, count,
+                                                          reinterpret_cast<float2*>(global_stats));
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_shard_score_finish(kvm_ctx* c, const kvm_score_desc* desc, uint32_t rows, uint32_t local_pages,
+                           const float* global_stats, float* mass_rows, float* mass_mean, void* stream) {
+    if (!c || !desc || !global_stats || !rows || !local_pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (desc->groups != 1 && desc->groups != desc->kv_heads) return KVM_ERR_INVALID_ARGUMENT;
+    kvm_score_desc local = *desc;
+    local.tokens = uint64_t(local_pages) * desc->page_tokens;
+    if (lse_bytes(&local, local.layers, rows) > c->ws_bytes) return KVM_ERR_STALE;  // no partial pass ran
+    DeviceGuard guard(c->device);
+    return normalize_layers(c, &local, rows, 0, local.layers, local_pages, static_cast<const float*>(c->ws),
+                            reinterpret_cast<const float2*>(global_stats), mass_rows, mass_mean,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int kvm_shard_candidates(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t local_pages, uint32_t score_stride,
+                         uint32_t page0, const uint32_t* keep, uint32_t nkeep, uint32_t k, float* cand_scores,
+                         uint32_t* cand_ids, void* stream) {
+    if (!c || !scores || !nrows || !local_pages || !k || !cand_scores || !cand_ids || (nkeep && !keep))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (local_pages > 196608 || score_stride < local_pages) return KVM_ERR_LENGTH;
+    const auto kd = distinct(keep, nkeep);
+    DeviceGuard guard(c->device);
+    KVM_TRY(upload_keep(c, kd.data(), uint32_t(kd.size())));
+    auto s = static_cast<cudaStream_t>(stream);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(shard_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    shard_candidates_kernel<<<nrows, kSelectThreads, local_pages, s>>>(
+        scores, local_pages, score_stride, page0, static_cast<const uint32_t*>(c->small), uint32_t(kd.size()), k,
+        cand_scores, cand_ids, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_shard_merge(kvm_ctx* c, const float* cand_scores, const uint32_t* cand_ids, uint32_t ranks, uint32_t nrows,
+                    uint32_t k, const uint32_t* keep, uint32_t nkeep, uint32_t budget, uint32_t* out_ids,
+                    uint32_t* out_n, uint32_t out_stride, void* stream) {
+    if (!c || !cand_scores || !cand_ids || !ranks || !nrows || !k || !budget || !out_ids || !out_n ||
+        (nkeep && !keep))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (uint64_t(ranks) * k > kMergeMax) return KVM_ERR_LENGTH;
+    const auto kd = distinct(keep, nkeep);
+    if (kd.size() > budget) return KVM_ERR_BUDGET_EXCEEDED;
+    if (out_stride < budget) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    KVM_TRY(upload_keep(c, kd.data(), uint32_t(kd.size())));
+    auto s = static_cast<cudaStream_t>(stream);
+    const size_t smem = size_t(ranks) * k * 8 + (size_t(budget) + kd.size()) * 4;
+    if (smem > 200 * 1024) return KVM_ERR_LENGTH;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    shard_merge_kernel<<<nrows, kSelectThreads, smem, s>>>(cand_scores, cand_ids, ranks, k, nrows,
+                                                            static_cast<const uint32_t*>(c->small),
+                                                            uint32_t(kd.size()), budget, out_ids, out_n, out_stride);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+}  // extern "C"

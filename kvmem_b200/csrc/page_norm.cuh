@@ -10,10 +10,12 @@ namespace kvmb {
 // (src/adapter/llama-kvmem-attention-cuda.cu:98-121): max, 1/sum(exp(lse-max)),
 // then sum_h exp(lse-max)*inv / heads. A (row, head) whose pages are all
 // empty has max = -inf and yields NaN, as the reference's normaliser does.
+// With `given` (sharded scoring) the statistics are not computed but read:
+// given[(l*rows + r)*q_heads + h] = (global max, 1/global sum).
 __global__ void __launch_bounds__(256) page_mass_normalize_kernel(const float* lse, uint32_t rows, uint32_t q_heads,
                                                                   uint32_t group, uint32_t groups, uint32_t pages,
                                                                   float* mass_rows, float* mass_mean,
-                                                                  uint32_t out_layer0) {
+                                                                  uint32_t out_layer0, const float2* given) {
     extern __shared__ float2 stats[];  // [rows * heads_per]
     const uint32_t l = blockIdx.x / groups, g = blockIdx.x % groups;
     const uint32_t heads_per = groups == 1 ? q_heads : group;
@@ -22,6 +24,10 @@ __global__ void __launch_bounds__(256) page_mass_normalize_kernel(const float* l
     const uint32_t nrow = rows * heads_per;
     for (uint32_t idx = warp; idx < nrow; idx += 8) {
         const uint32_t r = idx / heads_per, h = h0 + idx % heads_per;
+        if (given) {
+            if (lane == 0) stats[idx] = given[(uint64_t(l) * rows + r) * q_heads + h];
+            continue;
+        }
         const float* row = lse + ((uint64_t(l) * rows + r) * q_heads + h) * pages;
         float M = -INFINITY;
         for (uint32_t p = lane; p < pages; p += 32) M = fmaxf(M, row[p]);
