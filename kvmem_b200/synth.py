@@ -51,6 +51,7 @@ CONFIGS = {
     "c1": Workload("c1_cpu16k", 4, 32, 8, 128, 16384, 64, 16, 8, groups=8),
     "c2": Workload("c2_fp16_128k", 64, 24, 4, 256, 131072, 256, 32, 32),
     "c3": Workload("c3_q8k_q4v_256k", 64, 24, 4, 256, 262144, 256, 64, 32, k_type=3, v_type=4),
+    "c5": Workload("c5_q8k_sharded_1m", 64, 24, 4, 256, 1048576, 256, 128, 128, k_type=3, v_type=4),
 }
 
 
