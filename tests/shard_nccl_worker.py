@@ -35,7 +35,7 @@ def main(out_dir):
         kb = U.make_k(rng, U.F16, L, P * B, Hkv, D, needle_pages=needles, page=B, q_dir=qdir / np.sqrt(D))
         dev = torch.device("cuda", local)
         p0, p1 = page_ranges(P, world)[rank]
-                k_local = torch.from_numpy(np.ascontiguousarray(kb[:, p0 * B:p1 * B]).reshape(-1)).to(dev)
+        k_local = torch.from_numpy(np.ascontiguousarray(kb[:, p0 * B:p1 * B]).reshape(-1)).to(dev)
         q_d = torch.from_numpy(qb.reshape(-1).copy()).to(dev).view(torch.float32).view(L, 1, Hq, D)
         desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=B)
         q = K.RecallContext.make_query(q_d, 1)

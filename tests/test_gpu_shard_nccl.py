@@ -23,7 +23,9 @@ def test_two_rank_nccl_sharded_selection(tmp_path):
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",
            os.path.join(HERE, "shard_nccl_worker.py"), str(tmp_path)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    if r.returncode != 0:
+        lines = [x for x in (r.stdout + r.stderr).splitlines() if "rank" in x or "Error" in x or "error" in x]
+        raise AssertionError("torchrun workers failed:\n" + "\n".join(lines[:80]))
     res = [json.load(open(tmp_path / f"rank{i}.json")) for i in range(2)]
     assert res[0]["status"] == 0 and res[1]["status"] == 0
     assert res[0]["ids"] == res[1]["ids"] == res[0]["unsharded"]
