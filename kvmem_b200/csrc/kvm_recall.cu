@@ -107,7 +107,7 @@ struct LseConfig {
     size_t smem = 0;
     // Tensor-core scorer (fp16 / q8_0 / q4_0 keys, 1/2/4/8 KV heads), when usable.
     bool mma = false;
-    uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0;
+    uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0, mma_slot = 0;
     size_t mma_smem = 0;
 };
 
@@ -132,11 +132,21 @@ void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
         tpc <<= 1;
     const uint64_t cb = uint64_t(tpc) * row_all;
     if (cb > 65536) return;
+    // Quantised keys: one shared-memory slot per token, its stride 16 bytes past a
+    // multiple of 128 so the 8 tokens of an octet start in different bank groups.
+    uint64_t slot = row_all;
+    if (k->type != KVM_F16) {
+        if (row_all % 16) return;  // per-token bulk copies need 16-byte multiples
+        slot = (row_all + 127) / 128 * 128 + 16;
+        if (slot - 128 >= row_all) slot -= 128;
+    }
+    const uint64_t stage_bytes = k->type != KVM_F16 ? uint64_t(tpc) * slot : cb;
     cfg->mma = true;
     cfg->mma_tpc = tpc;
     cfg->mma_chunk_bytes = uint32_t(cb);
     cfg->mma_chunks = d->page_tokens / tpc;
-    cfg->mma_stage_stride = uint32_t((cb + 16 + 127) / 128 * 128);
+    cfg->mma_slot = uint32_t(slot);
+    cfg->mma_stage_stride = uint32_t((stage_bytes + 16 + 127) / 128 * 128);
     cfg->mma_stages = uint32_t(std::max<uint64_t>(2, std::min<uint64_t>(kMmaMaxStages, (110 * 1024) / cfg->mma_stage_stride)));
     cfg->mma_smem = size_t(cfg->mma_stages) * cfg->mma_stage_stride + 2 * kMmaMaxStages * sizeof(uint64_t) +
                     2 * 2 * kLseConsumerWarps * 8 * sizeof(float) + 16;
@@ -263,6 +273,8 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
         p.tpc = cfg.mma_tpc;
         p.stage_stride = cfg.mma_stage_stride;
         p.stages = cfg.mma_stages;
+        p.row_set = uint32_t(k->token_stride);
+        p.slot_stride = cfg.mma_slot;
         for (uint32_t v0 = 0; v0 < nvt; v0 += 8) {
             p.v0 = v0;
             p.nv = std::min<uint32_t>(8, nvt - v0);

@@ -55,6 +55,8 @@ struct LseParams {
     DeviceStatus* status;
     uint32_t stage_stride;  // bytes per ring stage in shared memory
     uint32_t stages;        // ring stages (tensor-core kernel; the SIMT kernel uses kLseStages)
+    uint32_t row_set;       // bytes of one token across KV heads (kv_heads * row_bytes)
+    uint32_t slot_stride;   // tensor-core kernel, quantised keys: padded shared-memory stride per token
 };
 
 // Decode the lane's 8 consecutive elements of one K row held in shared

@@ -16,16 +16,32 @@
 //    mma's k = 2c+j and 2c+8+j map to dims kk*32 + 8c + 4s + j and + 2 + j.
 //  * q8_0 / q4_0 codes are exact in fp16; each 32-dim block is one chunk, its
 //    partial dots are scaled by the token's block scale in fp32 and summed.
+//    For these keys lane c takes codes 4c..4c+3 and 16+4c..16+4c+3 of a block
+//    (two 32-bit words of q8_0 codes, one word of q4_0 nibbles) and the producer
+//    copies every token into its own shared-memory slot whose stride is 16
+//    bytes past a multiple of 128: the 8 tokens of an octet then start in 8
+//    different bank groups and every quantised load is conflict-free.
 //  * the K pages stream into shared memory through the same bulk-TMA mbarrier
 //    ring as the SIMT kernel; each consumer warp owns octets of 8 tokens of
 //    one KV head, keeps an online (max, sum) per (vector, token pair) and the
 //    lanes / warps that share a vector are merged at the end of the page.
 #pragma once
+#include <type_traits>
+
 #include "page_mass.cuh"
 
 namespace kvmb {
 
 constexpr int kMmaMaxStages = 8;
+
+// Calls f(std::integral_constant<int, kk>) for kk = 0 .. N-1 (compile-time chunk index).
+template <int N, int I = 0, class F>
+__device__ __forceinline__ void unroll_kk(F&& f) {
+    if constexpr (I < N) {
+        f(std::integral_constant<int, I>{});
+        unroll_kk<N, I + 1>(f);
+    }
+}
 
 __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -60,30 +76,36 @@ __device__ __forceinline__ void u4x4_to_h2(uint32_t x, uint16_t offset_bits, uin
 }
 
 // B fragments of one 32-dim chunk for this lane (token row `row`, lane part c):
-// b[0..1] for k-step 0, b[2..3] for k-step 1. Returns the block scale for
-// quantised keys (the scale of this lane's own token; callers fetch the
-// scales of their C tokens separately).
-template <int KT>
-__device__ __forceinline__ void load_b_chunk(const uint8_t* row, int kk, int c, uint32_t* b) {
+// b[0..1] for k-step 0, b[2..3] for k-step 1.
+//  fp16: dims 8c..8c+7 of the chunk, one 16-byte load.
+//  q8_0 / q4_0: codes 4c..4c+3 (k-step 0) and 16+4c..16+4c+3 (k-step 1) of block kk.
+template <int KT, int KK_INDEX>
+__device__ __forceinline__ void load_b_chunk(const uint8_t* row, int c, uint32_t* b) {
+    constexpr int kk = KK_INDEX;
     if constexpr (KT == KVM_F16) {
         const uint4 w = *reinterpret_cast<const uint4*>(row + kk * 64 + c * 16);
         b[0] = w.x; b[1] = w.y; b[2] = w.z; b[3] = w.w;
     } else {
         constexpr int kBlock = KT == KVM_Q8_0 ? 34 : 18;
-        const uint8_t* blk = row + kBlock * kk;
-        const uint8_t* src = KT == KVM_Q8_0 ? blk + 2 + 8 * c : blk + 2 + 8 * (c & 1);
-        const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
-        const uint32_t* base = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
-        const uint32_t sh = uint32_t(addr & 3) * 8;
-        const uint32_t w0 = base[0], w1 = base[1], w2 = base[2];
-        const uint32_t lo = __funnelshift_r(w0, w1, sh), hi = __funnelshift_r(w1, w2, sh);
-        if constexpr (KT == KVM_Q8_0) {
-            s8x4_to_h2(lo, b[0], b[1]);
-            s8x4_to_h2(hi, b[2], b[3]);
+        // Rows start 4-byte aligned; a block's codes start 2 + 34kk (18kk) bytes in,
+        // so the lane's words are aligned exactly when kk is odd.
+        constexpr bool aligned = (kBlock * kk + 2) % 4 == 0;
+        const uint8_t* src = row + kBlock * kk + 2 + 4 * c;
+        uint32_t w0, w1 = 0;
+        if constexpr (aligned) {
+            w0 = *reinterpret_cast<const uint32_t*>(src);
+            if constexpr (KT == KVM_Q8_0) w1 = *reinterpret_cast<const uint32_t*>(src + 16);
         } else {
-            const uint32_t shift = 4 * (c >> 1);
-            u4x4_to_h2((lo >> shift) & 0x0F0F0F0Fu, 0x6408 /* 1032 */, b[0], b[1]);
-            u4x4_to_h2((hi >> shift) & 0x0F0F0F0Fu, 0x6408, b[2], b[3]);
+            const uint32_t* a = reinterpret_cast<const uint32_t*>(src - 2);
+            w0 = __funnelshift_r(a[0], a[1], 16);
+            if constexpr (KT == KVM_Q8_0) w1 = __funnelshift_r(a[4], a[5], 16);
+        }
+        if constexpr (KT == KVM_Q8_0) {
+            s8x4_to_h2(w0, b[0], b[1]);
+            s8x4_to_h2(w1, b[2], b[3]);
+        } else {
+            u4x4_to_h2(w0 & 0x0F0F0F0Fu, 0x6408 /* 1032 */, b[0], b[1]);
+            u4x4_to_h2((w0 >> 4) & 0x0F0F0F0Fu, 0x6408, b[2], b[3]);
         }
     }
 }
@@ -140,8 +162,16 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
                         continue;
                     }
                     mbar_arrive_expect_tx(&full[s], P.chunk_bytes);
-                    bulk_g2s(stages + s * P.stage_stride, src + uint64_t(c) * P.chunk_bytes, P.chunk_bytes, &full[s],
-                             policy);
+                    if constexpr (QUANT) {
+                        // One copy per token into its padded slot.
+                        for (uint32_t t = 0; t < P.tpc; ++t)
+                            bulk_g2s(stages + s * P.stage_stride + t * P.slot_stride,
+                                     src + uint64_t(c) * P.chunk_bytes + uint64_t(t) * P.row_set, P.row_set, &full[s],
+                                     policy);
+                    } else {
+                        bulk_g2s(stages + s * P.stage_stride, src + uint64_t(c) * P.chunk_bytes, P.chunk_bytes,
+                                 &full[s], policy);
+                    }
                     issued = it + 1;
                 }
             }
@@ -175,11 +205,14 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
             const uint32_t vg = P.v0 + g, r = gvalid ? vg / P.group : 0, gg = gvalid ? vg % P.group : 0;
             const uint8_t* qp = P.q + l * P.q_layer + r * P.q_row + (kvh * P.group + gg) * P.q_head;
             const uint32_t esz = type_bytes(P.q_type);
+            // Dims of this lane's 8 values in chunk kk: fp16 keys 8c..8c+7;
+            // quantised keys 4c..4c+3 and 16+4c..16+4c+3 (see load_b_chunk).
 #pragma unroll
             for (int kk = 0; kk < KK; ++kk)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    qv[kk][i] = gvalid ? load_scalar(qp + (kk * 32 + c * 8 + i) * esz, P.q_type) : 0.f;
+                    const int dim = QUANT ? kk * 32 + (i < 4 ? 4 * c + i : 16 + 4 * c + i - 4) : kk * 32 + c * 8 + i;
+                    qv[kk][i] = gvalid ? load_scalar(qp + dim * esz, P.q_type) : 0.f;
                     amax = fmaxf(amax, fabsf(qv[kk][i]));
                 }
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -223,24 +256,27 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
                 const uint8_t* stage = stages + s * P.stage_stride;
                 for (uint32_t item = warp; item < items; item += NW) {
                     const uint32_t oct = item / P.kv_heads;  // kv head of `item` is kvh
-                    const uint8_t* brow = stage + ((oct * 8 + g) * P.kv_heads + kvh) * P.row_bytes;
                     float acc[4] = {0.f, 0.f, 0.f, 0.f};
                     if constexpr (!QUANT) {
+                        const uint8_t* brow = stage + ((oct * 8 + g) * P.kv_heads + kvh) * P.row_bytes;
                         uint32_t b[KK][4];
-#pragma unroll
-                        for (int kk = 0; kk < KK; ++kk) load_b_chunk<KT>(brow, kk, c, b[kk]);
+                        unroll_kk<KK>([&](auto kkc) {
+                            constexpr int kk = decltype(kkc)::value;
+                            load_b_chunk<KT, kk>(brow, c, b[kk]);
+                        });
 #pragma unroll
                         for (int kk = 0; kk < KK; ++kk) {
                             mma_16816(acc, qa[kk][0], b[kk][0], b[kk][1]);
                             mma_16816(acc, qa[kk][1], b[kk][2], b[kk][3]);
                         }
                     } else {
-                        const uint8_t* crow0 = stage + ((oct * 8 + 2 * c) * P.kv_heads + kvh) * P.row_bytes;
-                        const uint8_t* crow1 = crow0 + P.kv_heads * P.row_bytes;
-#pragma unroll
-                        for (int kk = 0; kk < KK; ++kk) {
+                        const uint8_t* brow = stage + (oct * 8 + g) * P.slot_stride + kvh * P.row_bytes;
+                        const uint8_t* crow0 = stage + (oct * 8 + 2 * c) * P.slot_stride + kvh * P.row_bytes;
+                        const uint8_t* crow1 = crow0 + P.slot_stride;
+                        unroll_kk<KK>([&](auto kkc) {
+                            constexpr int kk = decltype(kkc)::value;
                             uint32_t b[4];
-                            load_b_chunk<KT>(brow, kk, c, b);
+                            load_b_chunk<KT, kk>(brow, c, b);
                             float blk[4] = {0.f, 0.f, 0.f, 0.f};
                             mma_16816(blk, qa[kk][0], b[0], b[1]);
                             mma_16816(blk, qa[kk][1], b[2], b[3]);
@@ -249,7 +285,7 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_mma_kernel(const LseP
                             acc[1] = fmaf(blk[1], d1, acc[1]);
                             acc[2] = fmaf(blk[2], d0, acc[2]);
                             acc[3] = fmaf(blk[3], d1, acc[3]);
-                        }
+                        });
                     }
                     // Tokens 2c and 2c+1 of the octet for vector g.
                     const uint64_t t0 = tok0 + uint64_t(ch) * P.tpc + oct * 8 + 2 * c;
