@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "lse_launch.cuh"
+#include "page_mass_tc.cuh"
 #include "meank.cuh"
 #include "page_norm.cuh"
 #include "select.cuh"
@@ -109,14 +110,47 @@ struct LseConfig {
     bool mma = false;
     uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0, mma_slot = 0;
     size_t mma_smem = 0;
+    // tcgen05 scorer (fp16 keys, 16..256 query vectors per KV head), when usable.
+    bool tc = false;
+    int tc_ka = 0, tc_mt = 0;
+    uint32_t tc_stages = 0;
+    size_t tc_smem = 0;
 };
 
-// Scorer selection: KVM_SCORER=simt forces the FP32 SIMT kernel (used by the
-// tests to check both kernels against the oracle); anything else picks the
-// tensor-core kernel wherever it applies.
-bool force_simt() {
+// Scorer selection: KVM_SCORER=simt forces the FP32 SIMT kernel and
+// KVM_SCORER=mma the mma.sync kernel wherever it applies; KVM_SCORER=tc
+// requires the tcgen05 kernel (KVM_ERR_UNSUPPORTED where it does not apply).
+// The tests use them to check every kernel against the oracle; anything else
+// picks the tcgen05 kernel, then the mma.sync kernel, wherever they apply.
+bool scorer_is(const char* name) {
     const char* e = std::getenv("KVM_SCORER");
-    return e && std::strcmp(e, "simt") == 0;
+    return e && std::strcmp(e, name) == 0;
+}
+bool force_simt() { return scorer_is("simt"); }
+
+// tcgen05 scorer: fp16 K, head_dim 64 / 128, 16..256 query vectors per KV
+// head (rows x group), pages of 32 / 64 / 128 tokens or multiples of 128, a
+// token range addressable by 32-bit TMA coordinates, and room for at least
+// two K stages next to the query tiles.
+void plan_tc(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, LseConfig* cfg) {
+    if (force_simt() || scorer_is("mma")) return;
+    if (k->type != KVM_F16 || (d->head_dim != 64 && d->head_dim != 128)) return;
+    const uint64_t nv = uint64_t(q->rows) * (d->q_heads / d->kv_heads);
+    if (nv < 16 || nv > 256) return;
+    const uint32_t pt = d->page_tokens;
+    if (pt % 32 || (pt < 128 && 128 % pt) || (pt > 128 && pt % 128)) return;
+    const uint64_t pages = (d->tokens + pt - 1) / pt;
+    if (pages * pt + 128 > 0x7fffffffull) return;
+    const int ka = int(d->head_dim / 64), mt = nv > 128 ? 2 : 1;
+    const size_t fixed = tc_smem_bytes(ka, mt, 0);
+    const size_t stage = size_t(ka) * kTcAtomBytes;
+    if (fixed + 2 * stage > kTcSmemMax) return;
+    const uint32_t stages = uint32_t(std::min<size_t>(kTcMaxStages, (kTcSmemMax - fixed) / stage));
+    cfg->tc = true;
+    cfg->tc_ka = ka;
+    cfg->tc_mt = mt;
+    cfg->tc_stages = stages;
+    cfg->tc_smem = tc_smem_bytes(ka, mt, stages);
 }
 
 void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
@@ -199,6 +233,8 @@ int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache
     cfg->smem = size_t(kLseStages) * cfg->stage_stride + 2 * kLseStages * sizeof(uint64_t) +
                 2 * 2 * size_t(ng) * 8 * sizeof(float) + 16;
     plan_mma(d, k, cfg);
+    plan_tc(d, q, k, cfg);
+    if (scorer_is("tc") && !cfg->tc) return KVM_ERR_UNSUPPORTED;  // strict: the tcgen05 kernel or nothing
     return KVM_OK;
 }
 
@@ -214,6 +250,45 @@ int launch_lse_mma(kvm_ctx* c, int kt, const LseParams& p, int kk, size_t smem, 
         case KVM_Q4_0: return launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s);
         default: return KVM_ERR_UNSUPPORTED;
     }
+}
+
+// cuTensorMapEncodeTiled from the driver (the library links only the runtime).
+using TensorMapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+TensorMapEncodeFn tensor_map_encoder() {
+    static TensorMapEncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TensorMapEncodeFn>(ptr);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// 4-D tensor map of fp16 K of layers [0, nl) from `base`: dims (head_dim,
+// kv_heads, tokens, layers), box 64 dims x 1 head x 128 tokens x 1 layer,
+// 128-byte swizzle; reads past the allocated tokens fill zeros.
+int encode_k_map(const kvm_score_desc* d, const kvm_kcache* k, const void* base, uint32_t nl, CUtensorMap* map) {
+    TensorMapEncodeFn enc = tensor_map_encoder();
+    if (!enc) return KVM_ERR_CUDA;
+    uint64_t cap = std::min<uint64_t>(k->capacity_tokens, 0x7fffffffull);
+    if (nl > 1) cap = std::min<uint64_t>(cap, k->layer_stride / k->token_stride);  // layers never overlap
+    const cuuint64_t dims[4] = {d->head_dim, d->kv_heads, cap, nl};
+    const uint64_t lstride = nl > 1 ? k->layer_stride : cap * k->token_stride;
+    const cuuint64_t strides[3] = {k->head_stride, k->token_stride, lstride};
+    const cuuint32_t box[4] = {64, 1, uint32_t(kTcTile), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? KVM_OK : KVM_ERR_CUDA;
 }
 
 int launch_lse(kvm_ctx* c, int kt, const LseParams& p, int lpr, int vp, size_t smem, cudaStream_t s) {
@@ -265,6 +340,15 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
     p.lse = lse;
     p.status = c->status;
     p.stage_stride = cfg.stage_stride;
+    if (cfg.tc) {
+        // All query vectors of a KV head in one pass (one or two M tiles).
+        CUtensorMap map;
+        KVM_TRY(encode_k_map(d, k, p.k, nl, &map));
+        p.stages = cfg.tc_stages;
+        p.v0 = 0;
+        p.nv = nvt;
+        return launch_lse_tc(c, map, p, cfg.tc_ka, cfg.tc_mt, cfg.tc_smem, s);
+    }
     if (cfg.mma) {
         // Passes of up to 8 query vectors (the 16 rows of the mma's A tile hold
         // their fp16 hi and lo parts).

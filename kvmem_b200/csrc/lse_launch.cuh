@@ -3,6 +3,7 @@
 // type in lse_<type>.cu so the variants compile in parallel).
 #pragma once
 #include <algorithm>
+#include <cuda.h>
 #include <mutex>
 #include <vector>
 
@@ -112,6 +113,12 @@ int launch_lse_mma_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaS
     }
     return KVM_ERR_UNSUPPORTED;
 }
+
+// Tensor-core (tcgen05) scorer of fp16 keys, in lse_tc.cu: ka = head_dim / 64
+// (1 or 2), mt = M tiles of 128 query vectors (1 or 2); `map` is the 4-D TMA
+// tensor map of the K cache built by the caller.
+int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka, int mt, size_t smem,
+                  cudaStream_t s);
 
 // Instantiated once each in lse_<type>.cu.
 extern template int launch_lse_kt<KVM_F32>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);

@@ -1,0 +1,123 @@
+"""GPU parity of the tcgen05 page scorer (query replay / multi-lane batching).
+
+The tcgen05 kernel scores 16..256 query vectors per KV head (rows x group)
+against fp16 keys with head_dim 64 or 128. Every case runs twice: with
+KVM_SCORER=tc, which makes kvm_score_pages fail unless that kernel runs, and
+with KVM_SCORER=mma (the mma.sync kernel) on the same inputs; both are compared
+with the FP64 oracle at the north-star tolerance of 1e-3 relative.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import util as U
+from tests.test_gpu_page_mass import ABS, REL, run_case
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=["tc", "mma"])
+def scorer(request, monkeypatch):
+    monkeypatch.setenv("KVM_SCORER", request.param)
+    return request.param
+
+
+CASES = [
+    # config-4 shape, reduced history: 32 replay rows x 40/8 heads -> 160 vectors per KV head (two M tiles)
+    dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=32, page=128, T=1024, L=2),
+    # one M tile: 4 rows x 5 heads
+    dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=4, page=128, T=1024),
+    # M-tile edges: 128, 129 and 256 vectors
+    dict(ktype=U.F16, D=128, Hq=8, Hkv=2, R=32, page=64, T=512),
+    dict(ktype=U.F16, D=64, Hq=43, Hkv=1, R=3, page=64, T=256),
+    dict(ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320),
+    # head_dim 64, pages of 32, partial last page, spare capacity, three layers
+    dict(ktype=U.F16, D=64, Hq=16, Hkv=4, R=8, page=32, T=1000, cap=1088, L=3),
+    # pages of 256 and 384 tokens (several tiles per page)
+    dict(ktype=U.F16, D=128, Hq=24, Hkv=4, R=4, page=256, T=2048),
+    dict(ktype=U.F16, D=128, Hq=12, Hkv=2, R=3, page=384, T=1500),
+    # per-KV-head aggregation groups, f16 and bf16 queries, explicit scale, softcap
+    dict(ktype=U.F16, D=128, Hq=32, Hkv=8, R=8, page=64, T=512, groups=8),
+    dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=4, page=128, T=640, qtype=U.F16),
+    dict(ktype=U.F16, D=64, Hq=40, Hkv=8, R=8, page=128, T=640, qtype=U.BF16, scale=0.2),
+    dict(ktype=U.F16, D=128, Hq=16, Hkv=4, R=8, page=64, T=512, softcap=30.0, scale=0.25),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(f"{k}{v}" for k, v in c.items()))
+def test_tc_page_mass_matches_oracle(ctx, scorer, case):
+    got, exp = run_case(ctx, **case)
+    np.testing.assert_allclose(got.sum(axis=-1), 1.0, atol=2e-5)
+
+
+@pytest.mark.parametrize("mag", [1e-4, 1.0, 3e3])
+def test_tc_query_magnitudes(ctx, scorer, mag):
+    """Queries far from unit scale: the per-vector power-of-two prescale keeps the
+    fp16 hi / lo split exact enough at both ends (scale adjusted so logits stay O(1))."""
+    import kvmem_b200 as K
+    rng = np.random.default_rng(11)
+    L, R, Hq, Hkv, D, T, page = 1, 8, 16, 4, 128, 512, 64
+    kb = U.make_k(rng, U.F16, L, T, Hkv, D)
+    qf = (rng.standard_normal((L, R, Hq, D)) * mag).astype(np.float32)
+    scale = float(np.float32(1.0 / (np.sqrt(D) * mag)))
+    dev = torch.device("cuda", 0)
+    k_d = torch.from_numpy(kb.reshape(-1).copy()).to(dev)
+    q_d = torch.from_numpy(qf).to(dev)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=page,
+                                     scale=scale)
+    rows, _ = ctx.score_pages(desc, K.RecallContext.make_query(q_d, R),
+                              K.RecallContext.make_kcache(k_d, U.F16, kv_heads=Hkv, head_dim=D, capacity_tokens=T),
+                              want_mean=False)
+    torch.cuda.synchronize()
+    ctx.check_status("score_pages")
+    exp = O.page_mass(qf.view(np.uint8), U.F32, kb, U.F16, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D,
+                      tokens=T, page_tokens=page, scale=scale)
+    ok, worst, nbad = U.close(rows.cpu().numpy(), exp, REL, ABS)
+    assert ok, f"worst {worst:.3g}, {nbad} pages"
+
+
+def test_tc_mask_and_empty_rows(ctx, scorer):
+    """Additive mask rows on the tcgen05 path: hidden tokens, a causal tail, a
+    bias row, and a fully hidden row whose masses are NaN as the reference's."""
+    import kvmem_b200 as K
+    rng = np.random.default_rng(5)
+    L, R, Hq, Hkv, D, T, page = 1, 8, 16, 4, 128, 640, 128
+    mask = np.zeros((R, T), np.float32)
+    mask[0, 100:300] = -np.inf
+    mask[1, :] = rng.standard_normal(T).astype(np.float32)
+    mask[2, :] = -np.inf
+    for r in range(3, R):
+        mask[r, 500 + 10 * r:] = -np.inf
+    kb = U.make_k(rng, U.F16, L, T, Hkv, D)
+    qb = U.make_q(rng, U.F32, L, R, Hq, D)
+    dev = torch.device("cuda", 0)
+    k_d = torch.from_numpy(kb.reshape(-1).copy()).to(dev)
+    q_d = torch.from_numpy(qb.reshape(-1).copy()).to(dev).view(torch.float32).view(L, R, Hq, D)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=page,
+                                     mask=torch.from_numpy(mask).to(dev))
+    rows, _ = ctx.score_pages(desc, K.RecallContext.make_query(q_d, R),
+                              K.RecallContext.make_kcache(k_d, U.F16, kv_heads=Hkv, head_dim=D, capacity_tokens=T),
+                              want_mean=False)
+    torch.cuda.synchronize()
+    got = rows.cpu().numpy()
+    exp = O.page_mass(qb, U.F32, kb, U.F16, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                      page_tokens=page, scale=1 / np.sqrt(D), mask=mask)
+    assert np.isnan(got[0, 0, 2]).all() and np.isnan(exp[0, 0, 2]).all()
+    keep = [r for r in range(R) if r != 2]
+    ok, worst, _ = U.close(got[:, :, keep], exp[:, :, keep], REL, ABS)
+    assert ok, worst
+
+
+def test_tc_strict_mode_rejects_other_shapes(ctx, monkeypatch):
+    """KVM_SCORER=tc refuses shapes outside the tcgen05 kernel (here: 4 vectors per KV head)."""
+    import kvmem_b200 as K
+    monkeypatch.setenv("KVM_SCORER", "tc")
+    dev = torch.device("cuda", 0)
+    k_d = torch.zeros(256 * 2 * 128 * 2, dtype=torch.uint8, device=dev)
+    q_d = torch.zeros((1, 1, 8, 128), dtype=torch.float32, device=dev)
+    desc = K.RecallContext.make_desc(layers=1, q_heads=8, kv_heads=2, head_dim=128, tokens=256, page_tokens=64)
+    with pytest.raises(K.KvmError) as e:
+        ctx.score_pages(desc, K.RecallContext.make_query(q_d, 1),
+                        K.RecallContext.make_kcache(k_d, U.F16, kv_heads=2, head_dim=128, capacity_tokens=256))
+    assert e.value.code == K._abi.ERR_UNSUPPORTED
