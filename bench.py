@@ -7,7 +7,10 @@ memory into a device paged cache). One step = one decode step's recall over
 all 64 layers, steady state: queries drift per step (seeded) and only pages
 not already resident are staged. Prints one JSON line (rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3|c4|c5] [--impl ours|reference]
+
+Config 4 (multi-lane query replay) times selection only on the tcgen05
+scorer; config 5 shards one 1M-token history by page range over the ranks.
 
 Multi-GPU (torchrun): every rank runs an independent decode lane (replica) of
 the workload; value = all ranks' token-layers / max-over-ranks time.
@@ -34,6 +37,7 @@ sys.path.insert(0, ROOT)
 METRIC = "select+stage-in ms/decode step @128K; KV tokens scored/s; % HBM roofline"
 UNIT = "KV token-layers/s"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
 
 
 def parse():
@@ -300,6 +304,139 @@ def run_sharded(args, w, world, rank, local):
     }), flush=True)
 
 
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    except Exception:
+        return FALLBACK_TFLOPS, "fallback"
+
+
+def run_replay(args, w, world, rank, local):
+    """Config 4: multi-lane query replay, selection only. A step scores every page
+    of every (lane, layer) against the lane's 32 replayed query rows x 40 heads
+    (160 vectors per KV head: the tcgen05 kernel), averages the page masses over
+    the replayed rows and picks the top-24 pages per (lane, layer, KV head).
+    Each rank holds its own lanes (replicas: weak scaling)."""
+    import torch
+    import kvmem_b200 as K
+    dev = torch.device("cuda", local)
+    h = build_history(w, args.seed + rank, dev, need_host=False)
+    ctx = K.RecallContext(local)
+    P, L = w.pages, w.layers
+    srows = L * w.groups
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=P * w.page_tokens)
+    qs = [h["q_base"]] + h["drift"]
+    qdescs = [K.RecallContext.make_query(q, w.rows) for q in qs]
+    mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
+    sel_ids = torch.empty((srows, w.budget), dtype=torch.int32, device=dev)
+    sel_n = torch.empty((srows,), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i, qd=None):
+        ctx.recall_step(desc, qd or qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
+                        sel_n=sel_n, chunks=args.chunks)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    a0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    launches = ctx.launches - a0
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    ctx.check_status("replay steps")
+
+    # The page scorer alone (tcgen05 LSE pass + normaliser) for the roofline.
+    kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
+    vectors = w.rows * (w.q_heads // w.kv_heads)
+    flops = 2.0 * vectors * w.head_dim * w.kv_heads * P * w.page_tokens * L
+    ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
+    torch.cuda.synchronize()
+    n_k = max(3, min(10, args.steps))
+    ev0.record(stream)
+    for _ in range(n_k):
+        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = ev0.elapsed_time(ev1) / n_k
+    hbm_peak, hsrc = peaks()
+    tf_peak, tsrc = tensor_peak()
+    gbs = kbytes / (kernel_ms * 1e-3) / 1e9
+    tfs = flops / (kernel_ms * 1e-3) / 1e12
+
+    # End to end: H2D of the step's replayed queries from pinned host memory,
+    # the step, D2H of the selection.
+    q_host = [q.cpu().pin_memory() for q in qs[:2]]
+    q_dev = torch.empty_like(qs[0])
+    qd_e2e = K.RecallContext.make_query(q_dev, w.rows)
+    ids_host = torch.empty(sel_ids.shape, dtype=torch.int32, pin_memory=True)
+    n_host = torch.empty(sel_n.shape, dtype=torch.int32, pin_memory=True)
+    h2d = q_host[0].numel() * 4
+    d2h = ids_host.numel() * 4 + n_host.numel() * 4
+    n_e = max(3, min(10, args.steps))
+    for i in range(2):
+        q_dev.copy_(q_host[i % 2], non_blocking=True)
+        step(i, qd=qd_e2e)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0.record(stream)
+    for i in range(n_e):
+        q_dev.copy_(q_host[i % 2], non_blocking=True)
+        step(i, qd=qd_e2e)
+        ids_host.copy_(sel_ids, non_blocking=True)
+        n_host.copy_(sel_n, non_blocking=True)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / n_e, world)
+    ctx.check_status("replay e2e")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_replay(w, h)
+    ctx.close()
+    if rank != 0:
+        return
+    token_layers = L * w.tokens
+    print(json.dumps({
+        "metric": METRIC, "value": world * token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: seeded on-device N(0,1) fp16 K with per-channel scale U(0.5,2), N(0,1) replay queries",
+        "config": {"workload": w.name, "lanes": 8, "layers_per_lane": L // 8, "q_heads": w.q_heads,
+                   "kv_heads": w.kv_heads, "head_dim": w.head_dim, "tokens_per_lane": w.tokens,
+                   "page_tokens": w.page_tokens, "pages": P, "replay_rows": w.rows,
+                   "vectors_per_kv_head": vectors, "top_k": w.top_k, "selection": "per (lane, layer, KV head)",
+                   "parallelism": f"lane replicas x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
+                   "step": "score all pages (tcgen05) -> mean over replayed rows -> top-24; no stage-in"},
+        "clocks": clk.summary(),
+        "e2e": {"value": world * token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm" if kbytes / hbm_peak / 1e9 >= flops / tf_peak / 1e12 else "tensor",
+                     "kernel": "page_lse_tc_kernel (+page_mass_normalize_kernel)", "kernel_ms": kernel_ms,
+                     "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "peak_source": hsrc, "traffic": None, "algorithmic_bytes": kbytes,
+                     "tensor": {"achieved": tfs, "peak": tf_peak, "unit": "TFLOP/s", "frac": tfs / tf_peak,
+                                "peak_source": tsrc, "algorithmic_flops": flops,
+                                "note": "Q.K^T flops of 160 vectors per KV head, fp16 hi/lo passes not counted"}},
+        "cpu_baseline": cpu,
+    }), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import torch
     import kvmem_b200 as K
@@ -308,6 +445,8 @@ def run_ours(args, world, rank, local):
         return run_kernel_only(args, w, local)
     if args.config == "c5":
         return run_sharded(args, w, world, rank, local)
+    if args.config == "c4":
+        return run_replay(args, w, world, rank, local)
     dev = torch.device("cuda", local)
     seed = args.seed + rank
     h = build_history(w, seed, dev)
@@ -503,6 +642,23 @@ def cpu_baseline_port(w, h):
     return {"value": tokens / dt, "unit": UNIT, "cores": 1, "kind": "port",
             "sample": f"1 layer x {tokens} tokens x {w.q_heads} heads, FP64 oracle restatement "
                       f"(AttentionSampler::qualify), {dt:.1f} s"}
+
+
+def cpu_baseline_replay(w, h):
+    """FP64 per-token page mass of the oracle port (single thread), config 4 sample."""
+    from oracle import oracle as O
+    tokens = 8192
+    rb = h["rbk"]
+    k0 = h["k_dev"][: tokens * w.kv_heads * rb].cpu().numpy()
+    q0 = h["q_base"][0:1].cpu().numpy().astype(np.float32)
+    t0 = time.perf_counter()
+    O.page_mass(q0, O.F32, k0, w.k_type, layers=1, rows=w.rows, heads=w.q_heads, kv_heads=w.kv_heads,
+                dim=w.head_dim, tokens=tokens, page_tokens=w.page_tokens, scale=1 / np.sqrt(w.head_dim),
+                groups=w.groups, k_strides=(tokens * w.kv_heads * rb, w.kv_heads * rb, rb))
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"1 (lane, layer) x {tokens} tokens x {w.rows} replay rows x {w.q_heads} heads, "
+                      f"FP64 oracle restatement (AttentionSampler::qualify), {dt:.1f} s"}
 
 
 # --------------------------------------------------------------------------- reference arm

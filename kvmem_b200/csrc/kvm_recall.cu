@@ -110,9 +110,9 @@ struct LseConfig {
     bool mma = false;
     uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0, mma_slot = 0;
     size_t mma_smem = 0;
-    // tcgen05 scorer (fp16 keys, 16..256 query vectors per KV head), when usable.
+    // tcgen05 scorer (fp16 keys, 16..160 query vectors per KV head), when usable.
     bool tc = false;
-    int tc_ka = 0, tc_mt = 0;
+    int tc_ka = 0, tc_lm = 0;
     uint32_t tc_stages = 0;
     size_t tc_smem = 0;
 };
@@ -128,7 +128,7 @@ bool scorer_is(const char* name) {
 }
 bool force_simt() { return scorer_is("simt"); }
 
-// tcgen05 scorer: fp16 K, head_dim 64 / 128, 16..256 query vectors per KV
+// tcgen05 scorer: fp16 K, head_dim 64 / 128, 16..160 query vectors per KV
 // head (rows x group), pages of 32 / 64 / 128 tokens or multiples of 128, a
 // token range addressable by 32-bit TMA coordinates, and room for at least
 // two K stages next to the query tiles.
@@ -136,21 +136,21 @@ void plan_tc(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, L
     if (force_simt() || scorer_is("mma")) return;
     if (k->type != KVM_F16 || (d->head_dim != 64 && d->head_dim != 128)) return;
     const uint64_t nv = uint64_t(q->rows) * (d->q_heads / d->kv_heads);
-    if (nv < 16 || nv > 256) return;
+    if (nv < 16 || nv > kTcMaxVectors) return;
     const uint32_t pt = d->page_tokens;
     if (pt % 32 || (pt < 128 && 128 % pt) || (pt > 128 && pt % 128)) return;
     const uint64_t pages = (d->tokens + pt - 1) / pt;
     if (pages * pt + 128 > 0x7fffffffull) return;
-    const int ka = int(d->head_dim / 64), mt = nv > 128 ? 2 : 1;
-    const size_t fixed = tc_smem_bytes(ka, mt, 0);
+    const int ka = int(d->head_dim / 64), lm = tc_layout_for(uint32_t(nv));
+    const size_t fixed = tc_smem_bytes(ka, lm, 0);
     const size_t stage = size_t(ka) * kTcAtomBytes;
     if (fixed + 2 * stage > kTcSmemMax) return;
     const uint32_t stages = uint32_t(std::min<size_t>(kTcMaxStages, (kTcSmemMax - fixed) / stage));
     cfg->tc = true;
     cfg->tc_ka = ka;
-    cfg->tc_mt = mt;
+    cfg->tc_lm = lm;
     cfg->tc_stages = stages;
-    cfg->tc_smem = tc_smem_bytes(ka, mt, stages);
+    cfg->tc_smem = tc_smem_bytes(ka, lm, stages);
 }
 
 void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
@@ -347,7 +347,7 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
         p.stages = cfg.tc_stages;
         p.v0 = 0;
         p.nv = nvt;
-        return launch_lse_tc(c, map, p, cfg.tc_ka, cfg.tc_mt, cfg.tc_smem, s);
+        return launch_lse_tc(c, map, p, cfg.tc_ka, cfg.tc_lm, cfg.tc_smem, s);
     }
     if (cfg.mma) {
         // Passes of up to 8 query vectors (the 16 rows of the mma's A tile hold

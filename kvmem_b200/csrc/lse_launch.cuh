@@ -115,9 +115,10 @@ int launch_lse_mma_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaS
 }
 
 // Tensor-core (tcgen05) scorer of fp16 keys, in lse_tc.cu: ka = head_dim / 64
-// (1 or 2), mt = M tiles of 128 query vectors (1 or 2); `map` is the 4-D TMA
-// tensor map of the K cache built by the caller.
-int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka, int mt, size_t smem,
+// (1 or 2), lm = query-tile layout (1: <= 128 vectors per KV head, 2: 129..160
+// with a packed second tile); `map` is the 4-D TMA tensor map of the K cache
+// built by the caller.
+int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka, int lm, size_t smem,
                   cudaStream_t s);
 
 // Instantiated once each in lse_<type>.cu.

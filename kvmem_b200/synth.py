@@ -7,6 +7,12 @@ K rows are 0.8 * q_dir + 0.6 * N(0,1) (times the channel scale), q_dir being the
 layer's mean query direction of the KV head's group normalised to unit RMS;
 one decode query per head ~ N(0,1); top-32 plus first / last page kept.
 
+Config 4 (multi-lane replay): 8 lanes x 48 layers, 40 query / 8 KV heads,
+head_dim 128, 65,536 tokens per lane in pages of 128, fp16 K ~ N(0,1) times
+the channel scale; 32 replayed query rows per lane; top-24 per (lane, layer,
+KV head). The lanes are independent histories, so they are stacked on the
+layer axis (384 rows of K and queries).
+
 Everything is produced by torch generators seeded per (seed, layer) so a rerun
 gives the same bytes; host copies (for stage-in) are pinned and mapped.
 """
@@ -51,6 +57,9 @@ CONFIGS = {
     "c1": Workload("c1_cpu16k", 4, 32, 8, 128, 16384, 64, 16, 8, groups=8),
     "c2": Workload("c2_fp16_128k", 64, 24, 4, 256, 131072, 256, 32, 32),
     "c3": Workload("c3_q8k_q4v_256k", 64, 24, 4, 256, 262144, 256, 64, 32, k_type=3, v_type=4),
+    # 8 lanes x 48 layers folded into 384 (lane, layer) rows of independent selections.
+    "c4": Workload("c4_replay_8x48x64k", 8 * 48, 40, 8, 128, 65536, 128, 24, 0, keep_first_last=False,
+                   groups=8, rows=32),
     "c5": Workload("c5_q8k_sharded_1m", 64, 24, 4, 256, 1048576, 256, 128, 128, k_type=3, v_type=4),
 }
 

@@ -1,6 +1,6 @@
 """GPU parity of the tcgen05 page scorer (query replay / multi-lane batching).
 
-The tcgen05 kernel scores 16..256 query vectors per KV head (rows x group)
+The tcgen05 kernel scores 16..160 query vectors per KV head (rows x group)
 against fp16 keys with head_dim 64 or 128. Every case runs twice: with
 KVM_SCORER=tc, which makes kvm_score_pages fail unless that kernel runs, and
 with KVM_SCORER=mma (the mma.sync kernel) on the same inputs; both are compared
@@ -28,10 +28,11 @@ CASES = [
     dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=32, page=128, T=1024, L=2),
     # one M tile: 4 rows x 5 heads
     dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=4, page=128, T=1024),
-    # M-tile edges: 128, 129 and 256 vectors
+    # M-tile edges: 128, 129, 144 and 160 vectors
     dict(ktype=U.F16, D=128, Hq=8, Hkv=2, R=32, page=64, T=512),
     dict(ktype=U.F16, D=64, Hq=43, Hkv=1, R=3, page=64, T=256),
-    dict(ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320),
+    dict(ktype=U.F16, D=64, Hq=16, Hkv=2, R=18, page=32, T=320),
+    dict(ktype=U.F16, D=64, Hq=10, Hkv=2, R=32, page=64, T=700, L=2),
     # head_dim 64, pages of 32, partial last page, spare capacity, three layers
     dict(ktype=U.F16, D=64, Hq=16, Hkv=4, R=8, page=32, T=1000, cap=1088, L=3),
     # pages of 256 and 384 tokens (several tiles per page)
@@ -109,15 +110,22 @@ def test_tc_mask_and_empty_rows(ctx, scorer):
     assert ok, worst
 
 
-def test_tc_strict_mode_rejects_other_shapes(ctx, monkeypatch):
-    """KVM_SCORER=tc refuses shapes outside the tcgen05 kernel (here: 4 vectors per KV head)."""
+@pytest.mark.parametrize("rows", [1, 32])
+def test_tc_strict_mode_rejects_other_shapes(ctx, monkeypatch, rows):
+    """KVM_SCORER=tc refuses shapes outside the tcgen05 kernel: 4 and 256 vectors per KV head."""
     import kvmem_b200 as K
     monkeypatch.setenv("KVM_SCORER", "tc")
     dev = torch.device("cuda", 0)
     k_d = torch.zeros(256 * 2 * 128 * 2, dtype=torch.uint8, device=dev)
-    q_d = torch.zeros((1, 1, 8, 128), dtype=torch.float32, device=dev)
-    desc = K.RecallContext.make_desc(layers=1, q_heads=8, kv_heads=2, head_dim=128, tokens=256, page_tokens=64)
+    q_d = torch.zeros((1, rows, 16, 128), dtype=torch.float32, device=dev)
+    desc = K.RecallContext.make_desc(layers=1, q_heads=16, kv_heads=2, head_dim=128, tokens=256, page_tokens=64)
     with pytest.raises(K.KvmError) as e:
-        ctx.score_pages(desc, K.RecallContext.make_query(q_d, 1),
+        ctx.score_pages(desc, K.RecallContext.make_query(q_d, rows),
                         K.RecallContext.make_kcache(k_d, U.F16, kv_heads=2, head_dim=128, capacity_tokens=256))
     assert e.value.code == K._abi.ERR_UNSUPPORTED
+
+
+def test_beyond_tc_range_uses_mma_kernel(ctx, monkeypatch):
+    """256 vectors per KV head: the default scorer falls back to the mma.sync kernel, still exact."""
+    monkeypatch.setenv("KVM_SCORER", "auto")
+    run_case(ctx, ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320)
