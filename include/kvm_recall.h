@@ -245,6 +245,23 @@ int kvm_pool_read(kvm_pool* pool, int32_t* slot_of, int32_t* page_of, void* stre
 
 /* -------------------------------------------------------------- Mean-K path */
 
+/* Mean-K producer: per-page K sums kept in HBM. Adds the K rows of tokens
+ * [tok0, tok0 + n) of layers [0, layers) of `k` into
+ *   sums[l][page][kv_heads*head_dim] (device f32, page = token / page_tokens,
+ *   `pages` pages per layer), one f32 add per (token, element) in token order,
+ * and the number of tokens added to each page into counts[page] (device u32,
+ * once per page, not per layer). Replaces kvmem_meank_add + kvmem_meank_d2h +
+ * kvmem_meank_zero (src/adapter/llama-kvmem-stagein.cu:270-316, 1072-1114),
+ * which keep one open-block sum per layer that the host copies out on block
+ * fill and uploads again on every scoring call (kvmem/src/cuda/page_softmax.cu:239-248):
+ * here the table is directly the `sums` / `counts` input of kvm_meank_score.
+ * Key types as the reference's producer (f32, f16, bf16) plus q8_0 / q4_0 /
+ * q5_0 decoded as its key() (llama-kvmem-attention-cuda.cu:39-58). n = 0 is a
+ * no-op; tokens past k->capacity_tokens or pages past `pages` are rejected. */
+int kvm_meank_add(kvm_ctx* ctx, const kvm_kcache* k, uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
+                  uint64_t tok0, uint32_t n, uint32_t page_tokens, float* sums, uint32_t pages, uint32_t* counts,
+                  void* stream);
+
 /* Mean-K page softmax over device-resident per-page K sums. Replaces
  * PageSoftmaxCuda::score (kvmem/src/cuda/page_softmax.cu:202-280):
  *   mean[l,p]  = fp16(sum[l,p] * (1/count[p]))           (raw_kv_store.cpp:606-614, recall_fp16)

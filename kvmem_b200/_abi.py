@@ -105,6 +105,7 @@ SIGNATURES = {
     "kvm_stagein_copies": ([_vp, C.POINTER(Copy), _u32, _u32, _vp], _i),
     "kvm_stagein_wait": ([_vp, _vp, _u64], _i),
     "kvm_pool_read": ([_vp, _vp, _vp, _vp], _i),
+    "kvm_meank_add": ([_vp, C.POINTER(KCache), _u32, _u32, _u32, _u64, _u32, _u32, _vp, _u32, _vp, _vp], _i),
     "kvm_meank_score": ([_vp, _vp, _vp, _vp, C.POINTER(C.c_uint32), _u32, _u32, _u32, _u32, _u32, _u32,
                          C.POINTER(C.c_uint8), _i, C.c_float, _vp, _vp], _i),
     "kvm_recall_step": ([_vp, C.POINTER(StepDesc), _vp, C.POINTER(StageLayout), _vp, _vp, _vp, _vp], _i),

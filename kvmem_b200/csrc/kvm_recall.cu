@@ -707,6 +707,48 @@ int kvm_stagein_wait(kvm_ctx* c, void* stream, uint64_t timeout_us) {
     return kvm_ctx_status(c, stream);
 }
 
+int kvm_meank_add(kvm_ctx* c, const kvm_kcache* k, uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
+                  uint64_t tok0, uint32_t n, uint32_t page_tokens, float* sums, uint32_t pages, uint32_t* counts,
+                  void* stream) {
+    if (!c || !k || !k->data || !sums || !counts) return KVM_ERR_INVALID_ARGUMENT;
+    if (!layers || !kv_heads || !head_dim || !page_tokens || !pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (!supported_type(k->type)) return KVM_ERR_UNSUPPORTED;
+    if (k->type >= KVM_Q8_0 && head_dim % 32) return KVM_ERR_UNSUPPORTED;
+    if (n == 0) return KVM_OK;
+    const uint64_t rb = row_bytes_of(k->type, head_dim);
+    if (k->head_stride < rb || k->token_stride < k->head_stride * kv_heads) return KVM_ERR_INVALID_ARGUMENT;
+    if (layers > 1 && k->layer_stride < k->token_stride * k->capacity_tokens) return KVM_ERR_INVALID_ARGUMENT;
+    const uint64_t end = tok0 + n;
+    if (end > k->capacity_tokens) return KVM_ERR_LENGTH;
+    const uint64_t p0 = tok0 / page_tokens, p1 = (end - 1) / page_tokens;
+    if (p1 >= pages) return KVM_ERR_LENGTH;
+    const uint64_t n_embd = uint64_t(kv_heads) * head_dim;
+    if (n_embd > 0xffffffffull || p1 - p0 + 1 > 65535 || layers > 65535) return KVM_ERR_LENGTH;
+    DeviceGuard g(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(uint32_t((n_embd + 255) / 256), uint32_t(p1 - p0 + 1), layers);
+    const auto* kb = static_cast<const uint8_t*>(k->data);
+    switch (k->type) {
+#define KVM_MEANK_ADD(T)                                                                                          \
+    case T:                                                                                                      \
+        meank_add_kernel<T><<<grid, 256, 0, s>>>(kb, k->layer_stride, k->token_stride, k->head_stride, head_dim, \
+                                                 uint32_t(n_embd), tok0, end, page_tokens, uint32_t(p0), sums,   \
+                                                 pages, counts);                                                 \
+        break;
+        KVM_MEANK_ADD(KVM_F32)
+        KVM_MEANK_ADD(KVM_F16)
+        KVM_MEANK_ADD(KVM_BF16)
+        KVM_MEANK_ADD(KVM_Q8_0)
+        KVM_MEANK_ADD(KVM_Q4_0)
+        KVM_MEANK_ADD(KVM_Q5_0)
+#undef KVM_MEANK_ADD
+        default: return KVM_ERR_UNSUPPORTED;
+    }
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
 int kvm_meank_score(kvm_ctx* c, const float* sums, const uint32_t* counts, const float* q, const uint32_t* layer_rows,
                     uint32_t layers, uint32_t rows, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                     uint32_t pages, const uint8_t* score_mask, int aggregation, float scale, float* out,

@@ -137,4 +137,58 @@ __global__ void meank_accumulate_kernel(const float* logits, const float2* norms
     out[enabled[j]] = acc * weight;
 }
 
+// Element d of one K row (head slice) as float, as the reference's key()
+// (src/adapter/llama-kvmem-attention-cuda.cu:39-58): f32 / f16 / bf16 values,
+// GGUF q8_0 / q4_0 / q5_0 codes times the block's fp16 scale as one rounded
+// f32 product (__fmul_rn: never contracted into the caller's add).
+template <int KT>
+__device__ __forceinline__ float key_elem(const uint8_t* row, uint32_t d) {
+    const uint32_t at = d % 32;
+    if constexpr (KT == KVM_F32) return reinterpret_cast<const float*>(row)[d];
+    if constexpr (KT == KVM_F16) return __half2float(reinterpret_cast<const __half*>(row)[d]);
+    if constexpr (KT == KVM_BF16) return __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(row)[d]) << 16);
+    if constexpr (KT == KVM_Q8_0) {
+        const uint8_t* b = row + (d / 32) * 34u;
+        return __fmul_rn(float(int8_t(b[2 + at])), __half2float(*reinterpret_cast<const __half*>(b)));
+    }
+    if constexpr (KT == KVM_Q4_0) {
+        const uint8_t* b = row + (d / 32) * 18u;
+        const int code = (b[2 + at % 16] >> (at < 16 ? 0 : 4)) & 15;
+        return __fmul_rn(float(code - 8), __half2float(*reinterpret_cast<const __half*>(b)));
+    }
+    if constexpr (KT == KVM_Q5_0) {
+        const uint8_t* b = row + (d / 32) * 22u;
+        const int low = (b[6 + at % 16] >> (at < 16 ? 0 : 4)) & 15;
+        const int high = (b[2 + at / 8] >> (at % 8)) & 1;
+        return __fmul_rn(float((low | (high << 4)) - 16), __half2float(*reinterpret_cast<const __half*>(b)));
+    }
+    return 0.f;
+}
+
+// Mean-K producer: sums[l][page][e] += K[l][t][e] for the tokens t of
+// [tok0, tok_end) in page `page0 + blockIdx.y`, in token order, one f32 add per
+// (token, element) as the reference's meank_add_* kernels
+// (src/adapter/llama-kvmem-stagein.cu:270-316); e = kv_head * D + dim. Block
+// (x = 0, layer 0) of each page also adds the page's new tokens to counts.
+// Grid: x = ceil(n_embd / blockDim), y = pages touched, z = layers.
+template <int KT>
+__global__ void __launch_bounds__(256) meank_add_kernel(const uint8_t* k, uint64_t k_layer, uint64_t k_token,
+                                                        uint64_t k_head, uint32_t D, uint32_t n_embd, uint64_t tok0,
+                                                        uint64_t tok_end, uint32_t page_tokens, uint32_t page0,
+                                                        float* sums, uint32_t pages, uint32_t* counts) {
+    const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t p = page0 + blockIdx.y, l = blockIdx.z;
+    const uint64_t pb = uint64_t(p) * page_tokens;
+    const uint64_t t0 = tok0 > pb ? tok0 : pb;
+    const uint64_t t1 = tok_end < pb + page_tokens ? tok_end : pb + page_tokens;
+    if (l == 0 && blockIdx.x == 0 && threadIdx.x == 0 && t1 > t0) counts[p] += uint32_t(t1 - t0);
+    if (e >= n_embd) return;
+    const uint32_t h = e / D, d = e % D;
+    float* dst = sums + (uint64_t(l) * pages + p) * n_embd + e;
+    float s = *dst;
+    const uint8_t* base = k + l * k_layer + h * k_head;
+    for (uint64_t t = t0; t < t1; ++t) s += key_elem<KT>(base + t * k_token, d);
+    *dst = s;
+}
+
 }  // namespace kvmb

@@ -148,6 +148,17 @@ class RecallContext:
         A.check(rc, "kvm_select_topk")
         return out_ids, out_n
 
+    def meank_add(self, k: A.KCache, sums: torch.Tensor, counts: torch.Tensor, *, tok0: int, n: int,
+                  page_tokens: int, kv_heads: int, head_dim: int, stream=None) -> None:
+        """Adds tokens [tok0, tok0 + n) of every layer of `k` into the per-page sums
+        [L][P][Hkv*D] f32 and their count into counts [P] (int32 tensor, read as u32)."""
+        L, P, E = sums.shape
+        if E != kv_heads * head_dim or counts.numel() < P:
+            raise A.KvmError(A.ERR_INVALID_ARGUMENT, "meank_add: table shape")
+        rc = self.lib.kvm_meank_add(self.h, C.byref(k), L, kv_heads, head_dim, tok0, n, page_tokens,
+                                    sums.data_ptr(), P, counts.data_ptr(), _stream_ptr(stream))
+        A.check(rc, "kvm_meank_add")
+
     def meank_score(self, sums: torch.Tensor, counts: torch.Tensor, q: torch.Tensor, layer_rows: Sequence[int],
                     score_mask: Sequence[int], *, q_heads: int, kv_heads: int, head_dim: int, aggregation: int = 0,
                     scale: float = 0.0, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:

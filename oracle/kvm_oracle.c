@@ -100,6 +100,66 @@ double kvo_decode(int type, const uint8_t* row, uint32_t d) {
 }
 
 /*
+ * Mean-K producer — restates the reference's meank_add_f32/_f16/_bf16 kernels
+ * (src/adapter/llama-kvmem-stagein.cu:270-316: acc[d] += K[token][head][dim]
+ * in token order, one f32 add each) applied per page into a per-page table:
+ * sums[l][page][kv_heads*dim] += value, counts[page] += tokens added, for the
+ * tokens [tok0, tok0+n) of layers [0, layers). Values are the f32 reading of
+ * the key element (the reference's key(), llama-kvmem-attention-cuda.cu:39-58:
+ * codes times the fp16 block scale as one f32 product for q8_0/q4_0/q5_0).
+ * Returns 0, or 1 for a range outside the table.
+ */
+static float half_to_float(uint16_t h) { return (float)kvo_half_to_double(h); }
+
+static float key_elem_f32(int type, const uint8_t* row, uint32_t d) {
+    const uint32_t at = d % 32;
+    switch (type) {
+    case KVO_F32: { float f; memcpy(&f, row + 4ull * d, 4); return f; }
+    case KVO_F16: { uint16_t h; memcpy(&h, row + 2ull * d, 2); return half_to_float(h); }
+    case KVO_BF16: { uint16_t h; memcpy(&h, row + 2ull * d, 2); return (float)bf16_to_double(h); }
+    case KVO_Q8_0: {
+        const uint8_t* b = row + (d / 32) * 34ull;
+        uint16_t h; memcpy(&h, b, 2);
+        const float code = (float)(int8_t)b[2 + at];
+        return code * half_to_float(h);
+    }
+    case KVO_Q4_0: {
+        const uint8_t* b = row + (d / 32) * 18ull;
+        uint16_t h; memcpy(&h, b, 2);
+        const float code = (float)(((b[2 + at % 16] >> (at < 16 ? 0 : 4)) & 15) - 8);
+        return code * half_to_float(h);
+    }
+    case KVO_Q5_0: {
+        const uint8_t* b = row + (d / 32) * 22ull;
+        uint16_t h; memcpy(&h, b, 2);
+        const int low = (b[6 + at % 16] >> (at < 16 ? 0 : 4)) & 15;
+        const int high = (b[2 + at / 8] >> (at % 8)) & 1;
+        const float code = (float)((low | (high << 4)) - 16);
+        return code * half_to_float(h);
+    }
+    }
+    return NAN;
+}
+
+int kvo_meank_add(float* sums, uint32_t* counts, uint32_t pages, const uint8_t* k, int k_type, uint64_t k_layer,
+                  uint64_t k_token, uint64_t k_head, uint32_t layers, uint32_t kv_heads, uint32_t dim, uint64_t tok0,
+                  uint32_t n, uint32_t page_tokens) {
+    if (n == 0) return 0;
+    if ((tok0 + n - 1) / page_tokens >= pages) return 1;
+    const uint64_t n_embd = (uint64_t)kv_heads * dim;
+    for (uint64_t t = tok0; t < tok0 + n; ++t) counts[t / page_tokens] += 1;
+    for (uint32_t l = 0; l < layers; ++l)
+        for (uint64_t e = 0; e < n_embd; ++e) {
+            const uint32_t h = (uint32_t)(e / dim), d = (uint32_t)(e % dim);
+            for (uint64_t t = tok0; t < tok0 + n; ++t) {
+                float* s = sums + ((uint64_t)l * pages + t / page_tokens) * n_embd + e;
+                *s = *s + key_elem_f32(k_type, k + l * k_layer + t * k_token + h * k_head, d);
+            }
+        }
+    return 0;
+}
+
+/*
  * Per-token page mass, FP64 — restates the reference's dense oracle
  * AttentionSampler::qualify (src/adapter/llama-kvmem-attention.cpp:61-94):
  *   logit_t = scale * <q_rh, K_t,kvh(h)>   (FP64 dot of decoded operands)

@@ -70,6 +70,9 @@ def lib():
         L.kvo_plan_residency.argtypes = [_u64p, C.c_uint32, _u64p, C.c_uint32, C.c_int,
                                          _u64p, C.POINTER(C.c_uint32), _u64p, C.POINTER(C.c_uint32),
                                          _u64p, C.POINTER(C.c_uint32)]
+        L.kvo_meank_add.argtypes = [_f32p, _u32p, C.c_uint32, C.c_void_p, C.c_int, C.c_uint64, C.c_uint64,
+                                    C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32,
+                                    C.c_uint32]
         L.kvo_decode.argtypes = [C.c_int, C.c_void_p, C.c_uint32]
         L.kvo_decode.restype = C.c_double
         L.kvo_row_bytes.argtypes = [C.c_int, C.c_uint32]
@@ -143,6 +146,20 @@ def recall_fp16(value: float, use_ref: bool = False) -> float:
     if rc:
         raise ValueError("recall operand rejected")
     return out.value
+
+
+def meank_add(sums: np.ndarray, counts: np.ndarray, k: np.ndarray, k_type: int, *, layers: int, kv_heads: int,
+              dim: int, tok0: int, n: int, page_tokens: int, k_strides=None) -> int:
+    """In place: sums [L][P][Hkv*dim] f32 += K rows of tokens [tok0, tok0+n) (token order, f32 adds),
+    counts [P] u32 += tokens per page. k: bytes [L][T][Hkv][row_bytes] (or k_strides =
+    (layer, token, head) in bytes). Returns the oracle's status (0 ok)."""
+    assert sums.dtype == np.float32 and sums.flags.c_contiguous and counts.dtype == np.uint32
+    rb = row_bytes(k_type, dim)
+    ls, ts, hs = k_strides or (k.shape[1] * kv_heads * rb, kv_heads * rb, rb)
+    kb = np.ascontiguousarray(k).view(np.uint8)
+    return int(lib().kvo_meank_add(sums, counts, sums.shape[1],
+                                   kb.ctypes.data, k_type, ls, ts, hs, layers, kv_heads, dim, tok0, n,
+                                   page_tokens))
 
 
 def meank_scores(means: np.ndarray, q: np.ndarray, layer_rows, *, heads: int, kv_heads: int, dim: int,

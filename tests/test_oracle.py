@@ -274,3 +274,28 @@ def test_page_mass_groups_mask_and_empty_rows():
     assert m.shape == (1, 2, 2, 3)
     np.testing.assert_allclose(m[0, :, 0].sum(axis=1), [1, 1], atol=1e-12)
     assert np.isnan(m[0, :, 1]).all()
+
+
+def test_meank_add_oracle_matches_numpy_sequential_sums():
+    """The Mean-K producer restatement: per-page f32 sums of the decoded key
+    elements added in token order, counts per page; checked against an
+    independent numpy accumulation (f32 adds, f32 code*scale products)."""
+    rng = np.random.default_rng(21)
+    L, T, Hkv, D, B = 2, 150, 3, 64, 32
+    P = -(-T // B)
+    for kt in (U.F32, U.F16, U.BF16, U.Q8_0, U.Q4_0, U.Q5_0):
+        kb = U.make_k(rng, kt, L, T, Hkv, D)
+        sums = np.zeros((L, P, Hkv * D), np.float32)
+        counts = np.zeros(P, np.uint32)
+        for tok0, n in ((0, 40), (40, 1), (41, 1), (42, 108)):
+            assert O.meank_add(sums, counts, kb, kt, layers=L, kv_heads=Hkv, dim=D, tok0=tok0, n=n,
+                               page_tokens=B) == 0
+        vals = U.decode_rows_f32(kb, kt, D)  # [L][T][Hkv][D] float32, code*scale rounded in f32
+        ref = np.zeros_like(sums)
+        for t in range(T):
+            ref[:, t // B] = ref[:, t // B] + vals[:, t].reshape(L, Hkv * D)
+        assert np.array_equal(sums, ref), kt
+        assert counts.tolist() == [min(B, T - p * B) for p in range(P)]
+    # a range past the table is refused
+    assert O.meank_add(np.zeros((1, 2, 64), np.float32), np.zeros(2, np.uint32), U.make_k(rng, U.F16, 1, 100, 1, 64),
+                       U.F16, layers=1, kv_heads=1, dim=64, tok0=60, n=10, page_tokens=32) == 1

@@ -74,3 +74,35 @@ def close(actual, expected, rel=1e-3, abs_=1e-6):
     bound = abs_ + rel * np.abs(expected)
     bad = ~(err <= bound)
     return not bad.any(), float(err.max(initial=0.0)), int(bad.sum())
+
+
+def decode_rows_f32(kb: np.ndarray, ktype: int, dim: int) -> np.ndarray:
+    """Key bytes [..., row_bytes] -> float32 [..., dim], independently of the oracle: f32/f16/bf16
+    values as they are, GGUF q8_0 / q4_0 / q5_0 codes times the block's fp16 scale as one float32
+    product (the reference's key(), src/adapter/llama-kvmem-attention-cuda.cu:39-58)."""
+    lead = kb.shape[:-1]
+    rb = row_bytes(ktype, dim)
+    flat = np.ascontiguousarray(kb).reshape(-1, rb)
+    if ktype == F32:
+        out = flat.view(np.float32)
+    elif ktype == F16:
+        out = flat.view(np.float16).astype(np.float32)
+    elif ktype == BF16:
+        out = (flat.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    else:
+        nb = dim // 32
+        blocks = flat.reshape(-1, nb, BLOCK_BYTES[ktype])
+        scale = blocks[..., 0:2].copy().view(np.float16).astype(np.float32)[..., 0]
+        if ktype == Q8_0:
+            codes = blocks[..., 2:34].view(np.int8).astype(np.float32)
+        else:
+            qs = blocks[..., -16:]
+            low = np.concatenate([qs & 15, qs >> 4], axis=-1).astype(np.int32)
+            if ktype == Q4_0:
+                codes = (low - 8).astype(np.float32)
+            else:
+                qh = blocks[..., 2:6].copy().view(np.uint32)[..., 0]
+                high = ((qh[..., None] >> np.arange(32, dtype=np.uint32)) & 1).astype(np.int32)
+                codes = ((low | (high << 4)) - 16).astype(np.float32)
+        out = (codes * scale[..., None]).astype(np.float32).reshape(-1, dim)
+    return out.reshape(*lead, dim)
