@@ -179,6 +179,70 @@ int kvm_select_topk(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint32_t 
                     const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
                     uint32_t* out_ids, uint32_t* out_n, uint32_t out_stride, void* stream);
 
+/* ------------------------------------------------ post-scoring fusion */
+
+/* Attention-feedback graph (kvmem::GraphSnapshot, kvmem/include/kvmem/graph_recall.hpp:47-99)
+ * as plain arrays: rows in chunk order, each row's edges [edge_begin, edge_begin + edge_count),
+ * positions are page-start tokens. has_messages = 0: no message spans (span coefficient 1). */
+typedef struct kvm_graph_row {
+    uint64_t source;
+    uint64_t samples;
+    uint32_t edge_begin;
+    uint32_t edge_count;
+} kvm_graph_row;
+typedef struct kvm_graph_edge {
+    uint64_t target;
+    double mass;
+} kvm_graph_edge;
+typedef struct kvm_graph_span {
+    uint64_t begin, end;
+    uint32_t end_known;
+    uint32_t reserved;
+} kvm_graph_span;
+typedef struct kvm_graph {
+    uint32_t block_tokens;
+    int32_t has_messages;
+    uint64_t accepted_through, completed_through;
+    const kvm_graph_row* rows;
+    uint32_t nrows;
+    uint32_t nedges;
+    const kvm_graph_edge* edges;
+    const kvm_graph_span* spans;
+    uint32_t nspans;
+    uint32_t reserved;
+} kvm_graph;
+
+/* One-hop propagation of positive score mass over the graph, on the device.
+ * Replaces propagate_query_scores (kvmem/src/host/graph_recall.cpp:494-551):
+ *   total = sum of max(raw, 0) over transport pages, seed = max(raw, 0) / total,
+ *   each transport page sends total*seed*alpha/4*span_coefficient to its
+ *   neighbour pages (start -+ block_tokens) and total*seed*alpha/2*mass/den
+ *   along the edges of its completed graph row, out = max(min(raw, 0), result).
+ * The transfer weights depend only on the graph and the frame: the host side
+ * of this call builds them, the device applies them to the scores in double
+ * precision. raw / out: device f32 [n]; starts / transport_mask: host [n]
+ * (the frame of query_score_frame). Invalid inputs (alpha / cross outside
+ * [0, 1], a graph of another accepted prefix, duplicate or unaligned starts, a
+ * negative or non-finite edge mass) return KVM_ERR_INVALID_ARGUMENT before any
+ * launch; a non-finite raw score sets KVM_ERR_NONFINITE in the context status
+ * and out = raw. raw and out may be the same buffer; n <= 8192. The weights
+ * are uploaded from pageable memory, so the call waits for `stream` to reach
+ * the upload; they live in the context until its next propagation. */
+int kvm_propagate_scores(kvm_ctx* ctx, const float* raw, uint32_t n, const uint64_t* starts,
+                         const uint8_t* transport_mask, uint64_t accepted_through, const kvm_graph* graph,
+                         double alpha, double cross, float* out, void* stream);
+
+/* LRFU preview on the device. Replaces LrfuHistory::preview (kvmem/include/kvmem/lrfu.hpp:57-79):
+ *   threshold = the value of rank min(n-1, floor((1-fraction)*n)) in ascending order
+ *               (no gate when fraction == 1),
+ *   out[i] = lambda * prev[i] (0 for i >= n_prev) + (s[i] >= threshold ? s[i] : min(s[i], 0)).
+ * scores / out: device f32 [n]; prev: device f32 [n_prev] (the committed
+ * history; NULL when n_prev = 0). lambda in [0, 1], fraction in (0, 1], else
+ * KVM_ERR_INVALID_ARGUMENT; a non-finite score sets KVM_ERR_NONFINITE and
+ * leaves out unwritten. Rank the result with kvm_select_topk(signed_scores = 1). */
+int kvm_lrfu_preview(kvm_ctx* ctx, const float* scores, uint32_t n, const float* prev, uint32_t n_prev,
+                     double lambda, double fraction, float* out, void* stream);
+
 /* -------------------------------------------------------- residency + stage-in */
 
 /* Device residency table for `rows` independent selections (one per layer or

@@ -85,6 +85,26 @@ class StepDesc(C.Structure):
 
 
 _vp, _u32, _u64, _i = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int
+class GraphRow(C.Structure):
+    _fields_ = [("source", C.c_uint64), ("samples", C.c_uint64), ("edge_begin", C.c_uint32),
+                ("edge_count", C.c_uint32)]
+
+
+class GraphEdge(C.Structure):
+    _fields_ = [("target", C.c_uint64), ("mass", C.c_double)]
+
+
+class GraphSpan(C.Structure):
+    _fields_ = [("begin", C.c_uint64), ("end", C.c_uint64), ("end_known", C.c_uint32), ("reserved", C.c_uint32)]
+
+
+class Graph(C.Structure):
+    _fields_ = [("block_tokens", C.c_uint32), ("has_messages", C.c_int32), ("accepted_through", C.c_uint64),
+                ("completed_through", C.c_uint64), ("rows", C.POINTER(GraphRow)), ("nrows", C.c_uint32),
+                ("nedges", C.c_uint32), ("edges", C.POINTER(GraphEdge)), ("spans", C.POINTER(GraphSpan)),
+                ("nspans", C.c_uint32), ("reserved", C.c_uint32)]
+
+
 SIGNATURES = {
     "kvm_ctx_create": ([_i, C.POINTER(C.c_void_p)], _i),
     "kvm_ctx_destroy": ([_vp], _i),
@@ -105,6 +125,9 @@ SIGNATURES = {
     "kvm_stagein_copies": ([_vp, C.POINTER(Copy), _u32, _u32, _vp], _i),
     "kvm_stagein_wait": ([_vp, _vp, _u64], _i),
     "kvm_pool_read": ([_vp, _vp, _vp, _vp], _i),
+    "kvm_propagate_scores": ([_vp, _vp, _u32, _vp, _vp, _u64, C.POINTER(Graph), C.c_double, C.c_double, _vp, _vp],
+                             _i),
+    "kvm_lrfu_preview": ([_vp, _vp, _u32, _vp, _u32, C.c_double, C.c_double, _vp, _vp], _i),
     "kvm_meank_add": ([_vp, C.POINTER(KCache), _u32, _u32, _u32, _u64, _u32, _u32, _vp, _u32, _vp, _vp], _i),
     "kvm_meank_score": ([_vp, _vp, _vp, _vp, C.POINTER(C.c_uint32), _u32, _u32, _u32, _u32, _u32, _u32,
                          C.POINTER(C.c_uint8), _i, C.c_float, _vp, _vp], _i),

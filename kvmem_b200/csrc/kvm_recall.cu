@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <unordered_map>
 #include <vector>
 
 #include "common.cuh"
@@ -13,6 +14,7 @@
 #include "page_mass_tc.cuh"
 #include "meank.cuh"
 #include "page_norm.cuh"
+#include "post.cuh"
 #include "select.cuh"
 #include "shard.cuh"
 #include "stagein.cuh"
@@ -82,6 +84,33 @@ int ensure_small(kvm_ctx* c, size_t bytes) {
     KVM_CUDA(cudaMalloc(&c->small, want));
     c->small_bytes = want;
     return KVM_OK;
+}
+
+int ensure_aux(kvm_ctx* c, size_t bytes) {
+    if (bytes <= c->aux_bytes) return KVM_OK;
+    if (c->aux) {
+        cudaDeviceSynchronize();
+        cudaFree(c->aux);
+        c->aux = nullptr;
+        c->aux_bytes = 0;
+    }
+    const size_t want = std::max<size_t>(align256(bytes), 1 << 16);
+    KVM_CUDA(cudaMalloc(&c->aux, want));
+    c->aux_bytes = want;
+    return KVM_OK;
+}
+
+// span_coefficient (kvmem/src/host/graph_recall.cpp:234-246).
+double span_coefficient(const kvm_graph* g, uint64_t a, uint64_t b, double cross) {
+    if (!g->has_messages) return 1.0;
+    const uint64_t begin = std::min(a, b), end = std::max(a, b) + g->block_tokens;
+    for (uint32_t i = 0; i < g->nspans; ++i)
+        if (g->spans[i].begin <= begin && end <= g->spans[i].end) return 1.0;
+    for (uint32_t i = 0; i < g->nspans; ++i) {
+        const auto& sp = g->spans[i];
+        if ((begin < sp.begin && sp.begin < end) || (sp.end_known && begin < sp.end && sp.end < end)) return cross;
+    }
+    return 1.0;
 }
 
 // The keep list lives at the start of the small scratch (first 4 KiB + list);
@@ -515,6 +544,7 @@ int kvm_ctx_destroy(kvm_ctx* c) {
     if (c->status_host) cudaFreeHost(c->status_host);
     if (c->ws && !c->ws_borrowed) cudaFree(c->ws);
     if (c->small) cudaFree(c->small);
+    if (c->aux) cudaFree(c->aux);
     delete c;
     return KVM_OK;
 }
@@ -705,6 +735,136 @@ int kvm_stagein_wait(kvm_ctx* c, void* stream, uint64_t timeout_us) {
         if (uint64_t(us) >= timeout_us) return KVM_ERR_TIMEOUT;
     }
     return kvm_ctx_status(c, stream);
+}
+
+int kvm_propagate_scores(kvm_ctx* c, const float* raw, uint32_t n, const uint64_t* starts,
+                         const uint8_t* transport_mask, uint64_t accepted_through, const kvm_graph* g, double alpha,
+                         double cross, float* out, void* stream) {
+    if (!c || !raw || !out || !starts || !transport_mask || !g) return KVM_ERR_INVALID_ARGUMENT;
+    if (!(std::isfinite(alpha) && alpha >= 0 && alpha <= 1) || !(std::isfinite(cross) && cross >= 0 && cross <= 1))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (!g->block_tokens || g->accepted_through != accepted_through) return KVM_ERR_INVALID_ARGUMENT;
+    if ((g->nrows && !g->rows) || (g->nedges && !g->edges) || (g->has_messages && g->nspans && !g->spans))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (n == 0) return KVM_OK;
+    if (n > 8u * kPostThreads) return KVM_ERR_LENGTH;
+    const uint64_t block = g->block_tokens;
+    // Frame index of each transport page, by its start.
+    std::unordered_map<uint64_t, uint32_t> where;
+    std::unordered_map<uint64_t, uint32_t> seen;
+    uint32_t nallowed = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (starts[i] % block || !seen.emplace(starts[i], i).second) return KVM_ERR_INVALID_ARGUMENT;
+        if (transport_mask[i]) {
+            where.emplace(starts[i], i);
+            ++nallowed;
+        }
+    }
+    // Transfers (source, target, weight) in the reference's order: neighbours of
+    // every transport page, then the completed graph rows.
+    std::vector<uint32_t> ts, td;
+    std::vector<double> tw;
+    if (alpha > 0 && nallowed > 1) {
+        for (uint32_t i = 0; i < n; ++i) {
+            if (!transport_mask[i]) continue;
+            const uint64_t src = starts[i];
+            for (int dir = -1; dir <= 1; dir += 2) {
+                if (dir < 0 && src < block) continue;
+                if (dir > 0 && src > UINT64_MAX - block) continue;
+                const uint64_t tgt = dir < 0 ? src - block : src + block;
+                const auto it = where.find(tgt);
+                if (it == where.end()) continue;
+                ts.push_back(i);
+                td.push_back(it->second);
+                tw.push_back(alpha * .25 * span_coefficient(g, src, tgt, cross));
+            }
+        }
+        for (uint32_t r = 0; r < g->nrows; ++r) {
+            const kvm_graph_row& row = g->rows[r];
+            const auto sit = where.find(row.source);
+            if (sit == where.end() || !row.samples || row.source + block > g->completed_through) continue;
+            if (uint64_t(row.edge_begin) + row.edge_count > g->nedges) return KVM_ERR_INVALID_ARGUMENT;
+            double den = 0;
+            for (uint32_t e = row.edge_begin; e < row.edge_begin + row.edge_count; ++e) {
+                const kvm_graph_edge& edge = g->edges[e];
+                if (!(std::isfinite(edge.mass) && edge.mass >= 0)) return KVM_ERR_INVALID_ARGUMENT;
+                if (edge.target != row.source && where.count(edge.target)) den += edge.mass;
+            }
+            if (!den) continue;
+            for (uint32_t e = row.edge_begin; e < row.edge_begin + row.edge_count; ++e) {
+                const kvm_graph_edge& edge = g->edges[e];
+                const auto tit = where.find(edge.target);
+                if (tit == where.end() || edge.target == row.source) continue;
+                ts.push_back(sit->second);
+                td.push_back(tit->second);
+                tw.push_back(alpha * .5 * edge.mass / den);
+            }
+        }
+    }
+    // By source and by target, each in transfer order (counting sort).
+    const size_t m = tw.size();
+    std::vector<uint32_t> out_off(n + 1, 0), in_off(n + 1, 0), in_src(std::max<size_t>(m, 1));
+    std::vector<double> out_w(std::max<size_t>(m, 1)), in_w(std::max<size_t>(m, 1));
+    for (size_t k = 0; k < m; ++k) {
+        ++out_off[ts[k] + 1];
+        ++in_off[td[k] + 1];
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        out_off[i + 1] += out_off[i];
+        in_off[i + 1] += in_off[i];
+    }
+    {
+        std::vector<uint32_t> po(out_off.begin(), out_off.end() - 1), pi(in_off.begin(), in_off.end() - 1);
+        for (size_t k = 0; k < m; ++k) {
+            out_w[po[ts[k]]++] = tw[k];
+            in_src[pi[td[k]]] = ts[k];
+            in_w[pi[td[k]]++] = tw[k];
+        }
+    }
+    // One upload: allowed | out_off | in_off | in_src | out_w | in_w.
+    const size_t o_allowed = 0, o_outoff = align256(n), o_inoff = o_outoff + align256((n + 1) * 4ull),
+                 o_insrc = o_inoff + align256((n + 1) * 4ull), o_outw = o_insrc + align256(in_src.size() * 4),
+                 o_inw = o_outw + align256(out_w.size() * 8), total = o_inw + align256(in_w.size() * 8);
+    std::vector<uint8_t> host(total, 0);
+    std::memcpy(host.data() + o_allowed, transport_mask, n);
+    std::memcpy(host.data() + o_outoff, out_off.data(), (n + 1) * 4ull);
+    std::memcpy(host.data() + o_inoff, in_off.data(), (n + 1) * 4ull);
+    std::memcpy(host.data() + o_insrc, in_src.data(), in_src.size() * 4);
+    std::memcpy(host.data() + o_outw, out_w.data(), out_w.size() * 8);
+    std::memcpy(host.data() + o_inw, in_w.data(), in_w.size() * 8);
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_TRY(ensure_aux(c, total));
+    auto* a = static_cast<uint8_t*>(c->aux);
+    KVM_CUDA(cudaMemcpyAsync(a, host.data(), total, cudaMemcpyHostToDevice, s));
+    // No transfer at all (alpha 0, one transport page): the scores pass through.
+    propagate_kernel<<<1, kPostThreads, 0, s>>>(
+        raw, n, a + o_allowed, m ? nallowed : 0, reinterpret_cast<const uint32_t*>(a + o_outoff),
+        reinterpret_cast<const double*>(a + o_outw), reinterpret_cast<const uint32_t*>(a + o_inoff),
+        reinterpret_cast<const uint32_t*>(a + o_insrc), reinterpret_cast<const double*>(a + o_inw), out, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;  // a pageable upload is staged before cudaMemcpyAsync returns: `host` may go
+}
+
+int kvm_lrfu_preview(kvm_ctx* c, const float* scores, uint32_t n, const float* prev, uint32_t n_prev, double lambda,
+                     double fraction, float* out, void* stream) {
+    if (!c || !scores || !out || (n_prev && !prev)) return KVM_ERR_INVALID_ARGUMENT;
+    if (!(std::isfinite(lambda) && lambda >= 0 && lambda <= 1) ||
+        !(std::isfinite(fraction) && fraction > 0 && fraction <= 1))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (n == 0) return KVM_OK;
+    uint32_t rank = 0xffffffffu;
+    if (fraction < 1) {
+        const size_t r = static_cast<size_t>((1 - fraction) * n);  // lrfu.hpp:66-67
+        rank = uint32_t(std::min<size_t>(n - 1, r));
+    }
+    DeviceGuard guard(c->device);
+    lrfu_preview_kernel<<<1, kPostThreads, 0, static_cast<cudaStream_t>(stream)>>>(scores, n, prev, n_prev, lambda,
+                                                                                   rank, out, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
 }
 
 int kvm_meank_add(kvm_ctx* c, const kvm_kcache* k, uint32_t layers, uint32_t kv_heads, uint32_t head_dim,

@@ -23,6 +23,8 @@ struct kvm_ctx {
     bool ws_borrowed = false;
     void* small = nullptr;  // device copy of short host-built tables
     size_t small_bytes = 0;
+    void* aux = nullptr;  // device copy of per-call host-built tables (propagation weights)
+    size_t aux_bytes = 0;
     std::vector<uint32_t> keep_cached;
     bool keep_valid = false;
     uint64_t launches = 0;

@@ -148,6 +148,58 @@ class RecallContext:
         A.check(rc, "kvm_select_topk")
         return out_ids, out_n
 
+    @staticmethod
+    def make_graph(graph: dict):
+        """kvm_graph from dict(block, accepted, completed, rows=[(source, samples, [(target, mass), ...])],
+        spans=None | [(begin, end, end_known)]); returns (struct, keepalive)."""
+        rows = graph.get("rows", [])
+        edges = [e for r in rows for e in r[2]]
+        spans = graph.get("spans")
+        ra = (A.GraphRow * max(1, len(rows)))()
+        ea = (A.GraphEdge * max(1, len(edges)))()
+        sa = (A.GraphSpan * max(1, len(spans or [])))()
+        off = 0
+        for i, (src, samples, es) in enumerate(rows):
+            ra[i].source, ra[i].samples, ra[i].edge_begin, ra[i].edge_count = src, samples, off, len(es)
+            off += len(es)
+        for i, (tgt, mass) in enumerate(edges):
+            ea[i].target, ea[i].mass = tgt, mass
+        for i, (b, e, known) in enumerate(spans or []):
+            sa[i].begin, sa[i].end, sa[i].end_known = b, e, int(bool(known))
+        g = A.Graph()
+        g.block_tokens, g.has_messages = graph["block"], int(spans is not None)
+        g.accepted_through, g.completed_through = graph["accepted"], graph["completed"]
+        g.rows, g.nrows, g.edges, g.nedges = ra, len(rows), ea, len(edges)
+        g.spans, g.nspans = sa, len(spans or [])
+        return g, (ra, ea, sa)
+
+    def propagate_scores(self, raw: torch.Tensor, starts: Sequence[int], transport_mask: Sequence[int],
+                         accepted: int, graph: dict, *, alpha: float = 0.2, cross: float = 0.25,
+                         out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """raw [n] f32 on the device -> propagated scores [n] f32 (kvm_propagate_scores)."""
+        n = raw.numel()
+        if out is None:
+            out = torch.empty_like(raw)
+        st = (C.c_uint64 * max(1, n))(*starts)
+        tm = (C.c_uint8 * max(1, n))(*[1 if x else 0 for x in transport_mask])
+        g, keep = self.make_graph(graph)
+        rc = self.lib.kvm_propagate_scores(self.h, raw.data_ptr(), n, st, tm, accepted, C.byref(g), alpha, cross,
+                                           out.data_ptr(), _stream_ptr(stream))
+        A.check(rc, "kvm_propagate_scores")
+        return out
+
+    def lrfu_preview(self, scores: torch.Tensor, prev: Optional[torch.Tensor], *, lam: float = 0.5,
+                     fraction: float = 0.9, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """scores [n] f32, prev [n_prev] f32 (committed history, device) -> candidate [n] f32."""
+        n = scores.numel()
+        if out is None:
+            out = torch.empty_like(scores)
+        n_prev = 0 if prev is None else prev.numel()
+        rc = self.lib.kvm_lrfu_preview(self.h, scores.data_ptr(), n, prev.data_ptr() if n_prev else None, n_prev,
+                                       lam, fraction, out.data_ptr(), _stream_ptr(stream))
+        A.check(rc, "kvm_lrfu_preview")
+        return out
+
     def meank_add(self, k: A.KCache, sums: torch.Tensor, counts: torch.Tensor, *, tok0: int, n: int,
                   page_tokens: int, kv_heads: int, head_dim: int, stream=None) -> None:
         """Adds tokens [tok0, tok0 + n) of every layer of `k` into the per-page sums

@@ -160,6 +160,138 @@ int kvo_meank_add(float* sums, uint32_t* counts, uint32_t pages, const uint8_t* 
 }
 
 /*
+ * One-hop score propagation — restates propagate_query_scores
+ * (kvmem/src/host/graph_recall.cpp:494-551, span_coefficient :234-246) over a
+ * graph given as arrays: rows (source position, samples, edges
+ * [edge_begin, edge_begin + edge_count)), edges (target position, mass), and
+ * optional message spans. Sources are visited in frame order (the reference
+ * walks an unordered_map, so its own summation order is unspecified).
+ * Returns 0, 1 for an invalid input (the reference's invalid_argument).
+ */
+static double span_coef(uint64_t a, uint64_t b, uint32_t block, const uint64_t* sb, const uint64_t* se,
+                        const uint8_t* sk, uint32_t ns, int has_messages, double cross) {
+    if (!has_messages) return 1;
+    const uint64_t begin = a < b ? a : b, end = (a > b ? a : b) + block;
+    for (uint32_t i = 0; i < ns; ++i)
+        if (sb[i] <= begin && end <= se[i]) return 1;
+    for (uint32_t i = 0; i < ns; ++i)
+        if ((begin < sb[i] && sb[i] < end) || (sk[i] && begin < se[i] && se[i] < end)) return cross;
+    return 1;
+}
+
+static int64_t frame_index(const uint64_t* starts, const uint8_t* allowed, uint32_t n, uint64_t pos) {
+    for (uint32_t i = 0; i < n; ++i)
+        if (starts[i] == pos) return allowed[i] ? (int64_t)i : -1;
+    return -1;
+}
+
+int kvo_propagate_scores(const double* raw, uint32_t n, const uint64_t* starts, const uint8_t* transport_mask,
+                         uint64_t frame_accepted, uint32_t block, uint64_t graph_accepted, uint64_t completed,
+                         const uint64_t* row_source, const uint64_t* row_samples, const uint32_t* row_begin,
+                         const uint32_t* row_count, uint32_t nrows, const uint64_t* edge_target,
+                         const double* edge_mass, const uint64_t* span_begin, const uint64_t* span_end,
+                         const uint8_t* span_end_known, uint32_t nspans, int has_messages, double alpha,
+                         double cross, double* out) {
+    if (!(isfinite(alpha) && alpha >= 0 && alpha <= 1) || !(isfinite(cross) && cross >= 0 && cross <= 1)) return 1;
+    if (!block || graph_accepted != frame_accepted) return 1;
+    double total = 0;
+    uint32_t nallowed = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!isfinite(raw[i]) || starts[i] % block) return 1;
+        for (uint32_t j = 0; j < i; ++j)
+            if (starts[j] == starts[i]) return 1;
+        if (transport_mask[i]) {
+            ++nallowed;
+            total += raw[i] > 0 ? raw[i] : 0;
+        }
+    }
+    if (!isfinite(total)) return 1;
+    for (uint32_t i = 0; i < n; ++i) out[i] = raw[i];
+    if (nallowed <= 1 || total == 0 || alpha == 0) return 0;
+    double* seed = (double*)calloc(n, sizeof(double));
+    if (!seed) return 2;
+    for (uint32_t i = 0; i < n; ++i)
+        if (transport_mask[i]) seed[i] = (raw[i] > 0 ? raw[i] : 0) / total;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (!transport_mask[i]) continue;
+        const uint64_t src = starts[i];
+        for (int dir = -1; dir <= 1; dir += 2) {
+            if (dir < 0 && src < block) continue;
+            if (dir > 0 && src > UINT64_MAX - block) continue;
+            const uint64_t tgt = dir < 0 ? src - block : src + block;
+            const int64_t j = frame_index(starts, transport_mask, n, tgt);
+            if (j < 0) continue;
+            const double w = alpha * .25 *
+                             span_coef(src, tgt, block, span_begin, span_end, span_end_known, nspans, has_messages, cross);
+            const double delta = total * seed[i] * w;
+            out[i] -= delta;
+            out[j] += delta;
+        }
+    }
+    for (uint32_t r = 0; r < nrows; ++r) {
+        const int64_t i = frame_index(starts, transport_mask, n, row_source[r]);
+        if (i < 0 || !row_samples[r] || row_source[r] + block > completed) continue;
+        double den = 0;
+        for (uint32_t e = row_begin[r]; e < row_begin[r] + row_count[r]; ++e) {
+            if (!(isfinite(edge_mass[e]) && edge_mass[e] >= 0)) { free(seed); return 1; }
+            if (edge_target[e] != row_source[r] && frame_index(starts, transport_mask, n, edge_target[e]) >= 0)
+                den += edge_mass[e];
+        }
+        if (!den) continue;
+        for (uint32_t e = row_begin[r]; e < row_begin[r] + row_count[r]; ++e) {
+            const int64_t j = frame_index(starts, transport_mask, n, edge_target[e]);
+            if (j < 0 || edge_target[e] == row_source[r]) continue;
+            const double delta = total * seed[i] * (alpha * .5 * edge_mass[e] / den);
+            out[i] -= delta;
+            out[j] += delta;
+        }
+    }
+    free(seed);
+    for (uint32_t i = 0; i < n; ++i) {
+        const double residual = raw[i] < 0 ? raw[i] : 0;
+        if (!isfinite(out[i]) || out[i] < residual - 1e-12 * (total > 1 ? total : 1)) return 2;
+        if (out[i] < residual) out[i] = residual;
+    }
+    return 0;
+}
+
+/*
+ * LRFU preview — restates LrfuHistory::preview (kvmem/include/kvmem/lrfu.hpp:57-79):
+ * threshold = the value of rank min(n-1, floor((1-fraction)*n)) in ascending
+ * order (-inf when fraction == 1); out[i] = lambda*prev[i] (0 past n_prev) +
+ * (score >= threshold ? score : min(score, 0)). Returns 1 for a non-finite
+ * score or an invalid lambda / fraction.
+ */
+static int cmp_double(const void* a, const void* b) {
+    const double x = *(const double*)a, y = *(const double*)b;
+    return x < y ? -1 : x > y;
+}
+
+int kvo_lrfu_preview(const double* scores, uint32_t n, const double* prev, uint32_t n_prev, double lambda,
+                     double fraction, double* out) {
+    if (!(isfinite(lambda) && lambda >= 0 && lambda <= 1) || !(isfinite(fraction) && fraction > 0 && fraction <= 1))
+        return 1;
+    for (uint32_t i = 0; i < n; ++i)
+        if (!isfinite(scores[i])) return 1;
+    if (!n) return 0;
+    double threshold = -INFINITY;
+    if (fraction < 1) {
+        double* ranked = (double*)malloc(n * sizeof(double));
+        if (!ranked) return 2;
+        memcpy(ranked, scores, n * sizeof(double));
+        qsort(ranked, n, sizeof(double), cmp_double);
+        size_t rank = (size_t)((1 - fraction) * n);
+        if (rank > n - 1) rank = n - 1;
+        threshold = ranked[rank];
+        free(ranked);
+    }
+    for (uint32_t i = 0; i < n; ++i)
+        out[i] = lambda * (i < n_prev ? prev[i] : 0) +
+                 (scores[i] >= threshold ? scores[i] : (scores[i] < 0 ? scores[i] : 0));
+    return 0;
+}
+
+/*
  * Per-token page mass, FP64 — restates the reference's dense oracle
  * AttentionSampler::qualify (src/adapter/llama-kvmem-attention.cpp:61-94):
  *   logit_t = scale * <q_rh, K_t,kvh(h)>   (FP64 dot of decoded operands)

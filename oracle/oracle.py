@@ -42,6 +42,11 @@ def build(ref: bool = False) -> None:
                               stdout=subprocess.DEVNULL)
 
 
+_PROPAGATE_ARGS = [_f64p, C.c_uint32, _u64p, _u8p, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint64,
+                   _u64p, _u64p, _u32p, _u32p, C.c_uint32, _u64p, _f64p, _u64p, _u64p, _u8p, C.c_uint32,
+                   C.c_int, C.c_double, C.c_double, _f64p]
+_LRFU_ARGS = [_f64p, C.c_uint32, _f64p, C.c_uint32, C.c_double, C.c_double, _f64p]
+
 _lib = None
 _ref = None
 
@@ -73,6 +78,8 @@ def lib():
         L.kvo_meank_add.argtypes = [_f32p, _u32p, C.c_uint32, C.c_void_p, C.c_int, C.c_uint64, C.c_uint64,
                                     C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32,
                                     C.c_uint32]
+        L.kvo_propagate_scores.argtypes = _PROPAGATE_ARGS
+        L.kvo_lrfu_preview.argtypes = _LRFU_ARGS
         L.kvo_decode.argtypes = [C.c_int, C.c_void_p, C.c_uint32]
         L.kvo_decode.restype = C.c_double
         L.kvo_row_bytes.argtypes = [C.c_int, C.c_uint32]
@@ -97,6 +104,8 @@ def ref():
         L.kvref_recall_fp16.argtypes = [C.c_float, C.POINTER(C.c_float)]
         L.kvref_pick_scored.argtypes = lib().kvo_pick_scored.argtypes
         L.kvref_plan_residency.argtypes = lib().kvo_plan_residency.argtypes
+        L.kvref_propagate_scores.argtypes = _PROPAGATE_ARGS
+        L.kvref_lrfu_preview.argtypes = _LRFU_ARGS
         _ref = L
     return _ref
 
@@ -242,3 +251,45 @@ def ref_page_softmax_scores(sums, counts, q, layer_rows, *, heads, kv_heads, dim
     if rc:
         raise ValueError(f"reference page_softmax_scores rejected (rc={rc})")
     return out[:P]
+
+
+def _graph_arrays(graph):
+    """graph: dict(block, accepted, completed, rows=[(source, samples, [(target, mass), ...])],
+    spans=None | [(begin, end, end_known)])."""
+    rows = graph.get("rows", [])
+    src = np.array([r[0] for r in rows] or [0], np.uint64)
+    smp = np.array([r[1] for r in rows] or [0], np.uint64)
+    cnt = np.array([len(r[2]) for r in rows] or [0], np.uint32)
+    beg = np.concatenate([[0], np.cumsum(cnt)[:-1]]).astype(np.uint32) if rows else np.zeros(1, np.uint32)
+    edges = [e for r in rows for e in r[2]]
+    tgt = np.array([e[0] for e in edges] or [0], np.uint64)
+    mass = np.array([e[1] for e in edges] or [0.0], np.float64)
+    spans = graph.get("spans")
+    sb = np.array([x[0] for x in spans or []] or [0], np.uint64)
+    se = np.array([x[1] for x in spans or []] or [0], np.uint64)
+    sk = np.array([1 if x[2] else 0 for x in spans or []] or [0], np.uint8)
+    return src, smp, beg, cnt, len(rows), tgt, mass, sb, se, sk, len(spans or []), 1 if spans is not None else 0
+
+
+def propagate_scores(raw, starts, transport_mask, accepted, graph, alpha=0.2, cross=0.25, use_ref=False):
+    """(rc, out) of propagate_query_scores: the C restatement, or the reference itself (use_ref)."""
+    raw = np.ascontiguousarray(raw, np.float64)
+    n = len(raw)
+    out = np.zeros(max(1, n), np.float64)
+    src, smp, beg, cnt, nrows, tgt, mass, sb, se, sk, ns, hm = _graph_arrays(graph)
+    fn = ref().kvref_propagate_scores if use_ref else lib().kvo_propagate_scores
+    rc = fn(raw if n else np.zeros(1), n, np.ascontiguousarray(starts, np.uint64),
+            np.ascontiguousarray(transport_mask, np.uint8), accepted, graph["block"], graph["accepted"],
+            graph["completed"], src, smp, beg, cnt, nrows, tgt, mass, sb, se, sk, ns, hm, alpha, cross, out)
+    return int(rc), out[:n]
+
+
+def lrfu_preview(scores, prev, lam=0.5, fraction=0.9, use_ref=False):
+    scores = np.ascontiguousarray(scores, np.float64)
+    n_prev = len(prev)
+    prev = np.ascontiguousarray(prev if n_prev else [0.0], np.float64)
+    n = len(scores)
+    out = np.zeros(max(1, n), np.float64)
+    fn = ref().kvref_lrfu_preview if use_ref else lib().kvo_lrfu_preview
+    rc = fn(scores if n else np.zeros(1), n, prev, n_prev, lam, fraction, out)
+    return int(rc), out[:n]

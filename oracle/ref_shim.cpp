@@ -13,6 +13,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <vector>
 
@@ -123,6 +124,64 @@ int kvref_plan_residency(const uint64_t* resident, uint32_t nres, const uint64_t
         *nevict = uint32_t(d.evict.size());
         *nretain = uint32_t(d.retain.size());
         *nrestore = uint32_t(d.restore.size());
+    });
+}
+
+// propagate_query_scores (kvmem/src/host/graph_recall.cpp:494) on a
+// GraphSnapshot assembled from arrays (one chunk holding every row; message
+// spans when has_messages), a frame given by starts / transport_mask.
+int kvref_propagate_scores(const double* raw, uint32_t n, const uint64_t* starts, const uint8_t* transport_mask,
+                           uint64_t frame_accepted, uint32_t block, uint64_t graph_accepted, uint64_t completed,
+                           const uint64_t* row_source, const uint64_t* row_samples, const uint32_t* row_begin,
+                           const uint32_t* row_count, uint32_t nrows, const uint64_t* edge_target,
+                           const double* edge_mass, const uint64_t* span_begin, const uint64_t* span_end,
+                           const uint8_t* span_end_known, uint32_t nspans, int has_messages, double alpha,
+                           double cross, double* out) {
+    return guarded([&] {
+        kvmem::QueryScoreFrame frame;
+        frame.starts.assign(starts, starts + n);
+        frame.counts.assign(n, block);
+        frame.score_mask.assign(n, 1);
+        frame.transport_mask.assign(transport_mask, transport_mask + n);
+        frame.accepted_through = frame_accepted;
+        kvmem::GraphSnapshot graph;
+        graph.block_tokens = block;
+        graph.accepted_through = graph_accepted;
+        graph.completed_through = completed;
+        auto rows = std::make_shared<std::vector<kvmem::GraphRow>>();
+        for (uint32_t r = 0; r < nrows; ++r) {
+            kvmem::GraphRow row;
+            row.source = row_source[r];
+            row.samples = row_samples[r];
+            for (uint32_t e = row_begin[r]; e < row_begin[r] + row_count[r]; ++e)
+                row.edges.push_back({edge_target[e], edge_mass[e]});
+            rows->push_back(std::move(row));
+        }
+        if (nrows) graph.chunks.push_back(rows);
+        if (has_messages) {
+            auto spans = std::make_shared<std::vector<kvmem::GraphMessageSpan>>();
+            for (uint32_t i = 0; i < nspans; ++i) spans->push_back({span_begin[i], span_end[i], span_end_known[i] != 0});
+            graph.messages = spans;
+        }
+        const auto result = kvmem::propagate_query_scores(std::vector<double>(raw, raw + n), frame, graph, alpha, cross);
+        std::memcpy(out, result.data(), n * sizeof(double));
+    });
+}
+
+// LrfuHistory::preview (kvmem/include/kvmem/lrfu.hpp:57-79) after restoring a
+// committed history `prev` and opening the next round; out = score(i).
+int kvref_lrfu_preview(const double* scores, uint32_t n, const double* prev, uint32_t n_prev, double lambda,
+                       double fraction, double* out) {
+    return guarded([&] {
+        kvmem::LrfuHistory history(lambda, fraction);
+        kvmem::LrfuState state;
+        state.scores = std::make_shared<const std::vector<double>>(prev, prev + n_prev);
+        state.round = 1;
+        state.committed = true;
+        history.restore(state);
+        history.begin_round();
+        history.preview(std::vector<double>(scores, scores + n));
+        for (uint32_t i = 0; i < n; ++i) out[i] = history.score(i);
     });
 }
 

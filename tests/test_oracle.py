@@ -299,3 +299,84 @@ def test_meank_add_oracle_matches_numpy_sequential_sums():
     # a range past the table is refused
     assert O.meank_add(np.zeros((1, 2, 64), np.float32), np.zeros(2, np.uint32), U.make_k(rng, U.F16, 1, 100, 1, 64),
                        U.F16, layers=1, kv_heads=1, dim=64, tok0=60, n=10, page_tokens=32) == 1
+
+
+def _random_graph(rng, n, block, accepted):
+    starts = np.arange(n, dtype=np.uint64) * block
+    rows = []
+    for src in rng.choice(n + 3, size=rng.integers(0, n + 2), replace=False):
+        edges = [(int(rng.integers(0, n + 2)) * block, float(rng.choice([0.0, rng.random()])))
+                 for _ in range(rng.integers(0, 5))]
+        rows.append((int(src) * block, int(rng.integers(0, 3)), edges))
+    spans = None
+    if rng.random() < 0.6:
+        spans = []
+        for _ in range(rng.integers(1, 4)):
+            b = int(rng.integers(0, n * block))
+            spans.append((b, b + int(rng.integers(1, 3 * block + 2)), bool(rng.random() < 0.7)))
+    completed = int(rng.integers(0, n + 1)) * block
+    return starts, dict(block=block, accepted=accepted, completed=completed, rows=rows, spans=spans)
+
+
+def test_propagation_restatement_matches_reference():
+    """propagate_query_scores (graph_recall.cpp:494-551): the C restatement
+    against the compiled reference on random graphs, frames and scores."""
+    if O.ref() is None:
+        pytest.skip("reference library not built")
+    rng = np.random.default_rng(5)
+    for case in range(400):
+        n = int(rng.integers(1, 30))
+        block = int(rng.choice([1, 4, 64]))
+        accepted = n * block
+        starts, graph = _random_graph(rng, n, block, accepted)
+        mask = (rng.random(n) < 0.85).astype(np.uint8)
+        raw = rng.standard_normal(n) * rng.choice([0.01, 1.0, 30.0])
+        raw[rng.random(n) < 0.2] = 0.0
+        alpha = float(rng.choice([0.0, 0.2, 0.4, 1.0]))
+        cross = float(rng.choice([0.25, 1.0, 0.0]))
+        rc_o, out_o = O.propagate_scores(raw, starts, mask, accepted, graph, alpha, cross)
+        rc_r, out_r = O.propagate_scores(raw, starts, mask, accepted, graph, alpha, cross, use_ref=True)
+        assert rc_o == rc_r, (case, rc_o, rc_r)
+        if rc_o == 0:
+            np.testing.assert_allclose(out_o, out_r, rtol=1e-12, atol=1e-12 * max(1.0, np.abs(raw).sum()))
+
+
+def test_propagation_known_answers_and_rejections():
+    """Restated from the reference's graph_recall_test.cpp:160-187: three adjacent
+    one-token pages, page 2 attends to page 0; explicit transport matrix."""
+    starts = np.arange(3, dtype=np.uint64)
+    graph = dict(block=1, accepted=3, completed=3, rows=[(2, 1, [(0, 1.0)])], spans=None)
+    raw = np.array([0.8, -0.2, 0.4])
+    rc, out = O.propagate_scores(raw, starts, np.ones(3, np.uint8), 3, graph, 0.4)
+    assert rc == 0
+    np.testing.assert_allclose(out, [0.8, -0.08, 0.28], atol=1e-12)
+    assert abs(out.sum() - 1.0) < 1e-12
+    rc, out = O.propagate_scores(raw, starts, np.ones(3, np.uint8), 3, graph, 0.0)
+    assert rc == 0 and np.array_equal(out, raw)
+    neg = np.array([-0.8, -0.2, -0.4])
+    rc, out = O.propagate_scores(neg, starts, np.ones(3, np.uint8), 3, graph, 1.0)
+    assert rc == 0 and np.array_equal(out, neg)
+    rc, out = O.propagate_scores(raw, starts, np.array([1, 1, 0], np.uint8), 3, graph, 0.4)
+    np.testing.assert_allclose(out, [0.72, -0.12, 0.4], atol=1e-12)
+    assert O.propagate_scores([0, np.nan, 0], starts, np.ones(3, np.uint8), 3, graph, 0.0)[0] == 1
+    assert O.propagate_scores([0, np.inf, 0], starts, np.ones(3, np.uint8), 3, graph, 0.4)[0] == 1
+    assert O.propagate_scores(raw, starts, np.ones(3, np.uint8), 4, graph, 0.4)[0] == 1  # prefix mismatch
+
+
+def test_lrfu_restatement_matches_reference():
+    """LrfuHistory::preview (lrfu.hpp:57-79): bit-identical to the reference."""
+    if O.ref() is None:
+        pytest.skip("reference library not built")
+    rng = np.random.default_rng(8)
+    for case in range(300):
+        n = int(rng.integers(1, 50))
+        scores = rng.standard_normal(n) * rng.choice([0.001, 1.0, 100.0])
+        scores[rng.random(n) < 0.1] = 0.0
+        prev = rng.standard_normal(int(rng.integers(0, n + 5)))
+        lam = float(rng.choice([0.0, 0.5, 1.0, 0.3]))
+        frac = float(rng.choice([1.0, 0.9, 0.5, 0.01]))
+        rc_o, a = O.lrfu_preview(scores, prev, lam, frac)
+        rc_r, b = O.lrfu_preview(scores, prev, lam, frac, use_ref=True)
+        assert rc_o == rc_r == 0
+        assert np.array_equal(a, b), case
+    assert O.lrfu_preview([1.0, np.nan], [], 0.5, 0.9)[0] == 1
