@@ -307,6 +307,28 @@ int kvm_stagein_wait(kvm_ctx* ctx, void* stream, uint64_t timeout_us);
  * slot_of[rows][pages] (-1 = not resident) and page_of[rows][slots]. */
 int kvm_pool_read(kvm_pool* pool, int32_t* slot_of, int32_t* page_of, void* stream);
 
+/* Raw-K restore transform of stage-in, fused: each item's `tokens` packed K
+ * rows (q8_0 or q4_0, n_head * head_dim elements per row, rows contiguous)
+ * are dequantised, rotated by NeoX RoPE on the first n_rot dims of every head
+ * at position pos0 + token (angle = position * theta[i], i < n_rot / 2),
+ * Walsh-Hadamard transformed over every nrot-element chunk (scaled by
+ * 1/sqrt(nrot); nrot = 0: no transform) and requantised into dst in the same
+ * format. Replaces kvmem_stagein_enqueue_k + kvmem_stagein_flush
+ * (src/adapter/llama-kvmem-stagein.cu:104-234, 499-671, 673-858): one launch
+ * for all items, no f32 scratch, src may be mapped pinned host memory.
+ * items / theta: host arrays; src / dst: device-accessible. type must be
+ * KVM_Q8_0 or KVM_Q4_0 (else KVM_ERR_UNSUPPORTED); nrot in {0, 64, 128, 256,
+ * 512} dividing n_head * head_dim, n_rot even and <= head_dim, head_dim a
+ * multiple of 32, else KVM_ERR_INVALID_ARGUMENT. */
+typedef struct kvm_restore_item {
+    const void* src;
+    void* dst;
+    uint32_t tokens;
+    int32_t pos0;
+} kvm_restore_item;
+int kvm_restore_k(kvm_ctx* ctx, int type, const kvm_restore_item* items, uint32_t n_items, uint32_t n_head,
+                  uint32_t head_dim, uint32_t n_rot, const float* theta, uint32_t nrot, void* stream);
+
 /* -------------------------------------------------------------- Mean-K path */
 
 /* Mean-K producer: per-page K sums kept in HBM. Adds the K rows of tokens

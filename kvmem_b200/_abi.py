@@ -85,6 +85,10 @@ class StepDesc(C.Structure):
 
 
 _vp, _u32, _u64, _i = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int
+class RestoreItem(C.Structure):
+    _fields_ = [("src", C.c_void_p), ("dst", C.c_void_p), ("tokens", C.c_uint32), ("pos0", C.c_int32)]
+
+
 class GraphRow(C.Structure):
     _fields_ = [("source", C.c_uint64), ("samples", C.c_uint64), ("edge_begin", C.c_uint32),
                 ("edge_count", C.c_uint32)]
@@ -125,6 +129,8 @@ SIGNATURES = {
     "kvm_stagein_copies": ([_vp, C.POINTER(Copy), _u32, _u32, _vp], _i),
     "kvm_stagein_wait": ([_vp, _vp, _u64], _i),
     "kvm_pool_read": ([_vp, _vp, _vp, _vp], _i),
+    "kvm_restore_k": ([_vp, _i, C.POINTER(RestoreItem), _u32, _u32, _u32, _u32, C.POINTER(C.c_float), _u32, _vp],
+                      _i),
     "kvm_propagate_scores": ([_vp, _vp, _u32, _vp, _vp, _u64, C.POINTER(Graph), C.c_double, C.c_double, _vp, _vp],
                              _i),
     "kvm_lrfu_preview": ([_vp, _vp, _u32, _vp, _u32, C.c_double, C.c_double, _vp, _vp], _i),

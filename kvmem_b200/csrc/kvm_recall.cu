@@ -15,6 +15,7 @@
 #include "meank.cuh"
 #include "page_norm.cuh"
 #include "post.cuh"
+#include "restore.cuh"
 #include "select.cuh"
 #include "shard.cuh"
 #include "stagein.cuh"
@@ -735,6 +736,59 @@ int kvm_stagein_wait(kvm_ctx* c, void* stream, uint64_t timeout_us) {
         if (uint64_t(us) >= timeout_us) return KVM_ERR_TIMEOUT;
     }
     return kvm_ctx_status(c, stream);
+}
+
+int kvm_restore_k(kvm_ctx* c, int type, const kvm_restore_item* items, uint32_t n_items, uint32_t n_head,
+                  uint32_t head_dim, uint32_t n_rot, const float* theta, uint32_t nrot, void* stream) {
+    if (!c || (n_items && !items)) return KVM_ERR_INVALID_ARGUMENT;
+    if (type != KVM_Q8_0 && type != KVM_Q4_0) return KVM_ERR_UNSUPPORTED;
+    if (!n_head || !head_dim || head_dim % 32 || n_rot % 2 || n_rot > head_dim || (n_rot && !theta))
+        return KVM_ERR_INVALID_ARGUMENT;
+    const uint64_t n_embd = uint64_t(n_head) * head_dim;
+    if (nrot && ((nrot != 64 && nrot != 128 && nrot != 256 && nrot != 512) || n_embd % nrot))
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (n_embd > 16384) return KVM_ERR_LENGTH;
+    std::vector<RestoreItem> its(std::max<uint32_t>(n_items, 1));
+    std::vector<uint64_t> base(n_items + 1, 0);
+    for (uint32_t i = 0; i < n_items; ++i) {
+        if (!items[i].src || !items[i].dst) return KVM_ERR_INVALID_ARGUMENT;
+        its[i] = RestoreItem{static_cast<const uint8_t*>(items[i].src), static_cast<uint8_t*>(items[i].dst),
+                             items[i].tokens, items[i].pos0};
+        base[i + 1] = base[i] + items[i].tokens;
+    }
+    if (!base[n_items]) return KVM_OK;
+    const uint32_t half = n_rot / 2;
+    const size_t o_items = 0, o_base = align256(its.size() * sizeof(RestoreItem)),
+                 o_theta = o_base + align256(base.size() * 8), total = o_theta + align256(std::max<uint32_t>(half, 1) * 4);
+    std::vector<uint8_t> host(total, 0);
+    std::memcpy(host.data() + o_items, its.data(), its.size() * sizeof(RestoreItem));
+    std::memcpy(host.data() + o_base, base.data(), base.size() * 8);
+    if (half) std::memcpy(host.data() + o_theta, theta, half * 4);
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_TRY(ensure_aux(c, total));
+    auto* a = static_cast<uint8_t*>(c->aux);
+    KVM_CUDA(cudaMemcpyAsync(a, host.data(), total, cudaMemcpyHostToDevice, s));
+    const float scale = nrot ? 1.0f / std::sqrt(float(nrot)) : 1.0f;
+    const uint32_t grid = uint32_t(std::min<uint64_t>(base[n_items], uint64_t(c->num_sms) * 8));
+    const size_t smem = n_embd * 4;
+    const auto* di = reinterpret_cast<const RestoreItem*>(a + o_items);
+    const auto* db = reinterpret_cast<const uint64_t*>(a + o_base);
+    const auto* dt = reinterpret_cast<const float*>(a + o_theta);
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaFuncSetAttribute(restore_k_kernel<KVM_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaFuncSetAttribute(restore_k_kernel<KVM_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    });
+    if (type == KVM_Q8_0)
+        restore_k_kernel<KVM_Q8_0><<<grid, kRestoreThreads, smem, s>>>(di, n_items, db, n_head, head_dim, n_rot, dt,
+                                                                       nrot, scale);
+    else
+        restore_k_kernel<KVM_Q4_0><<<grid, kRestoreThreads, smem, s>>>(di, n_items, db, n_head, head_dim, n_rot, dt,
+                                                                       nrot, scale);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
 }
 
 int kvm_propagate_scores(kvm_ctx* c, const float* raw, uint32_t n, const uint64_t* starts,

@@ -148,6 +148,17 @@ class RecallContext:
         A.check(rc, "kvm_select_topk")
         return out_ids, out_n
 
+    def restore_k(self, ktype: int, items: Sequence[tuple], *, n_head: int, head_dim: int, n_rot: int = 0,
+                  theta: Optional[Sequence[float]] = None, nrot: int = 0, stream=None) -> None:
+        """items: (src_ptr, dst_ptr, tokens, pos0) -> kvm_restore_k (raw-K restore transform)."""
+        arr = (A.RestoreItem * max(1, len(items)))()
+        for i, (src, dst, tokens, pos0) in enumerate(items):
+            arr[i].src, arr[i].dst, arr[i].tokens, arr[i].pos0 = src, dst, tokens, pos0
+        th = (C.c_float * max(1, n_rot // 2))(*(list(theta or [])[: n_rot // 2]))
+        rc = self.lib.kvm_restore_k(self.h, ktype, arr, len(items), n_head, head_dim, n_rot, th, nrot,
+                                    _stream_ptr(stream))
+        A.check(rc, "kvm_restore_k")
+
     @staticmethod
     def make_graph(graph: dict):
         """kvm_graph from dict(block, accepted, completed, rows=[(source, samples, [(target, mass), ...])],

@@ -292,6 +292,116 @@ int kvo_lrfu_preview(const double* scores, uint32_t n, const double* prev, uint3
 }
 
 /*
+ * Raw-K restore transform — restates the reference's stage-in kernels
+ * (src/adapter/llama-kvmem-stagein.cu: dequant_q8_0 / dequant_q4_0 :134-160,
+ * rope_neox_kernel :162-180, fwht_kernel :104-130 with scale 1/sqrtf(nrot),
+ * quant_q8_0 / quant_q4_0 :182-234) for `nt` contiguous rows of n_head*dim
+ * elements, one f32 operation at a time (this file is built without
+ * floating-point contraction). Angles use sinf / cosf. Returns 1 for an
+ * invalid shape.
+ */
+static float h2f(const uint8_t* b) { uint16_t h; memcpy(&h, b, 2); return (float)kvo_half_to_double(h); }
+
+static uint16_t f2h_rn(float f) {
+    /* float -> IEEE half, round to nearest even (values here are finite). */
+    uint32_t x; memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    int32_t exp = (int32_t)((x >> 23) & 255) - 127 + 15;
+    uint32_t man = x & 0x7fffffu;
+    if (((x >> 23) & 255) == 0 && man == 0) return (uint16_t)sign;
+    if (exp >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (exp <= 0) {
+        if (exp < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        const uint32_t shift = (uint32_t)(14 - exp);
+        uint32_t half_man = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1), halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (half_man & 1))) ++half_man;
+        return (uint16_t)(sign | half_man);
+    }
+    uint32_t half_man = man >> 13;
+    const uint32_t rem = man & 0x1fffu;
+    uint32_t h = sign | ((uint32_t)exp << 10) | half_man;
+    if (rem > 0x1000u || (rem == 0x1000u && (half_man & 1))) ++h;
+    return (uint16_t)h;
+}
+
+int kvo_restore_k(int type, const uint8_t* src, uint8_t* dst, uint32_t nt, uint32_t n_head, uint32_t dim,
+                  uint32_t n_rot, int32_t pos0, const float* theta, uint32_t nrot) {
+    if (type != KVO_Q8_0 && type != KVO_Q4_0) return 1;
+    const uint32_t n_embd = n_head * dim, nblk = n_embd / 32, kb = type == KVO_Q8_0 ? 34 : 18;
+    if (!n_embd || dim % 32 || n_rot % 2 || n_rot > dim) return 1;
+    if (nrot && ((nrot != 64 && nrot != 128 && nrot != 256 && nrot != 512) || n_embd % nrot)) return 1;
+    float* row = (float*)malloc(n_embd * sizeof(float));
+    if (!row) return 2;
+    const float scale = nrot ? 1.0f / sqrtf((float)nrot) : 1.0f;
+    for (uint32_t t = 0; t < nt; ++t) {
+        const uint8_t* s = src + (uint64_t)t * nblk * kb;
+        uint8_t* o = dst + (uint64_t)t * nblk * kb;
+        for (uint32_t e = 0; e < n_embd; ++e) {
+            const uint8_t* b = s + (e / 32) * kb;
+            const uint32_t j = e % 32;
+            const float code = type == KVO_Q8_0 ? (float)(int8_t)b[2 + j]
+                                                : (float)(((b[2 + j % 16] >> (j < 16 ? 0 : 4)) & 15) - 8);
+            row[e] = code * h2f(b);
+        }
+        if (n_rot) {
+            const uint32_t half = n_rot / 2;
+            const float pos = (float)(int32_t)(pos0 + (int32_t)t);
+            for (uint32_t h = 0; h < n_head; ++h)
+                for (uint32_t i = 0; i < half; ++i) {
+                    const float ang = pos * theta[i];
+                    const float sn = sinf(ang), cs = cosf(ang);
+                    float* r = row + h * dim;
+                    const float x0 = r[i], x1 = r[i + half];
+                    const float a0 = x0 * cs, a1 = x1 * sn, b0 = x0 * sn, b1 = x1 * cs;
+                    r[i] = a0 - a1;
+                    r[i + half] = b0 + b1;
+                }
+        }
+        if (nrot) {
+            for (uint32_t e = 0; e < n_embd; ++e) row[e] = row[e] * scale;
+            for (uint32_t c0 = 0; c0 < n_embd; c0 += nrot)
+                for (uint32_t h = 1; h < nrot; h *= 2)
+                    for (uint32_t i = 0; i < nrot; i += 2 * h)
+                        for (uint32_t j = 0; j < h; ++j) {
+                            const float a = row[c0 + i + j], b = row[c0 + i + j + h];
+                            row[c0 + i + j] = a + b;
+                            row[c0 + i + j + h] = a - b;
+                        }
+        }
+        for (uint32_t bi = 0; bi < nblk; ++bi) {
+            const float* x = row + bi * 32;
+            uint8_t* b = o + bi * kb;
+            if (type == KVO_Q8_0) {
+                float amax = 0.0f;
+                for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[j]));
+                const float d = amax / 127.0f, id = d != 0.0f ? 1.0f / d : 0.0f;
+                const uint16_t hd = f2h_rn(d);
+                memcpy(b, &hd, 2);
+                for (int j = 0; j < 32; ++j) b[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+            } else {
+                float amax = 0.0f, vmax = 0.0f;
+                for (int j = 0; j < 32; ++j)
+                    if (amax < fabsf(x[j])) { amax = fabsf(x[j]); vmax = x[j]; }
+                const float d = vmax / -8.0f, id = d != 0.0f ? 1.0f / d : 0.0f;
+                const uint16_t hd = f2h_rn(d);
+                memcpy(b, &hd, 2);
+                for (int j = 0; j < 16; ++j) {
+                    const float x0 = x[j] * id, x1 = x[j + 16] * id;
+                    int xi0 = (int)(x0 + 8.5f), xi1 = (int)(x1 + 8.5f);
+                    if (xi0 > 15) xi0 = 15;
+                    if (xi1 > 15) xi1 = 15;
+                    b[2 + j] = (uint8_t)((xi0 & 15) | ((xi1 & 15) << 4));
+                }
+            }
+        }
+    }
+    free(row);
+    return 0;
+}
+
+/*
  * Per-token page mass, FP64 — restates the reference's dense oracle
  * AttentionSampler::qualify (src/adapter/llama-kvmem-attention.cpp:61-94):
  *   logit_t = scale * <q_rh, K_t,kvh(h)>   (FP64 dot of decoded operands)

@@ -78,6 +78,8 @@ def lib():
         L.kvo_meank_add.argtypes = [_f32p, _u32p, C.c_uint32, C.c_void_p, C.c_int, C.c_uint64, C.c_uint64,
                                     C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32,
                                     C.c_uint32]
+        L.kvo_restore_k.argtypes = [C.c_int, _u8p, _u8p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                    C.c_int32, _f32p, C.c_uint32]
         L.kvo_propagate_scores.argtypes = _PROPAGATE_ARGS
         L.kvo_lrfu_preview.argtypes = _LRFU_ARGS
         L.kvo_decode.argtypes = [C.c_int, C.c_void_p, C.c_uint32]
@@ -293,3 +295,13 @@ def lrfu_preview(scores, prev, lam=0.5, fraction=0.9, use_ref=False):
     fn = ref().kvref_lrfu_preview if use_ref else lib().kvo_lrfu_preview
     rc = fn(scores if n else np.zeros(1), n, prev, n_prev, lam, fraction, out)
     return int(rc), out[:n]
+
+
+def restore_k(ktype: int, src: np.ndarray, *, tokens: int, n_head: int, dim: int, n_rot: int = 0, pos0: int = 0,
+              theta=None, nrot: int = 0):
+    """Raw-K restore transform of `tokens` packed rows -> (rc, packed output bytes)."""
+    src = np.ascontiguousarray(src, np.uint8).reshape(-1)
+    dst = np.zeros_like(src)
+    th = np.ascontiguousarray(list(theta) if theta is not None and len(theta) else [0.0], np.float32)
+    rc = lib().kvo_restore_k(ktype, src, dst, tokens, n_head, dim, n_rot, pos0, th, nrot)
+    return int(rc), dst

@@ -380,3 +380,29 @@ def test_lrfu_restatement_matches_reference():
         assert rc_o == rc_r == 0
         assert np.array_equal(a, b), case
     assert O.lrfu_preview([1.0, np.nan], [], 0.5, 0.9)[0] == 1
+
+
+@pytest.mark.parametrize("kt", [U.Q8_0, U.Q4_0])
+def test_restore_k_oracle_matches_numpy(kt):
+    """Raw-K restore transform (stagein.cu:104-234): dequant -> NeoX RoPE -> FWHT ->
+    requant. Bit-exact against the numpy restatement without RoPE; with RoPE the
+    sin / cos of the two libraries may differ in the last bits, so requantised
+    values stay within one quantisation step and nearly all codes agree."""
+    rng = np.random.default_rng(12 + kt)
+    tokens, n_head, dim = 9, 4, 128
+    theta = (10000.0 ** (-np.arange(0, dim, 2) / dim)).astype(np.float32)
+    kb = U.make_k(rng, kt, 1, tokens, n_head, dim).reshape(-1)
+    for n_rot, nrot in ((0, 0), (0, 64), (0, 128), (0, 512), (dim, 256), (64, 128), (dim, 0)):
+        rc, got = O.restore_k(kt, kb, tokens=tokens, n_head=n_head, dim=dim, n_rot=n_rot, pos0=1000, theta=theta,
+                              nrot=nrot)
+        assert rc == 0
+        exp = U.restore_k_numpy(kt, kb, tokens, n_head, dim, n_rot, 1000, theta, nrot)
+        if n_rot == 0:
+            assert np.array_equal(got, exp), (n_rot, nrot)
+        else:
+            a = U.decode_rows_f32(got.reshape(tokens * n_head, -1), kt, dim)
+            b = U.decode_rows_f32(exp.reshape(tokens * n_head, -1), kt, dim)
+            step = np.abs(U.decode_rows_f32(exp.reshape(tokens * n_head, -1), kt, dim)).max() / (7 if kt == U.Q4_0 else 100)
+            assert np.abs(a - b).max() <= step
+            assert np.mean(got == exp) > 0.97
+    assert O.restore_k(kt, kb, tokens=tokens, n_head=n_head, dim=dim, nrot=96)[0] == 1

@@ -106,3 +106,53 @@ def decode_rows_f32(kb: np.ndarray, ktype: int, dim: int) -> np.ndarray:
                 codes = ((low | (high << 4)) - 16).astype(np.float32)
         out = (codes * scale[..., None]).astype(np.float32).reshape(-1, dim)
     return out.reshape(*lead, dim)
+
+
+def restore_k_numpy(ktype: int, src: np.ndarray, tokens: int, n_head: int, dim: int, n_rot: int = 0, pos0: int = 0,
+                    theta=None, nrot: int = 0) -> np.ndarray:
+    """Independent numpy restatement of the raw-K restore transform (float32
+    arithmetic in the reference's order; sin / cos from numpy in float32)."""
+    n_embd = n_head * dim
+    row = decode_rows_f32(np.ascontiguousarray(src).reshape(tokens, -1), ktype, n_embd).astype(np.float32)
+    if n_rot:
+        half = n_rot // 2
+        th = np.asarray(theta[:half], np.float32)
+        pos = (np.arange(tokens, dtype=np.int64) + pos0).astype(np.float32)
+        ang = (pos[:, None] * th[None, :]).astype(np.float32)
+        sn, cs = np.sin(ang).astype(np.float32), np.cos(ang).astype(np.float32)
+        r = row.reshape(tokens, n_head, dim)
+        x0, x1 = r[:, :, :half].copy(), r[:, :, half:n_rot].copy()
+        r[:, :, :half] = (x0 * cs[:, None, :]).astype(np.float32) - (x1 * sn[:, None, :]).astype(np.float32)
+        r[:, :, half:n_rot] = (x0 * sn[:, None, :]).astype(np.float32) + (x1 * cs[:, None, :]).astype(np.float32)
+        row = r.reshape(tokens, n_embd)
+    if nrot:
+        row = (row * np.float32(1.0 / np.sqrt(np.float32(nrot)))).astype(np.float32)
+        c = row.reshape(tokens, n_embd // nrot, nrot)
+        h = 1
+        while h < nrot:
+            c = c.reshape(tokens, n_embd // nrot, nrot // (2 * h), 2, h)
+            a, b = c[:, :, :, 0, :].copy(), c[:, :, :, 1, :].copy()
+            c[:, :, :, 0, :], c[:, :, :, 1, :] = a + b, a - b
+            c = c.reshape(tokens, n_embd // nrot, nrot)
+            h *= 2
+        row = c.reshape(tokens, n_embd)
+    blocks = row.reshape(tokens, n_embd // 32, 32)
+    out = np.zeros((tokens, n_embd // 32, BLOCK_BYTES[ktype]), np.uint8)
+    if ktype == Q8_0:
+        d = (np.abs(blocks).max(axis=-1) / np.float32(127)).astype(np.float32)
+        inv = np.where(d != 0, (np.float32(1) / np.where(d != 0, d, 1)).astype(np.float32), 0).astype(np.float32)
+        x = (blocks * inv[..., None]).astype(np.float32)
+        ax = np.abs(x)
+        q = np.floor(ax)
+        q = (q + ((ax - q) >= 0.5)) * np.sign(x)
+        out[..., 0:2] = d.astype(np.float16)[..., None].view(np.uint8).reshape(tokens, -1, 2)
+        out[..., 2:] = q.astype(np.int8).view(np.uint8)
+    else:
+        idx = np.abs(blocks).argmax(axis=-1)  # first of the largest magnitudes
+        vmax = np.take_along_axis(blocks, idx[..., None], -1)[..., 0]
+        d = (vmax / np.float32(-8)).astype(np.float32)
+        inv = np.where(d != 0, (np.float32(1) / np.where(d != 0, d, 1)).astype(np.float32), 0).astype(np.float32)
+        xi = np.minimum(np.trunc((blocks * inv[..., None]).astype(np.float32) + np.float32(8.5)), 15).astype(np.int32)
+        out[..., 0:2] = d.astype(np.float16)[..., None].view(np.uint8).reshape(tokens, -1, 2)
+        out[..., 2:] = ((xi[..., :16] & 15) | ((xi[..., 16:] & 15) << 4)).astype(np.uint8)
+    return out.reshape(-1)
