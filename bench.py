@@ -540,6 +540,35 @@ def run_ours(args, world, rank, local):
         g_ms.append(ev0.elapsed_time(ev1))
     gather_ms = statistics.median(g_ms)
 
+    # Stage-out (harvest) of one filled block per layer: its K and V bytes from the
+    # device cache into the two 32 MiB pinned slots in turn -> D2H link GB/s.
+    so = K.StageOut(local)
+    out_bytes = L * (page_k + page_v)
+
+    def harvest():
+        pending = -1
+        for l in range(L):
+            for cache, pb in ((cache_k, page_k), (cache_v, page_v)):
+                src = cache.data_ptr() + l * slots * pb
+                if so.enqueue(src, pb) is None:
+                    slot = so.submit(ctas=args.stage_ctas)
+                    so.wait(pending)
+                    pending = slot
+                    so.enqueue(src, pb)
+        slot = so.submit(ctas=args.stage_ctas)
+        so.wait(pending)
+        so.wait(slot)
+
+    harvest()
+    o_ms = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        harvest()
+        o_ms.append((time.perf_counter() - t0) * 1e3)
+    so.close()
+    stageout_ms = statistics.median(o_ms)
+
     # Dominant kernel alone: the page log-sum-exp pass over all layers (+ its tiny normaliser).
     kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
     for _ in range(2):
@@ -622,6 +651,9 @@ def run_ours(args, world, rank, local):
                  "note": "every selected page staged every step (force_reload)"},
         "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
                     "ctas": args.stage_ctas, "link": "PCIe Gen5 x16 (mapped pinned host reads)"},
+        "stageout": {"ms": stageout_ms, "bytes": out_bytes, "GB/s": out_bytes / (stageout_ms * 1e-3) / 1e9,
+                     "what": "K+V of one block per layer into two 32 MiB pinned slots in turn (host clock, "
+                             "submit to last slot observed)", "ctas": args.stage_ctas},
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)

@@ -303,6 +303,56 @@ int kvm_stagein_copies(kvm_ctx* ctx, const kvm_copy* ops, uint32_t n, uint32_t c
  * (replaces kvmem_stagein_sync_checked, src/adapter/llama-kvmem-stagein.cu:656). */
 int kvm_stagein_wait(kvm_ctx* ctx, void* stream, uint64_t timeout_us);
 
+/* ----------------------------------------------------------------- stage-out */
+
+/* Device page bytes (K / V rows of a filled block) gathered into one of two
+ * pinned host slots, alternately, so the host writes one batch into its store
+ * while the GPU fills the other. Replaces the reverse slab of
+ * src/adapter/llama-kvmem-stagein.h:48-55 (stagein.cu:883-1004), whose gather
+ * kernel packs the regions into a 32 MiB device buffer and then copies it to
+ * the slot with one D2H memcpy: here one kernel writes straight into the
+ * mapped pinned slot. A handle is owned by one execution state, like a
+ * kvm_ctx. */
+typedef struct kvm_stageout kvm_stageout;
+
+/* Two mapped pinned slots of slot_bytes (a multiple of 16; the reference uses
+ * 32 MiB) and room for max_items regions per batch (the reference's
+ * GATHER_MAX is 8192). */
+int kvm_stageout_create(int device, uint64_t slot_bytes, uint32_t max_items, kvm_stageout** out);
+int kvm_stageout_destroy(kvm_stageout* so);
+
+/* Queues nbytes of device memory at dev_src for the next submit and returns
+ * its byte offset in the slot (kvmem_stageout_enqueue, stagein.cu:883).
+ * Offsets are rounded up to 16 bytes (the reference packs back to back), and
+ * kvm_stageout_used() is the next item's offset, so a caller that reads the
+ * offset from kvm_stageout_used() before enqueueing, as the reference's
+ * harvest does (src/adapter/llama-memory-kvmem.cpp:4033-4036), finds its
+ * bytes there. KVM_ERR_LENGTH when the batch is full (bytes or items): submit
+ * and retry, as the reference's caller flushes its slab. */
+int kvm_stageout_enqueue(kvm_stageout* so, const void* dev_src, uint64_t nbytes, uint64_t* offset);
+uint64_t kvm_stageout_used(const kvm_stageout* so);
+
+/* Enqueues the gather of the queued regions into the current slot on
+ * `stream`, records the slot's event and switches to the other slot
+ * (kvmem_stageout_submit, stagein.cu:907-973). *slot = the slot filled, or
+ * -1 when nothing was queued. If the slot's previous batch is still in
+ * flight, waits for it first (bounded: KVM_ERR_TIMEOUT after 30 s). `ctas`
+ * bounds the SMs the gather occupies (0 = 32). */
+int kvm_stageout_submit(kvm_stageout* so, uint32_t ctas, void* stream, int* slot);
+
+/* Bounded host wait for a submitted slot (kvmem_stageout_wait,
+ * stagein.cu:975-990): KVM_OK once its bytes are in host memory, KVM_OK for
+ * slot -1, KVM_ERR_TIMEOUT after timeout_us. */
+int kvm_stageout_wait(kvm_stageout* so, int slot, uint64_t timeout_us);
+
+/* Host address of slot 0 or 1 (kvmem_stageout_slot_base, stagein.cu:992),
+ * NULL otherwise. */
+const uint8_t* kvm_stageout_slot_base(const kvm_stageout* so, int slot);
+
+/* Drops the queued, not yet submitted regions (kvmem_stageout_clear,
+ * stagein.cu:999-1004). */
+int kvm_stageout_clear(kvm_stageout* so);
+
 /* Pool introspection (tests): copies the device tables to host arrays
  * slot_of[rows][pages] (-1 = not resident) and page_of[rows][slots]. */
 int kvm_pool_read(kvm_pool* pool, int32_t* slot_of, int32_t* page_of, void* stream);

@@ -128,6 +128,14 @@ SIGNATURES = {
     "kvm_stagein_pool": ([_vp, _vp, C.POINTER(StageLayout), _u32, _vp], _i),
     "kvm_stagein_copies": ([_vp, C.POINTER(Copy), _u32, _u32, _vp], _i),
     "kvm_stagein_wait": ([_vp, _vp, _u64], _i),
+    "kvm_stageout_create": ([_i, _u64, _u32, C.POINTER(C.c_void_p)], _i),
+    "kvm_stageout_destroy": ([_vp], _i),
+    "kvm_stageout_enqueue": ([_vp, _vp, _u64, C.POINTER(C.c_uint64)], _i),
+    "kvm_stageout_used": ([_vp], _u64),
+    "kvm_stageout_submit": ([_vp, _u32, _vp, C.POINTER(C.c_int)], _i),
+    "kvm_stageout_wait": ([_vp, _i, _u64], _i),
+    "kvm_stageout_slot_base": ([_vp, _i], _vp),
+    "kvm_stageout_clear": ([_vp], _i),
     "kvm_pool_read": ([_vp, _vp, _vp, _vp], _i),
     "kvm_restore_k": ([_vp, _i, C.POINTER(RestoreItem), _u32, _u32, _u32, _u32, C.POINTER(C.c_float), _u32, _vp],
                       _i),

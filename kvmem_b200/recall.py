@@ -310,6 +310,66 @@ class ResidencyPool:
         return slot_of, page_of
 
 
+class StageOut:
+    """Double-buffered stage-out (kvm_stageout): device regions gathered into
+    two pinned host slots in turn. Method names follow the reference's
+    kvmem_stageout_* functions (src/adapter/llama-kvmem-stagein.h:50-55);
+    failures raise KvmError instead of returning false / -1."""
+
+    SLAB = 32 << 20  # the reference's slot size
+    GATHER_MAX = 8192
+
+    def __init__(self, device: int = 0, slot_bytes: int = SLAB, max_items: int = GATHER_MAX):
+        self.lib = A.load()
+        self.slot_bytes = slot_bytes
+        h = C.c_void_p()
+        A.check(self.lib.kvm_stageout_create(device, slot_bytes, max_items, C.byref(h)), "kvm_stageout_create")
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.kvm_stageout_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def enqueue(self, dev_ptr: int, nbytes: int) -> Optional[int]:
+        """Queue a device region; its slot offset, or None when the batch is full."""
+        off = C.c_uint64()
+        rc = self.lib.kvm_stageout_enqueue(self.h, dev_ptr, nbytes, C.byref(off))
+        if rc == A.ERR_LENGTH:
+            return None
+        A.check(rc, "kvm_stageout_enqueue")
+        return off.value
+
+    def used(self) -> int:
+        return int(self.lib.kvm_stageout_used(self.h))
+
+    def submit(self, ctas: int = 0, stream=None) -> int:
+        slot = C.c_int(-1)
+        A.check(self.lib.kvm_stageout_submit(self.h, ctas, _stream_ptr(stream), C.byref(slot)), "kvm_stageout_submit")
+        return slot.value
+
+    def wait(self, slot: int, timeout_s: float = 30.0) -> None:
+        A.check(self.lib.kvm_stageout_wait(self.h, slot, int(timeout_s * 1e6)), "kvm_stageout_wait")
+
+    def slot_view(self, slot: int, offset: int, nbytes: int):
+        """numpy uint8 view of bytes [offset, offset + nbytes) of a slot (no copy)."""
+        import numpy as np
+        base = self.lib.kvm_stageout_slot_base(self.h, slot)
+        if not base or offset + nbytes > self.slot_bytes:
+            raise ValueError("slot range")
+        buf = (C.c_uint8 * nbytes).from_address(base + offset)
+        return np.frombuffer(buf, dtype=np.uint8)
+
+    def clear(self) -> None:
+        A.check(self.lib.kvm_stageout_clear(self.h), "kvm_stageout_clear")
+
+
 def stage_layout(planes: Sequence[dict]) -> A.StageLayout:
     """planes: up to two dicts with host_base, host_row_stride, host_page_stride,
     dev_base, dev_row_stride, dev_slot_stride, bytes."""

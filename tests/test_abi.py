@@ -14,7 +14,7 @@ def declared_functions():
         if h.endswith(".h"):
             src = open(os.path.join(ROOT, "include", h)).read()
             src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-            names += re.findall(r"^\s*(?:int|size_t|uint64_t)\s+(kvm_\w+)\s*\(", src, flags=re.M)
+            names += re.findall(r"^\s*(?:int|size_t|uint64_t|const\s+uint8_t\s*\*)\s*(kvm_\w+)\s*\(", src, flags=re.M)
     return names
 
 
