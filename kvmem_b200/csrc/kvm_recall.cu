@@ -276,8 +276,12 @@ size_t lse_bytes(const kvm_score_desc* d, uint32_t layers, uint32_t rows) {
 int launch_lse_mma(kvm_ctx* c, int kt, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
     switch (kt) {
         case KVM_F16: return launch_lse_mma_kt<KVM_F16>(c, p, kk, smem, s);
-        case KVM_Q8_0: return launch_lse_mma_kt<KVM_Q8_0>(c, p, kk, smem, s);
-        case KVM_Q4_0: return launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s);
+        case KVM_Q8_0:
+            return scorer_is("mma_generic") ? launch_lse_mma_kt<KVM_Q8_0>(c, p, kk, smem, s)
+                                            : launch_lse_q_kt<KVM_Q8_0>(c, p, kk, smem, s);
+        case KVM_Q4_0:
+            return scorer_is("mma_generic") ? launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s)
+                                            : launch_lse_q_kt<KVM_Q4_0>(c, p, kk, smem, s);
         default: return KVM_ERR_UNSUPPORTED;
     }
 }

@@ -1,0 +1,329 @@
+// Per-token page mass, first pass, for quantised keys (q8_0 / q4_0) on the
+// tensor cores: the page log-sum-exp of up to 8 query vectors that share a KV
+// head. Same mathematics as page_lse_mma_kernel (page_mass_mma.cuh): the
+// vectors are the A operand of mma.sync m16n8k16 as fp16 hi (rows 0..7) and lo
+// (rows 8..15) parts after an exact power-of-two prescale, the codes of one
+// 32-element block of 8 tokens are the B operand (exact in fp16), and each
+// block's partial dots are scaled by the token's block scale in fp32.
+//
+// What differs is the instruction stream of the consumer warps, which sets
+// this kernel's speed (the K bytes arrive faster than the SMs can fold them):
+//  * the KV-head count, block geometry and row bytes are template constants,
+//    each warp serves one KV head and a fixed set of octets, and its
+//    shared-memory addresses advance by a constant per octet (no division or
+//    parameter reload per octet);
+//  * blocks whose codes start 2 bytes off a 32-bit word (every other block:
+//    the 34- / 18-byte blocks alternate) are read as the aligned words that
+//    hold codes 2..29 (q8_0; nibble bytes 2..13 for q4_0) plus one word
+//    spliced (byte permute) from the halves of the block's first and last
+//    words: lane c holds the aligned words 1+c and 5+c, lane 3's second word
+//    is {30, 31, 0, 1}. The mma's k index follows the same lane-dependent
+//    order for the queries, so every element is counted once;
+//  * a chunk that is fully visible, unmasked and without softcap takes a
+//    branchless online (max, sum) update per token pair; everything else
+//    takes the general per-token path.
+#pragma once
+#include "page_mass_mma.cuh"
+
+namespace kvmb {
+
+// Element (0..31) of a block held in position i (0..7) of lane c's B
+// fragment for block kk: positions 0..3 form k-step 0, 4..7 k-step 1.
+template <int KT>
+__host__ __device__ constexpr int q_dim(int kk, int c, int i) {
+    const bool aligned = (kk & 1) != 0;  // codes start on a word boundary
+    if constexpr (KT == KVM_Q8_0) {
+        if (aligned) return i < 4 ? 4 * c + i : 16 + 4 * c + (i - 4);
+        if (i < 4) return 4 * c + 2 + i;
+        if (c < 3) return 4 * c + 18 + (i - 4);
+        return (i - 4) < 2 ? 30 + (i - 4) : (i - 4) - 2;
+    } else {  // q4_0: byte j holds elements j (low nibble) and 16 + j (high nibble)
+        const int j = i & 3;
+        int byte;
+        if (aligned) byte = 4 * c + j;
+        else if (c < 3) byte = 4 * c + 2 + j;
+        else byte = j < 2 ? 14 + j : j - 2;
+        return i < 4 ? byte : 16 + byte;
+    }
+}
+
+// B fragments of block kk for this lane from its token's row: b[0..1] k-step 0, b[2..3] k-step 1.
+template <int KT, int kk>
+__device__ __forceinline__ void q_b_frag(const uint8_t* row, int c, uint32_t splice, uint32_t* b) {
+    constexpr int kBlock = KT == KVM_Q8_0 ? 34 : 18;
+    const uint8_t* blk = row + kBlock * kk;
+    if constexpr (KT == KVM_Q8_0) {
+        uint32_t w0, w1;
+        if constexpr (kk & 1) {
+            w0 = *reinterpret_cast<const uint32_t*>(blk + 2 + 4 * c);
+            w1 = *reinterpret_cast<const uint32_t*>(blk + 18 + 4 * c);
+        } else {
+            w0 = *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * c);
+            const uint32_t r = *reinterpret_cast<const uint32_t*>(blk + 20 + 4 * c);
+            const uint32_t h = *reinterpret_cast<const uint32_t*>(blk);
+            w1 = __byte_perm(r, h, splice);
+        }
+        s8x4_to_h2(w0, b[0], b[1]);
+        s8x4_to_h2(w1, b[2], b[3]);
+    } else {
+        uint32_t w;
+        if constexpr (kk & 1) {
+            w = *reinterpret_cast<const uint32_t*>(blk + 2 + 4 * c);
+        } else {
+            const uint32_t r = *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * c);
+            const uint32_t h = *reinterpret_cast<const uint32_t*>(blk);
+            w = __byte_perm(r, h, splice);
+        }
+        u4x4_to_h2(w & 0x0F0F0F0Fu, 0x6408 /* 1032 */, b[0], b[1]);
+        u4x4_to_h2((w >> 4) & 0x0F0F0F0Fu, 0x6408, b[2], b[3]);
+    }
+}
+
+// KK = head_dim / 32 blocks per row; KVH = KV heads (1, 2, 4 or 8).
+template <int KT, int KK, int KVH, bool MASK>
+__global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LseParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int NW = kLseConsumerWarps;
+    constexpr int WPH = NW / KVH;  // warps per KV head
+    constexpr int kBlock = KT == KVM_Q8_0 ? 34 : 18;
+    constexpr uint32_t kRow = uint32_t(kBlock * KK);
+    static_assert(NW % KVH == 0, "warps per KV head");
+    const uint32_t S = P.stages;
+    uint8_t* stages = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.stage_stride);
+    uint64_t* empty = full + kMmaMaxStages;
+    float* red_m = reinterpret_cast<float*>(empty + kMmaMaxStages);  // [2][NW][8]
+    float* red_s = red_m + 2 * NW * 8;
+    int* abort_flag = reinterpret_cast<int*>(red_s + 2 * NW * 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const uint32_t units = P.layers * P.pages;
+    const uint32_t per_cta = (units + gridDim.x - 1) / gridDim.x;
+    const uint32_t unit_begin = min(units, blockIdx.x * per_cta), unit_end = min(units, unit_begin + per_cta);
+
+    if (warp == NW) {
+        if (lane == 0) {
+            const uint64_t policy = policy_evict_first();
+            uint32_t s = 0, phase = 0, issued = 0;
+            bool wrapped = false;
+            for (uint32_t unit = unit_begin; unit < unit_end; ++unit) {
+                const uint32_t l = unit / P.pages, p = unit - l * P.pages;
+                const uint8_t* src = P.k + l * P.k_layer + uint64_t(p) * P.page_bytes;
+                for (uint32_t c = 0; c < P.chunks; ++c) {
+                    if (!*reinterpret_cast<volatile int*>(abort_flag)) {
+                        if (wrapped && !mbar_wait(&empty[s], phase ^ 1)) {
+                            record_error(P.status, KVM_ERR_TIMEOUT, 4);
+                            *reinterpret_cast<volatile int*>(abort_flag) = 1;
+                        } else {
+                            mbar_arrive_expect_tx(&full[s], P.chunk_bytes);
+                            uint8_t* dst = stages + s * P.stage_stride;
+                            const uint8_t* from = src + uint64_t(c) * P.chunk_bytes;
+                            for (uint32_t t = 0; t < P.tpc; ++t)
+                                bulk_g2s(dst + t * P.slot_stride, from + uint64_t(t) * P.row_set, P.row_set, &full[s],
+                                         policy);
+                            ++issued;
+                        }
+                    }
+                    if (++s == S) {
+                        s = 0;
+                        phase ^= 1;
+                        wrapped = true;
+                    }
+                }
+            }
+            // Wait for the copies still in flight before the CTA may exit.
+            const uint32_t total = (unit_end - unit_begin) * P.chunks;
+            for (uint32_t i = total > S ? total - S : 0; i < total && issued; ++i) {
+                const uint32_t ss = i % S, ph = (i / S) & 1;
+                if (!mbar_wait(&full[ss], ph)) record_error(P.status, KVM_ERR_TIMEOUT, 5);
+            }
+        }
+        return;
+    }
+
+    // Consumers: lane = g*4 + c; warp serves KV head kvh and octets wsub, wsub + WPH, ... of a chunk.
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t kvh = uint32_t(warp) % KVH, wsub = uint32_t(warp) / KVH;
+    const uint32_t splice = c == 3 ? 0x7610u : 0x3210u;
+    const bool gvalid = g < int(P.nv);
+    const uint32_t myr = gvalid ? (P.v0 + g) / P.group : 0;
+    const uint32_t slot = P.slot_stride;
+    const uint32_t nj = P.tpc / (8 * WPH);
+    const uint32_t lane_b = (wsub * 8 + g) * slot + kvh * kRow;      // code row: token g of the octet
+    const uint32_t lane_s = (wsub * 8 + 2 * c) * slot + kvh * kRow;  // scale rows: tokens 2c, 2c+1
+    const uint32_t jstep = WPH * 8 * slot;
+
+    uint32_t qa[KK][2][4];
+    float sl2 = 0.f;  // 2^-shift * scale * log2(e)
+    float qinv = 1.f;
+    uint32_t s = 0, phase = 0, ucount = 0, qlayer = 0xffffffffu;
+    for (uint32_t unit = unit_begin; unit < unit_end; ++unit, ++ucount) {
+        const uint32_t l = unit / P.pages, p = unit - l * P.pages;
+        if (l != qlayer) {
+            qlayer = l;
+            float qv[KK][8];
+            float amax = 0.f;
+            const uint32_t vg = P.v0 + g, r = gvalid ? vg / P.group : 0, gg = gvalid ? vg % P.group : 0;
+            const uint8_t* qp = P.q + l * P.q_layer + r * P.q_row + (kvh * P.group + gg) * P.q_head;
+            const uint32_t esz = type_bytes(P.q_type);
+#pragma unroll
+            for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int dim = kk * 32 + q_dim<KT>(kk, c, i);
+                    qv[kk][i] = gvalid ? load_scalar(qp + dim * esz, P.q_type) : 0.f;
+                    amax = fmaxf(amax, fabsf(qv[kk][i]));
+                }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            int shift = 0;
+            if (amax > 0.f) {
+                const int e = int((__float_as_uint(amax) >> 23) & 255) - 127;
+                shift = min(100, max(-100, 13 - e));
+            }
+            const float qs = ldexpf(1.f, shift);
+            qinv = ldexpf(1.f, -shift);
+            sl2 = qinv * P.scale * kLog2e;
+#pragma unroll
+            for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+                for (int st = 0; st < 2; ++st) {
+                    float h[4], lo[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float x = qv[kk][4 * st + j] * qs;
+                        h[j] = __half2float(__float2half_rn(x));
+                        lo[j] = x - h[j];
+                    }
+                    qa[kk][st][0] = pack_half2(h[0], h[1]);
+                    qa[kk][st][1] = pack_half2(lo[0], lo[1]);
+                    qa[kk][st][2] = pack_half2(h[2], h[3]);
+                    qa[kk][st][3] = pack_half2(lo[2], lo[3]);
+                }
+        }
+        float m = -INFINITY, ssum = 0.f;
+        const uint64_t tok0 = uint64_t(p) * P.page_tokens;
+
+        for (uint32_t ch = 0; ch < P.chunks; ++ch) {
+            bool ok = !*reinterpret_cast<volatile int*>(abort_flag);
+            if (ok && !mbar_wait(&full[s], phase)) {
+                record_error(P.status, KVM_ERR_TIMEOUT, 6);
+                *reinterpret_cast<volatile int*>(abort_flag) = 1;
+                ok = false;
+            }
+            if (ok) {
+                const uint8_t* stage = stages + s * P.stage_stride;
+                const uint64_t ctok = tok0 + uint64_t(ch) * P.tpc;
+                const bool fast = !MASK && P.softcap <= 0.f && ctok + P.tpc <= P.tokens;
+                for (uint32_t j = 0; j < nj; ++j) {
+                    const uint8_t* brow = stage + lane_b + j * jstep;
+                    const uint8_t* srow = stage + lane_s + j * jstep;
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                    unroll_kk<KK>([&](auto kkc) {
+                        constexpr int kk = decltype(kkc)::value;
+                        uint32_t b[4];
+                        q_b_frag<KT, kk>(brow, c, splice, b);
+                        float blk[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma_16816(blk, qa[kk][0], b[0], b[1]);
+                        mma_16816(blk, qa[kk][1], b[2], b[3]);
+                        const float d0 = __half2float(*reinterpret_cast<const __half*>(srow + kBlock * kk));
+                        const float d1 = __half2float(*reinterpret_cast<const __half*>(srow + slot + kBlock * kk));
+                        acc[0] = fmaf(blk[0], d0, acc[0]);
+                        acc[1] = fmaf(blk[1], d1, acc[1]);
+                        acc[2] = fmaf(blk[2], d0, acc[2]);
+                        acc[3] = fmaf(blk[3], d1, acc[3]);
+                    });
+                    if (fast) {
+                        const float x0 = (acc[0] + acc[2]) * sl2, x1 = (acc[1] + acc[3]) * sl2;
+                        const float mn = fmaxf(m, fmaxf(x0, x1));
+                        ssum = fmaf(ssum, fast_exp2(m - mn), fast_exp2(x0 - mn) + fast_exp2(x1 - mn));
+                        m = mn;
+                    } else {
+                        const uint64_t t0 = ctok + (wsub + j * WPH) * 8 + 2 * c;
+#pragma unroll
+                        for (int jj = 0; jj < 2; ++jj) {
+                            const float dot = (acc[jj] + acc[2 + jj]) * qinv;
+                            float x;
+                            if (P.softcap > 0.f) x = P.softcap * tanhf(dot * P.scale / P.softcap) * kLog2e;
+                            else x = dot * P.scale * kLog2e;
+                            const uint64_t t = t0 + jj;
+                            bool visible = gvalid && t < P.tokens;
+                            if constexpr (MASK) {
+                                if (visible) {
+                                    const float bias = load_scalar(
+                                        P.mask + myr * P.mask_row + t * type_bytes(P.mask_type), P.mask_type);
+                                    visible = isfinite(bias);
+                                    x += bias * kLog2e;
+                                }
+                            }
+                            if (visible) {
+                                if (x > m) {
+                                    ssum = ssum * fast_exp2(m - x) + 1.f;
+                                    m = x;
+                                } else {
+                                    ssum += fast_exp2(x - m);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+
+        // Merge the four lanes of vector g, then the warps of the KV head.
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, ssum, o);
+            const float M = fmaxf(m, m2);
+            float Sx = 0.f;
+            if (M != -INFINITY) {
+                if (ssum > 0.f) Sx += ssum * fast_exp2(m - M);
+                if (s2 > 0.f) Sx += s2 * fast_exp2(m2 - M);
+            }
+            m = M;
+            ssum = Sx;
+        }
+        const int buf = ucount & 1;
+        if (c == 0) {
+            red_m[(buf * NW + warp) * 8 + g] = m;
+            red_s[(buf * NW + warp) * 8 + g] = ssum;
+        }
+        named_sync(1, NW * 32);
+        if (tid < KVH * 8) {
+            const uint32_t h_kv = tid / 8, v = tid % 8;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w2 = 0; w2 < WPH; ++w2) M = fmaxf(M, red_m[(buf * NW + h_kv + w2 * KVH) * 8 + v]);
+            float Sx = 0.f;
+            if (M != -INFINITY)
+#pragma unroll
+                for (int w2 = 0; w2 < WPH; ++w2) {
+                    const int at = (buf * NW + h_kv + w2 * KVH) * 8 + v;
+                    if (red_s[at] > 0.f) Sx += red_s[at] * fast_exp2(red_m[at] - M);
+                }
+            if (v < P.nv) {
+                const uint32_t vg = P.v0 + v, r = vg / P.group, gg = vg % P.group;
+                const uint32_t h = h_kv * P.group + gg;
+                P.lse[((uint64_t(l) * P.rows + r) * P.q_heads + h) * P.pages + p] =
+                    Sx > 0.f ? (M + fast_log2(Sx)) * kLn2 : -INFINITY;
+            }
+        }
+    }
+}
+
+}  // namespace kvmb

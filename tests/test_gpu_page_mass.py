@@ -82,6 +82,13 @@ CASES = [
     dict(ktype=U.F16, D=64, Hq=8, Hkv=1, page=64, T=512, qtype=U.F16),
     dict(ktype=U.Q4_0, D=256, Hq=24, Hkv=4, page=256, T=768, qtype=U.BF16),
     dict(ktype=U.Q8_0, D=128, Hq=40, Hkv=8, R=2, page=128, T=512),
+    # quantised keys across the quantised kernel's variants: head_dim 64 (two blocks),
+    # 8 and 1 KV heads, partial last page, softcap, f16 queries
+    dict(ktype=U.Q8_0, D=64, Hq=16, Hkv=8, page=64, T=512),
+    dict(ktype=U.Q4_0, D=64, Hq=4, Hkv=2, page=128, T=1000, cap=1024),
+    dict(ktype=U.Q8_0, D=256, Hq=24, Hkv=4, page=256, T=700, cap=768, softcap=30.0),
+    dict(ktype=U.Q8_0, D=128, Hq=8, Hkv=1, page=64, T=512, qtype=U.F16),
+    dict(ktype=U.Q4_0, D=128, Hq=16, Hkv=8, page=64, T=640, softcap=20.0, scale=0.1),
 ]
 
 
@@ -120,6 +127,16 @@ def test_mask_hides_tokens_and_empty_rows_are_nan(ctx, scorer):
     ok, worst, _ = U.close(got[:, :, :2], exp[:, :, :2], REL, ABS)
     assert ok, worst
     assert got[0, 0, 0, 2] < 1e-6  # page 2 (tokens 128..191) fully hidden for row 0
+
+
+@pytest.mark.parametrize("ktype", [U.Q8_0, U.Q4_0])
+def test_quantised_keys_with_mask(ctx, scorer, ktype):
+    R, T, page = 2, 640, 64
+    rng = np.random.default_rng(7)
+    mask = rng.standard_normal((R, T)).astype(np.float32)
+    mask[0, 64:200] = -np.inf
+    mask[1, 600:] = -np.inf
+    run_case(ctx, ktype=ktype, D=256, Hq=24, Hkv=4, R=R, page=page, T=T, mask=mask, seed=3)
 
 
 def test_unsupported_layouts_are_rejected(ctx):
