@@ -140,6 +140,10 @@ struct LseConfig {
     bool mma = false;
     uint32_t mma_tpc = 0, mma_chunk_bytes = 0, mma_chunks = 0, mma_stage_stride = 0, mma_stages = 0, mma_slot = 0;
     size_t mma_smem = 0;
+    // Quantised-key scorer (q8_0 / q4_0, page_mass_q.cuh), when usable.
+    bool q = false;
+    uint32_t q_tpc = 0, q_chunks = 0, q_slot = 0, q_hpg = 0, q_groups = 0, q_stage_stride = 0, q_stages = 0, q_tx = 0;
+    size_t q_smem = 0;
     // tcgen05 scorer (fp16 keys, 16..160 query vectors per KV head), when usable.
     bool tc = false;
     int tc_ka = 0, tc_lm = 0;
@@ -216,6 +220,50 @@ void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
                     2 * 2 * kLseConsumerWarps * 8 * sizeof(float) + 16;
 }
 
+// Quantised-key scorer: the K heads of a token are split into groups of hpg
+// heads whose row bytes are a multiple of 16 and fit one TMA box row (<= 255
+// u64 elements with the pad); each group's rows land in shared memory at a
+// stride of an odd number of 16-byte units (pad = 0 or 16 zero-filled bytes).
+// A chunk is 8 tokens per warp of a KV head (2 octets when that keeps the
+// stage within 20 KiB); stages fill ~100 KiB so two CTAs share an SM.
+void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
+    if (force_simt() || scorer_is("mma_generic")) return;
+    if (k->type != KVM_Q8_0 && k->type != KVM_Q4_0) return;
+    const uint32_t kvh = d->kv_heads;
+    if (kvh == 0 || 8 % kvh) return;
+    const uint64_t rb = row_bytes_of(k->type, d->head_dim);
+    uint32_t hpg = 0, pad = 0;
+    for (uint32_t h = kvh; h >= 1; h >>= 1) {
+        const uint64_t gb = h * rb;
+        if (kvh % h || gb % 16) continue;
+        const uint32_t pd = (gb / 16) % 2 ? 0 : 16;
+        if ((gb + pd) / 8 > 255) continue;
+        hpg = h;
+        pad = pd;
+        break;
+    }
+    if (!hpg) return;
+    const uint32_t slot = uint32_t(hpg * rb + pad), groups = kvh / hpg;
+    const uint32_t wph = kLseConsumerWarps / kvh;
+    uint32_t tpc = 8 * wph;
+    if (d->page_tokens % tpc || tpc > 256) return;
+    if (d->page_tokens % (2 * tpc) == 0 && 2 * tpc <= 256 && uint64_t(2 * tpc) * slot * groups <= 20 * 1024) tpc *= 2;
+    const uint64_t stage = uint64_t(tpc) * slot * groups;
+    const uint32_t stride = uint32_t((stage + 127) / 128 * 128);
+    const uint32_t stages = uint32_t(std::min<uint64_t>(kMmaMaxStages, (100 * 1024) / stride));
+    if (stages < 2) return;
+    cfg->q = true;
+    cfg->q_tpc = tpc;
+    cfg->q_chunks = d->page_tokens / tpc;
+    cfg->q_slot = slot;
+    cfg->q_hpg = hpg;
+    cfg->q_groups = groups;
+    cfg->q_stage_stride = stride;
+    cfg->q_stages = stages;
+    cfg->q_tx = uint32_t(stage);
+    cfg->q_smem = size_t(stages) * stride + q_smem_extra();
+}
+
 bool supported_type(int t) { return t >= KVM_F32 && t <= KVM_Q5_0; }
 
 int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, LseConfig* cfg) {
@@ -263,6 +311,7 @@ int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache
     cfg->smem = size_t(kLseStages) * cfg->stage_stride + 2 * kLseStages * sizeof(uint64_t) +
                 2 * 2 * size_t(ng) * 8 * sizeof(float) + 16;
     plan_mma(d, k, cfg);
+    plan_q(d, k, cfg);
     plan_tc(d, q, k, cfg);
     if (scorer_is("tc") && !cfg->tc) return KVM_ERR_UNSUPPORTED;  // strict: the tcgen05 kernel or nothing
     return KVM_OK;
@@ -276,12 +325,8 @@ size_t lse_bytes(const kvm_score_desc* d, uint32_t layers, uint32_t rows) {
 int launch_lse_mma(kvm_ctx* c, int kt, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
     switch (kt) {
         case KVM_F16: return launch_lse_mma_kt<KVM_F16>(c, p, kk, smem, s);
-        case KVM_Q8_0:
-            return scorer_is("mma_generic") ? launch_lse_mma_kt<KVM_Q8_0>(c, p, kk, smem, s)
-                                            : launch_lse_q_kt<KVM_Q8_0>(c, p, kk, smem, s);
-        case KVM_Q4_0:
-            return scorer_is("mma_generic") ? launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s)
-                                            : launch_lse_q_kt<KVM_Q4_0>(c, p, kk, smem, s);
+        case KVM_Q8_0: return launch_lse_mma_kt<KVM_Q8_0>(c, p, kk, smem, s);
+        case KVM_Q4_0: return launch_lse_mma_kt<KVM_Q4_0>(c, p, kk, smem, s);
         default: return KVM_ERR_UNSUPPORTED;
     }
 }
@@ -323,6 +368,37 @@ int encode_k_map(const kvm_score_desc* d, const kvm_kcache* k, const void* base,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? KVM_OK : KVM_ERR_CUDA;
+}
+
+// 4-D tensor map of quantised K of layers [0, nl) from `base`, in u64 units:
+// dims (group row bytes / 8, head groups, tokens, layers), box (row + pad
+// columns, 1 group, tpc tokens, 1 layer); the pad columns lie past the
+// group's row and read as zeros.
+int encode_q_map(const kvm_score_desc* d, const kvm_kcache* k, const void* base, uint32_t nl, const LseConfig& cfg,
+                 CUtensorMap* map) {
+    TensorMapEncodeFn enc = tensor_map_encoder();
+    if (!enc) return KVM_ERR_CUDA;
+    const uint64_t gb = uint64_t(cfg.q_hpg) * k->head_stride;
+    uint64_t cap = std::min<uint64_t>(k->capacity_tokens, 0x7fffffffull);
+    if (nl > 1) cap = std::min<uint64_t>(cap, k->layer_stride / k->token_stride);
+    const cuuint64_t dims[4] = {gb / 8, cfg.q_groups, cap, nl};
+    const uint64_t lstride = nl > 1 ? k->layer_stride : cap * k->token_stride;
+    const cuuint64_t strides[3] = {cfg.q_groups > 1 ? gb : k->token_stride, k->token_stride, lstride};
+    const cuuint32_t box[4] = {cfg.q_slot / 8, 1, cfg.q_tpc, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? KVM_OK : KVM_ERR_CUDA;
+}
+
+int launch_lse_q(kvm_ctx* c, int kt, const CUtensorMap& map, const LseParams& p, int kk, size_t smem,
+                 cudaStream_t s) {
+    switch (kt) {
+        case KVM_Q8_0: return launch_lse_q_kt<KVM_Q8_0>(c, map, p, kk, smem, s);
+        case KVM_Q4_0: return launch_lse_q_kt<KVM_Q4_0>(c, map, p, kk, smem, s);
+        default: return KVM_ERR_UNSUPPORTED;
+    }
 }
 
 int launch_lse(kvm_ctx* c, int kt, const LseParams& p, int lpr, int vp, size_t smem, cudaStream_t s) {
@@ -382,6 +458,25 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
         p.v0 = 0;
         p.nv = nvt;
         return launch_lse_tc(c, map, p, cfg.tc_ka, cfg.tc_lm, cfg.tc_smem, s);
+    }
+    if (cfg.q) {
+        // Passes of up to 8 query vectors, as the mma.sync kernel below.
+        CUtensorMap map;
+        KVM_TRY(encode_q_map(d, k, p.k, nl, cfg, &map));
+        p.chunk_bytes = cfg.q_tx;
+        p.chunks = cfg.q_chunks;
+        p.tpc = cfg.q_tpc;
+        p.stage_stride = cfg.q_stage_stride;
+        p.stages = cfg.q_stages;
+        p.slot_stride = cfg.q_slot;
+        p.hpg = cfg.q_hpg;
+        p.groups_tma = cfg.q_groups;
+        for (uint32_t v0 = 0; v0 < nvt; v0 += 8) {
+            p.v0 = v0;
+            p.nv = std::min<uint32_t>(8, nvt - v0);
+            KVM_TRY(launch_lse_q(c, k->type, map, p, int(d->head_dim / 32), cfg.q_smem, s));
+        }
+        return KVM_OK;
     }
     if (cfg.mma) {
         // Passes of up to 8 query vectors (the 16 rows of the mma's A tile hold

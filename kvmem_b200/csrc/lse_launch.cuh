@@ -118,7 +118,7 @@ int launch_lse_mma_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaS
 }
 
 template <int KT, int KK, int KVH, bool MASK>
-int launch_lse_q_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
+int launch_lse_q_t(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, size_t smem, cudaStream_t s) {
     auto fn = page_lse_q_kernel<KT, KK, KVH, MASK>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
@@ -127,39 +127,39 @@ int launch_lse_q_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) 
     });
     if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLseThreads, smem) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQThreads, smem) != cudaSuccess) {
         cudaGetLastError();
         return KVM_ERR_CUDA;
     }
     if (per_sm < 1) return KVM_ERR_UNSUPPORTED;
     const uint32_t units = p.layers * p.pages;
     const uint32_t grid = std::min<uint32_t>(units, uint32_t(c->num_sms * per_sm));
-    fn<<<grid, kLseThreads, smem, s>>>(p);
+    fn<<<grid, kQThreads, smem, s>>>(map, p);
     ++c->launches;
     if (cudaGetLastError() != cudaSuccess) return KVM_ERR_CUDA;
     return KVM_OK;
 }
 
 template <int KT, int KK>
-int launch_lse_q_kk(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
+int launch_lse_q_kk(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, size_t smem, cudaStream_t s) {
     const bool m = p.mask != nullptr;
     switch (p.kv_heads) {
-        case 1: return m ? launch_lse_q_t<KT, KK, 1, true>(c, p, smem, s) : launch_lse_q_t<KT, KK, 1, false>(c, p, smem, s);
-        case 2: return m ? launch_lse_q_t<KT, KK, 2, true>(c, p, smem, s) : launch_lse_q_t<KT, KK, 2, false>(c, p, smem, s);
-        case 4: return m ? launch_lse_q_t<KT, KK, 4, true>(c, p, smem, s) : launch_lse_q_t<KT, KK, 4, false>(c, p, smem, s);
-        case 8: return m ? launch_lse_q_t<KT, KK, 8, true>(c, p, smem, s) : launch_lse_q_t<KT, KK, 8, false>(c, p, smem, s);
+        case 1: return m ? launch_lse_q_t<KT, KK, 1, true>(c, map, p, smem, s) : launch_lse_q_t<KT, KK, 1, false>(c, map, p, smem, s);
+        case 2: return m ? launch_lse_q_t<KT, KK, 2, true>(c, map, p, smem, s) : launch_lse_q_t<KT, KK, 2, false>(c, map, p, smem, s);
+        case 4: return m ? launch_lse_q_t<KT, KK, 4, true>(c, map, p, smem, s) : launch_lse_q_t<KT, KK, 4, false>(c, map, p, smem, s);
+        case 8: return m ? launch_lse_q_t<KT, KK, 8, true>(c, map, p, smem, s) : launch_lse_q_t<KT, KK, 8, false>(c, map, p, smem, s);
     }
     return KVM_ERR_UNSUPPORTED;
 }
 
 // Tensor-core scorer for q8_0 / q4_0 keys (page_mass_q.cuh); kk = head_dim / 32.
 template <int KT>
-int launch_lse_q_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
+int launch_lse_q_kt(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int kk, size_t smem, cudaStream_t s) {
     if constexpr (KT == KVM_Q8_0 || KT == KVM_Q4_0) {
         switch (kk) {
-            case 2: return launch_lse_q_kk<KT, 2>(c, p, smem, s);
-            case 4: return launch_lse_q_kk<KT, 4>(c, p, smem, s);
-            case 8: return launch_lse_q_kk<KT, 8>(c, p, smem, s);
+            case 2: return launch_lse_q_kk<KT, 2>(c, map, p, smem, s);
+            case 4: return launch_lse_q_kk<KT, 4>(c, map, p, smem, s);
+            case 8: return launch_lse_q_kk<KT, 8>(c, map, p, smem, s);
         }
     }
     return KVM_ERR_UNSUPPORTED;
@@ -182,7 +182,9 @@ extern template int launch_lse_kt<KVM_Q5_0>(kvm_ctx*, const LseParams&, int, int
 extern template int launch_lse_mma_kt<KVM_F16>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
 extern template int launch_lse_mma_kt<KVM_Q8_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
 extern template int launch_lse_mma_kt<KVM_Q4_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
-extern template int launch_lse_q_kt<KVM_Q8_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
-extern template int launch_lse_q_kt<KVM_Q4_0>(kvm_ctx*, const LseParams&, int, size_t, cudaStream_t);
+extern template int launch_lse_q_kt<KVM_Q8_0>(kvm_ctx*, const CUtensorMap&, const LseParams&, int, size_t,
+                                              cudaStream_t);
+extern template int launch_lse_q_kt<KVM_Q4_0>(kvm_ctx*, const CUtensorMap&, const LseParams&, int, size_t,
+                                              cudaStream_t);
 
 }  // namespace kvmb

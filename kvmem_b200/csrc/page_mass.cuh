@@ -57,6 +57,8 @@ struct LseParams {
     uint32_t stages;        // ring stages (tensor-core kernel; the SIMT kernel uses kLseStages)
     uint32_t row_set;       // bytes of one token across KV heads (kv_heads * row_bytes)
     uint32_t slot_stride;   // tensor-core kernel, quantised keys: padded shared-memory stride per token
+    uint32_t hpg;           // quantised-key kernel: KV heads per TMA head group
+    uint32_t groups_tma;    // quantised-key kernel: head groups (one tiled TMA box each per chunk)
 };
 
 // Decode the lane's 8 consecutive elements of one K row held in shared

@@ -19,6 +19,11 @@
 //    words: lane c holds the aligned words 1+c and 5+c, lane 3's second word
 //    is {30, 31, 0, 1}. The mma's k index follows the same lane-dependent
 //    order for the queries, so every element is counted once;
+//  * each chunk arrives as one tiled TMA box per group of KV heads whose
+//    inner extent runs 16 bytes past the group's row bytes into zero-filled
+//    out-of-bounds columns, so token rows land in shared memory at a stride
+//    of an odd number of 16-byte units: the 8 tokens of an octet start in 8
+//    different bank groups and every 32-bit load is conflict-free;
 //  * a chunk that is fully visible, unmasked and without softcap takes a
 //    branchless online (max, sum) update per token pair; everything else
 //    takes the general per-token path.
@@ -79,78 +84,75 @@ __device__ __forceinline__ void q_b_frag(const uint8_t* row, int c, uint32_t spl
     }
 }
 
+constexpr int kQThreads = kLseConsumerWarps * 32;  // no producer warp: 16 warps per SM at 2 CTAs
+
+// Shared memory of page_lse_q_kernel beyond its S ring stages.
+__host__ __device__ constexpr size_t q_smem_extra() {
+    return kMmaMaxStages * (sizeof(uint64_t) + 2 * sizeof(uint32_t)) +  // full barriers, release counts, issues
+           2 * 2 * kLseConsumerWarps * 8 * sizeof(float) +              // per-page merge buffers
+           kLseConsumerWarps * 2 * 64 * sizeof(float) +                 // per-warp scale tables (double buffered)
+           16;
+}
+
 // KK = head_dim / 32 blocks per row; KVH = KV heads (1, 2, 4 or 8).
+//
+// Ring protocol: thread 0 fills the first S stages; afterwards the warp that
+// releases a stage last (a shared-memory count of releases per stage) issues
+// the stage's next chunk, S chunks ahead. There is no producer warp, so the
+// SM holds 16 warps of two CTAs and each thread may use 128 registers.
 template <int KT, int KK, int KVH, bool MASK>
-__global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LseParams P) {
+__global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                  const LseParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = kLseConsumerWarps;
     constexpr int WPH = NW / KVH;  // warps per KV head
     constexpr int kBlock = KT == KVM_Q8_0 ? 34 : 18;
     constexpr uint32_t kRow = uint32_t(kBlock * KK);
-    static_assert(NW % KVH == 0, "warps per KV head");
+    static_assert(NW % KVH == 0 && (NW & (NW - 1)) == 0, "warps per KV head");
     const uint32_t S = P.stages;
     uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.stage_stride);
-    uint64_t* empty = full + kMmaMaxStages;
-    float* red_m = reinterpret_cast<float*>(empty + kMmaMaxStages);  // [2][NW][8]
+    uint32_t* released = reinterpret_cast<uint32_t*>(full + kMmaMaxStages);
+    uint32_t* issued = released + kMmaMaxStages;
+    float* red_m = reinterpret_cast<float*>(issued + kMmaMaxStages);  // [2][NW][8]
     float* red_s = red_m + 2 * NW * 8;
-    int* abort_flag = reinterpret_cast<int*>(red_s + 2 * NW * 8);
+    float* tables = red_s + 2 * NW * 8;  // [NW][2][KK<=8][8 tokens]
+    int* abort_flag = reinterpret_cast<int*>(tables + NW * 2 * 64);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) {
-        for (uint32_t s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NW);
-        }
-        *abort_flag = 0;
-        mbar_fence_init();
-    }
-    __syncthreads();
     const uint32_t units = P.layers * P.pages;
     const uint32_t per_cta = (units + gridDim.x - 1) / gridDim.x;
     const uint32_t unit_begin = min(units, blockIdx.x * per_cta), unit_end = min(units, unit_begin + per_cta);
+    const uint32_t total = (unit_end - unit_begin) * P.chunks;  // chunks of this CTA
+    const uint64_t policy = policy_evict_first();
 
-    if (warp == NW) {
-        if (lane == 0) {
-            const uint64_t policy = policy_evict_first();
-            uint32_t s = 0, phase = 0, issued = 0;
-            bool wrapped = false;
-            for (uint32_t unit = unit_begin; unit < unit_end; ++unit) {
-                const uint32_t l = unit / P.pages, p = unit - l * P.pages;
-                const uint8_t* src = P.k + l * P.k_layer + uint64_t(p) * P.page_bytes;
-                for (uint32_t c = 0; c < P.chunks; ++c) {
-                    if (!*reinterpret_cast<volatile int*>(abort_flag)) {
-                        if (wrapped && !mbar_wait(&empty[s], phase ^ 1)) {
-                            record_error(P.status, KVM_ERR_TIMEOUT, 4);
-                            *reinterpret_cast<volatile int*>(abort_flag) = 1;
-                        } else {
-                            mbar_arrive_expect_tx(&full[s], P.chunk_bytes);
-                            uint8_t* dst = stages + s * P.stage_stride;
-                            const uint8_t* from = src + uint64_t(c) * P.chunk_bytes;
-                            for (uint32_t t = 0; t < P.tpc; ++t)
-                                bulk_g2s(dst + t * P.slot_stride, from + uint64_t(t) * P.row_set, P.row_set, &full[s],
-                                         policy);
-                            ++issued;
-                        }
-                    }
-                    if (++s == S) {
-                        s = 0;
-                        phase ^= 1;
-                        wrapped = true;
-                    }
-                }
-            }
-            // Wait for the copies still in flight before the CTA may exit.
-            const uint32_t total = (unit_end - unit_begin) * P.chunks;
-            for (uint32_t i = total > S ? total - S : 0; i < total && issued; ++i) {
-                const uint32_t ss = i % S, ph = (i / S) & 1;
-                if (!mbar_wait(&full[ss], ph)) record_error(P.status, KVM_ERR_TIMEOUT, 5);
-            }
+    // Chunk ch of page unit_begin + u into stage s: one tiled box per head group,
+    // tokens x (the group's row bytes + zero-filled pad columns) -> rows of
+    // slot_stride bytes, group after group.
+    auto issue = [&](uint32_t s, uint32_t u, uint32_t ch) {
+        const uint32_t unit = unit_begin + u;
+        const uint32_t l = unit / P.pages, p = unit - l * P.pages;
+        const int tok = int(p * P.page_tokens + ch * P.tpc);
+        uint8_t* dst = stages + s * P.stage_stride;
+        mbar_arrive_expect_tx(&full[s], P.chunk_bytes);
+        for (uint32_t grp = 0; grp < P.groups_tma; ++grp)
+            tma_load_4d(dst + grp * P.tpc * P.slot_stride, &kmap, 0, int(grp), tok, int(l), &full[s], policy);
+        ++issued[s];
+    };
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            released[s] = 0;
+            issued[s] = 0;
         }
-        return;
+        *abort_flag = 0;
+        mbar_fence_init();
+        for (uint32_t i = 0; i < S && i < total; ++i) issue(i, i / P.chunks, i % P.chunks);
     }
+    __syncthreads();
 
-    // Consumers: lane = g*4 + c; warp serves KV head kvh and octets wsub, wsub + WPH, ... of a chunk.
+    // lane = g*4 + c; warp serves KV head kvh and octets wsub, wsub + WPH, ... of each chunk.
     const int g = lane >> 2, c = lane & 3;
     const uint32_t kvh = uint32_t(warp) % KVH, wsub = uint32_t(warp) / KVH;
     const uint32_t splice = c == 3 ? 0x7610u : 0x3210u;
@@ -158,14 +160,18 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LsePar
     const uint32_t myr = gvalid ? (P.v0 + g) / P.group : 0;
     const uint32_t slot = P.slot_stride;
     const uint32_t nj = P.tpc / (8 * WPH);
-    const uint32_t lane_b = (wsub * 8 + g) * slot + kvh * kRow;      // code row: token g of the octet
-    const uint32_t lane_s = (wsub * 8 + 2 * c) * slot + kvh * kRow;  // scale rows: tokens 2c, 2c+1
+    const uint32_t head_off = (kvh / P.hpg) * P.tpc * slot + (kvh % P.hpg) * kRow;
+    const uint32_t lane_b = (wsub * 8 + g) * slot + head_off;             // code row: token g of the octet
+    const uint32_t tab_row = (wsub * 8 + (lane & 7)) * slot + head_off;  // scale-table fill: token lane % 8
     const uint32_t jstep = WPH * 8 * slot;
+    float* tab = tables + warp * 2 * 64;
 
     uint32_t qa[KK][2][4];
     float sl2 = 0.f;  // 2^-shift * scale * log2(e)
     float qinv = 1.f;
-    uint32_t s = 0, phase = 0, ucount = 0, qlayer = 0xffffffffu;
+    uint32_t s = 0, phase = 0, ucount = 0, qlayer = 0xffffffffu, tb = 0;
+    // Refill cursor: the chunk S ahead of the one being consumed.
+    uint32_t r_idx = S, r_u = S / P.chunks, r_ch = S % P.chunks;
     for (uint32_t unit = unit_begin; unit < unit_end; ++unit, ++ucount) {
         const uint32_t l = unit / P.pages, p = unit - l * P.pages;
         if (l != qlayer) {
@@ -226,7 +232,21 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LsePar
                 const bool fast = !MASK && P.softcap <= 0.f && ctok + P.tpc <= P.tokens;
                 for (uint32_t j = 0; j < nj; ++j) {
                     const uint8_t* brow = stage + lane_b + j * jstep;
-                    const uint8_t* srow = stage + lane_s + j * jstep;
+                    // Block scales of the octet's 8 tokens as floats: tab[kk][token].
+                    {
+                        const uint8_t* trow = stage + tab_row + j * jstep;
+                        float* t = tab + tb * 64;
+#pragma unroll
+                        for (int b = 0; b < (KK + 3) / 4; ++b) {
+                            const int kk = (lane >> 3) + 4 * b;
+                            if (kk < KK)
+                                t[kk * 8 + (lane & 7)] =
+                                    __half2float(*reinterpret_cast<const __half*>(trow + kBlock * kk));
+                        }
+                        __syncwarp();
+                    }
+                    const float* tsc = tab + tb * 64 + 2 * c;
+                    tb ^= 1;
                     float acc[4] = {0.f, 0.f, 0.f, 0.f};
                     unroll_kk<KK>([&](auto kkc) {
                         constexpr int kk = decltype(kkc)::value;
@@ -235,12 +255,11 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LsePar
                         float blk[4] = {0.f, 0.f, 0.f, 0.f};
                         mma_16816(blk, qa[kk][0], b[0], b[1]);
                         mma_16816(blk, qa[kk][1], b[2], b[3]);
-                        const float d0 = __half2float(*reinterpret_cast<const __half*>(srow + kBlock * kk));
-                        const float d1 = __half2float(*reinterpret_cast<const __half*>(srow + slot + kBlock * kk));
-                        acc[0] = fmaf(blk[0], d0, acc[0]);
-                        acc[1] = fmaf(blk[1], d1, acc[1]);
-                        acc[2] = fmaf(blk[2], d0, acc[2]);
-                        acc[3] = fmaf(blk[3], d1, acc[3]);
+                        const float2 d = *reinterpret_cast<const float2*>(tsc + kk * 8);  // tokens 2c, 2c+1
+                        acc[0] = fmaf(blk[0], d.x, acc[0]);
+                        acc[1] = fmaf(blk[1], d.y, acc[1]);
+                        acc[2] = fmaf(blk[2], d.x, acc[2]);
+                        acc[3] = fmaf(blk[3], d.y, acc[3]);
                     });
                     if (fast) {
                         const float x0 = (acc[0] + acc[2]) * sl2, x1 = (acc[1] + acc[3]) * sl2;
@@ -277,8 +296,23 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LsePar
                     }
                 }
             }
+            // Release the stage; the last warp to release it refills it S chunks ahead.
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0) {
+                __threadfence_block();
+                const uint32_t before = atomicAdd(&released[s], 1u);
+                if ((before & (NW - 1)) == NW - 1 && r_idx < total &&
+                    !*reinterpret_cast<volatile int*>(abort_flag)) {
+                    __threadfence_block();
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(s, r_u, r_ch);
+                }
+            }
+            ++r_idx;
+            if (++r_ch == P.chunks) {
+                r_ch = 0;
+                ++r_u;
+            }
             if (++s == S) {
                 s = 0;
                 phase ^= 1;
@@ -323,6 +357,13 @@ __global__ void __launch_bounds__(kLseThreads, 2) page_lse_q_kernel(const LsePar
                     Sx > 0.f ? (M + fast_log2(Sx)) * kLn2 : -INFINITY;
             }
         }
+    }
+
+    // After a timeout no copy may still be landing in this CTA's shared memory when it exits.
+    __syncthreads();
+    if (tid == 0 && *reinterpret_cast<volatile int*>(abort_flag)) {
+        for (uint32_t st = 0; st < S; ++st)
+            if (issued[st] && !mbar_wait(&full[st], (issued[st] - 1) & 1)) record_error(P.status, KVM_ERR_TIMEOUT, 5);
     }
 }
 

@@ -96,16 +96,6 @@ __device__ __forceinline__ void tc_wait_ld(uint32_t* r) {
                  : "memory");
 }
 
-// Tiled 4-D TMA load of one box into this CTA's shared memory (no multicast).
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
-                                            uint64_t* bar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
-        : "memory");
-}
-
 // Power-of-two prescale exponent of a query vector: |q| * 2^shift < 2^14.
 __device__ __forceinline__ int tc_shift_of(float amax) {
     if (!(amax > 0.f)) return 0;
