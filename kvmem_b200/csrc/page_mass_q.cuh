@@ -1,24 +1,32 @@
 // Per-token page mass, first pass, for quantised keys (q8_0 / q4_0) on the
-// tensor cores: the page log-sum-exp of up to 8 query vectors that share a KV
-// head. Same mathematics as page_lse_mma_kernel (page_mass_mma.cuh): the
-// vectors are the A operand of mma.sync m16n8k16 as fp16 hi (rows 0..7) and lo
-// (rows 8..15) parts after an exact power-of-two prescale, the codes of one
-// 32-element block of 8 tokens are the B operand (exact in fp16), and each
-// block's partial dots are scaled by the token's block scale in fp32.
+// integer tensor cores: the page log-sum-exp of up to 8 query vectors that
+// share a KV head.
 //
-// What differs is the instruction stream of the consumer warps, which sets
-// this kernel's speed (the K bytes arrive faster than the SMs can fold them):
+// The K codes enter mma.sync m16n8k32 (s8 x s8 -> s32; q4_0 nibbles as u8)
+// exactly as they are stored, so no key element is ever converted. The query
+// vectors are the A operand as two int8 digits per element: each 32-element
+// block of a vector is scaled by its own power of two so that its largest
+// magnitude lies in [2^13, 2^15), rounded to an integer q and split as
+// q = 256*hi + lo (rows 0..7: hi of vectors 0..7, rows 8..15: lo). The block's
+// dots are exact integers; the mma's C operand starts at the bit pattern of
+// M = 1.5 * 2^(23+k) (k = the row's power of two; q4_0 also subtracts
+// 8 * the row's digit sum for the nibble offset), so the s32 result read as a
+// float is M + dot * 2^k exactly and one FADD of M recovers the scaled dot.
+// Each block's dot is then scaled by the token's fp16 block scale in fp32.
+// The query keeps 15-16 significant bits per block (relative error <= 2^-15 of
+// the block's largest element), within the 1e-3 relative bound on page scores.
+//
+// Instruction stream of the consumer warps:
 //  * the KV-head count, block geometry and row bytes are template constants,
-//    each warp serves one KV head and a fixed set of octets, and its
-//    shared-memory addresses advance by a constant per octet (no division or
-//    parameter reload per octet);
+//    each warp serves one KV head and a fixed set of octets (8 tokens), and
+//    its shared-memory addresses advance by a constant per octet;
 //  * blocks whose codes start 2 bytes off a 32-bit word (every other block:
 //    the 34- / 18-byte blocks alternate) are read as the aligned words that
 //    hold codes 2..29 (q8_0; nibble bytes 2..13 for q4_0) plus one word
 //    spliced (byte permute) from the halves of the block's first and last
 //    words: lane c holds the aligned words 1+c and 5+c, lane 3's second word
 //    is {30, 31, 0, 1}. The mma's k index follows the same lane-dependent
-//    order for the queries, so every element is counted once;
+//    order for the query digits, so every element is counted once;
 //  * each chunk arrives as one tiled TMA box per group of KV heads whose
 //    inner extent runs 16 bytes past the group's row bytes into zero-filled
 //    out-of-bounds columns, so token rows land in shared memory at a stride
@@ -52,24 +60,23 @@ __host__ __device__ constexpr int q_dim(int kk, int c, int i) {
     }
 }
 
-// B fragments of block kk for this lane from its token's row: b[0..1] k-step 0, b[2..3] k-step 1.
+// B fragments of block kk for this lane from its token's row, as the mma
+// takes them: b[0] = positions 0..3 (k 4c..4c+3), b[1] = positions 4..7
+// (k 16+4c..16+4c+3); q8_0 codes as s8, q4_0 nibbles as u8 (0..15).
 template <int KT, int kk>
 __device__ __forceinline__ void q_b_frag(const uint8_t* row, int c, uint32_t splice, uint32_t* b) {
     constexpr int kBlock = KT == KVM_Q8_0 ? 34 : 18;
     const uint8_t* blk = row + kBlock * kk;
     if constexpr (KT == KVM_Q8_0) {
-        uint32_t w0, w1;
         if constexpr (kk & 1) {
-            w0 = *reinterpret_cast<const uint32_t*>(blk + 2 + 4 * c);
-            w1 = *reinterpret_cast<const uint32_t*>(blk + 18 + 4 * c);
+            b[0] = *reinterpret_cast<const uint32_t*>(blk + 2 + 4 * c);
+            b[1] = *reinterpret_cast<const uint32_t*>(blk + 18 + 4 * c);
         } else {
-            w0 = *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * c);
+            b[0] = *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * c);
             const uint32_t r = *reinterpret_cast<const uint32_t*>(blk + 20 + 4 * c);
             const uint32_t h = *reinterpret_cast<const uint32_t*>(blk);
-            w1 = __byte_perm(r, h, splice);
+            b[1] = __byte_perm(r, h, splice);
         }
-        s8x4_to_h2(w0, b[0], b[1]);
-        s8x4_to_h2(w1, b[2], b[3]);
     } else {
         uint32_t w;
         if constexpr (kk & 1) {
@@ -79,19 +86,53 @@ __device__ __forceinline__ void q_b_frag(const uint8_t* row, int c, uint32_t spl
             const uint32_t h = *reinterpret_cast<const uint32_t*>(blk);
             w = __byte_perm(r, h, splice);
         }
-        u4x4_to_h2(w & 0x0F0F0F0Fu, 0x6408 /* 1032 */, b[0], b[1]);
-        u4x4_to_h2((w >> 4) & 0x0F0F0F0Fu, 0x6408, b[2], b[3]);
+        b[0] = w & 0x0F0F0F0Fu;
+        b[1] = (w >> 4) & 0x0F0F0F0Fu;
     }
 }
 
+// d (s32) = a (16 x 32 s8, row-major) . b (32 x 8, s8 or u8) + c.
+template <int KT>
+__device__ __forceinline__ void imma_16832(int* d, const uint32_t* a, const uint32_t* b, const int4& c) {
+    if constexpr (KT == KVM_Q8_0) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c.x), "r"(c.y), "r"(c.z),
+              "r"(c.w));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(c.x), "r"(c.y), "r"(c.z),
+              "r"(c.w));
+    }
+}
+
+// Power of two of one query block: |q| * 2^s <= 32639 (two int8 digits),
+// with the largest element at 2^14 or above when that fits, else 2^13.
+__device__ __forceinline__ int q_block_shift(float amax) {
+    if (!(amax > 0.f)) return 0;
+    const int e = int((__float_as_uint(amax) >> 23) & 255) - 127;  // floor(log2(amax)) for normals
+    int sh = 14 - e;
+    if (ldexpf(amax, sh) > 32639.f) sh = 13 - e;
+    return min(140, max(-96, sh));
+}
+
 constexpr int kQThreads = kLseConsumerWarps * 32;  // no producer warp: 16 warps per SM at 2 CTAs
+// Per-page merge buffers: warps are at most (stages) chunks apart, so a buffer
+// is reused only after the page that last used it has been merged.
+constexpr int kQPageBufs = kMmaMaxStages + 2;
 
 // Shared memory of page_lse_q_kernel beyond its S ring stages.
 __host__ __device__ constexpr size_t q_smem_extra() {
-    return kMmaMaxStages * (sizeof(uint64_t) + 2 * sizeof(uint32_t)) +  // full barriers, release counts, issues
-           2 * 2 * kLseConsumerWarps * 8 * sizeof(float) +              // per-page merge buffers
-           kLseConsumerWarps * 2 * 64 * sizeof(float) +                 // per-warp scale tables (double buffered)
-           16;
+    return 256 +                                                  // barriers and counters
+           kLseConsumerWarps * 8 * 8 * 8 * sizeof(float) +        // per-warp mma C / magic values [kk][g][8]
+           kLseConsumerWarps * 2 * 64 * sizeof(float) +           // per-warp scale tables (double buffered)
+           2 * kQPageBufs * kLseConsumerWarps * 8 * sizeof(float) +  // per-page merge buffers
+           16;                                                    // abort flag
 }
 
 // KK = head_dim / 32 blocks per row; KVH = KV heads (1, 2, 4 or 8).
@@ -111,13 +152,19 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     static_assert(NW % KVH == 0 && (NW & (NW - 1)) == 0, "warps per KV head");
     const uint32_t S = P.stages;
     uint8_t* stages = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * P.stage_stride);
+    // After the ring (128-byte aligned): 256 bytes of barriers and counters, then
+    // 16-byte aligned float arrays.
+    uint8_t* extra = smem + S * P.stage_stride;
+    uint64_t* full = reinterpret_cast<uint64_t*>(extra);           // [kMmaMaxStages]
     uint32_t* released = reinterpret_cast<uint32_t*>(full + kMmaMaxStages);
     uint32_t* issued = released + kMmaMaxStages;
-    float* red_m = reinterpret_cast<float*>(issued + kMmaMaxStages);  // [2][NW][8]
-    float* red_s = red_m + 2 * NW * 8;
-    float* tables = red_s + 2 * NW * 8;  // [NW][2][KK<=8][8 tokens]
-    int* abort_flag = reinterpret_cast<int*>(tables + NW * 2 * 64);
+    uint32_t* arrived = issued + kMmaMaxStages;                     // [kQPageBufs]
+    static_assert(kMmaMaxStages * 16 + kQPageBufs * 4 <= 256, "counter area");
+    float* cstart = reinterpret_cast<float*>(extra + 256);          // [NW][8][8][8]
+    float* tables = cstart + NW * 8 * 8 * 8;                        // [NW][2][8][8]
+    float* red_m = tables + NW * 2 * 64;                            // [kQPageBufs][NW][8]
+    float* red_s = red_m + kQPageBufs * NW * 8;
+    int* abort_flag = reinterpret_cast<int*>(red_s + kQPageBufs * NW * 8);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t units = P.layers * P.pages;
@@ -146,6 +193,7 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
             released[s] = 0;
             issued[s] = 0;
         }
+        for (int b = 0; b < kQPageBufs; ++b) arrived[b] = 0;
         *abort_flag = 0;
         mbar_fence_init();
         for (uint32_t i = 0; i < S && i < total; ++i) issue(i, i / P.chunks, i % P.chunks);
@@ -165,56 +213,63 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     const uint32_t tab_row = (wsub * 8 + (lane & 7)) * slot + head_off;  // scale-table fill: token lane % 8
     const uint32_t jstep = WPH * 8 * slot;
     float* tab = tables + warp * 2 * 64;
+    float* cw = cstart + warp * 8 * 8 * 8;
 
-    uint32_t qa[KK][2][4];
-    float sl2 = 0.f;  // 2^-shift * scale * log2(e)
-    float qinv = 1.f;
-    uint32_t s = 0, phase = 0, ucount = 0, qlayer = 0xffffffffu, tb = 0;
+    uint32_t qa[KK][4];  // A fragments: int8 digits [block][a0..a3]
+    const float sl2 = P.scale * kLog2e;
+    uint32_t s = 0, phase = 0, pb = 0, qlayer = 0xffffffffu, tb = 0;
     // Refill cursor: the chunk S ahead of the one being consumed.
     uint32_t r_idx = S, r_u = S / P.chunks, r_ch = S % P.chunks;
-    for (uint32_t unit = unit_begin; unit < unit_end; ++unit, ++ucount) {
+    for (uint32_t unit = unit_begin; unit < unit_end; ++unit) {
         const uint32_t l = unit / P.pages, p = unit - l * P.pages;
         if (l != qlayer) {
             qlayer = l;
-            float qv[KK][8];
-            float amax = 0.f;
             const uint32_t vg = P.v0 + g, r = gvalid ? vg / P.group : 0, gg = gvalid ? vg % P.group : 0;
             const uint8_t* qp = P.q + l * P.q_layer + r * P.q_row + (kvh * P.group + gg) * P.q_head;
             const uint32_t esz = type_bytes(P.q_type);
+            __syncwarp();
 #pragma unroll
-            for (int kk = 0; kk < KK; ++kk)
+            for (int kk = 0; kk < KK; ++kk) {
+                float qv[8];
+                float amax = 0.f;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int dim = kk * 32 + q_dim<KT>(kk, c, i);
-                    qv[kk][i] = gvalid ? load_scalar(qp + dim * esz, P.q_type) : 0.f;
-                    amax = fmaxf(amax, fabsf(qv[kk][i]));
+                    qv[i] = gvalid ? load_scalar(qp + dim * esz, P.q_type) : 0.f;
+                    amax = fmaxf(amax, fabsf(qv[i]));
                 }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            int shift = 0;
-            if (amax > 0.f) {
-                const int e = int((__float_as_uint(amax) >> 23) & 255) - 127;
-                shift = min(100, max(-100, 13 - e));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                const int sh = q_block_shift(amax);
+                uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+                int dsum_hi = 0, dsum_lo = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int qi = __float2int_rn(ldexpf(qv[i], sh));  // |qi| <= 32639
+                    const int h = (qi + 128) >> 8, lw = qi - (h << 8);  // h, lw in [-128, 127]
+                    hi[i >> 2] |= uint32_t(h & 255) << (8 * (i & 3));
+                    lo[i >> 2] |= uint32_t(lw & 255) << (8 * (i & 3));
+                    dsum_hi += h;
+                    dsum_lo += lw;
+                }
+                qa[kk][0] = hi[0];  // row g,   k 4c..4c+3
+                qa[kk][1] = lo[0];  // row g+8, k 4c..4c+3
+                qa[kk][2] = hi[1];  // row g,   k 16+4c..16+4c+3
+                qa[kk][3] = lo[1];  // row g+8, k 16+4c..16+4c+3
+                // C start (bits of M, minus 8 * digit sum for q4_0) and M of rows g / g+8.
+                dsum_hi += __shfl_xor_sync(0xffffffffu, dsum_hi, 1);
+                dsum_lo += __shfl_xor_sync(0xffffffffu, dsum_lo, 1);
+                dsum_hi += __shfl_xor_sync(0xffffffffu, dsum_hi, 2);
+                dsum_lo += __shfl_xor_sync(0xffffffffu, dsum_lo, 2);
+                if (c == 0) {
+                    const float mh = ldexpf(12582912.f, 8 - sh), ml = ldexpf(12582912.f, -sh);  // 1.5 * 2^(23+k)
+                    const int off_h = KT == KVM_Q4_0 ? -8 * dsum_hi : 0, off_l = KT == KVM_Q4_0 ? -8 * dsum_lo : 0;
+                    const int ch_ = int(__float_as_uint(mh)) + off_h, cl_ = int(__float_as_uint(ml)) + off_l;
+                    *reinterpret_cast<int4*>(cw + (kk * 8 + g) * 8) = make_int4(ch_, ch_, cl_, cl_);
+                    *reinterpret_cast<float4*>(cw + (kk * 8 + g) * 8 + 4) = make_float4(mh, ml, 0.f, 0.f);
+                }
             }
-            const float qs = ldexpf(1.f, shift);
-            qinv = ldexpf(1.f, -shift);
-            sl2 = qinv * P.scale * kLog2e;
-#pragma unroll
-            for (int kk = 0; kk < KK; ++kk)
-#pragma unroll
-                for (int st = 0; st < 2; ++st) {
-                    float h[4], lo[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float x = qv[kk][4 * st + j] * qs;
-                        h[j] = __half2float(__float2half_rn(x));
-                        lo[j] = x - h[j];
-                    }
-                    qa[kk][st][0] = pack_half2(h[0], h[1]);
-                    qa[kk][st][1] = pack_half2(lo[0], lo[1]);
-                    qa[kk][st][2] = pack_half2(h[2], h[3]);
-                    qa[kk][st][3] = pack_half2(lo[2], lo[3]);
-                }
+            __syncwarp();
         }
         float m = -INFINITY, ssum = 0.f;
         const uint64_t tok0 = uint64_t(p) * P.page_tokens;
@@ -247,22 +302,31 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
                     }
                     const float* tsc = tab + tb * 64 + 2 * c;
                     tb ^= 1;
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                    float acc[2] = {0.f, 0.f};  // tokens 2c, 2c+1 of the octet for vector g
                     unroll_kk<KK>([&](auto kkc) {
                         constexpr int kk = decltype(kkc)::value;
-                        uint32_t b[4];
+                        uint32_t b[2];
                         q_b_frag<KT, kk>(brow, c, splice, b);
-                        float blk[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma_16816(blk, qa[kk][0], b[0], b[1]);
-                        mma_16816(blk, qa[kk][1], b[2], b[3]);
+                        const int4 cc = *reinterpret_cast<const int4*>(cw + (kk * 8 + g) * 8);
+                        int dd[4];
+                        imma_16832<KT>(dd, qa[kk], b, cc);
+                        float mh, ml;
+                        if constexpr (KT == KVM_Q8_0) {
+                            mh = __int_as_float(cc.x);
+                            ml = __int_as_float(cc.z);
+                        } else {
+                            const float2 mm = *reinterpret_cast<const float2*>(cw + (kk * 8 + g) * 8 + 4);
+                            mh = mm.x;
+                            ml = mm.y;
+                        }
                         const float2 d = *reinterpret_cast<const float2*>(tsc + kk * 8);  // tokens 2c, 2c+1
-                        acc[0] = fmaf(blk[0], d.x, acc[0]);
-                        acc[1] = fmaf(blk[1], d.y, acc[1]);
-                        acc[2] = fmaf(blk[2], d.x, acc[2]);
-                        acc[3] = fmaf(blk[3], d.y, acc[3]);
+                        acc[0] = fmaf(__int_as_float(dd[0]) - mh, d.x, acc[0]);
+                        acc[1] = fmaf(__int_as_float(dd[1]) - mh, d.y, acc[1]);
+                        acc[0] = fmaf(__int_as_float(dd[2]) - ml, d.x, acc[0]);
+                        acc[1] = fmaf(__int_as_float(dd[3]) - ml, d.y, acc[1]);
                     });
                     if (fast) {
-                        const float x0 = (acc[0] + acc[2]) * sl2, x1 = (acc[1] + acc[3]) * sl2;
+                        const float x0 = acc[0] * sl2, x1 = acc[1] * sl2;
                         const float mn = fmaxf(m, fmaxf(x0, x1));
                         ssum = fmaf(ssum, fast_exp2(m - mn), fast_exp2(x0 - mn) + fast_exp2(x1 - mn));
                         m = mn;
@@ -270,7 +334,7 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
                         const uint64_t t0 = ctok + (wsub + j * WPH) * 8 + 2 * c;
 #pragma unroll
                         for (int jj = 0; jj < 2; ++jj) {
-                            const float dot = (acc[jj] + acc[2 + jj]) * qinv;
+                            const float dot = acc[jj];
                             float x;
                             if (P.softcap > 0.f) x = P.softcap * tanhf(dot * P.scale / P.softcap) * kLog2e;
                             else x = dot * P.scale * kLog2e;
@@ -332,31 +396,40 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
             m = M;
             ssum = Sx;
         }
-        const int buf = ucount & 1;
+        // The last warp to finish the page merges its KV heads' warps (no CTA barrier).
         if (c == 0) {
-            red_m[(buf * NW + warp) * 8 + g] = m;
-            red_s[(buf * NW + warp) * 8 + g] = ssum;
+            red_m[(pb * NW + warp) * 8 + g] = m;
+            red_s[(pb * NW + warp) * 8 + g] = ssum;
         }
-        named_sync(1, NW * 32);
-        if (tid < KVH * 8) {
-            const uint32_t h_kv = tid / 8, v = tid % 8;
-            float M = -INFINITY;
+        __syncwarp();
+        uint32_t before = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            before = atomicAdd(&arrived[pb], 1u);
+        }
+        if ((__shfl_sync(0xffffffffu, before, 0) & (NW - 1)) == NW - 1) {
+            __threadfence_block();
+            for (int idx = lane; idx < KVH * 8; idx += 32) {
+                const uint32_t h_kv = idx / 8, v = idx % 8;
+                float M = -INFINITY;
 #pragma unroll
-            for (int w2 = 0; w2 < WPH; ++w2) M = fmaxf(M, red_m[(buf * NW + h_kv + w2 * KVH) * 8 + v]);
-            float Sx = 0.f;
-            if (M != -INFINITY)
+                for (int w2 = 0; w2 < WPH; ++w2) M = fmaxf(M, red_m[(pb * NW + h_kv + w2 * KVH) * 8 + v]);
+                float Sx = 0.f;
+                if (M != -INFINITY)
 #pragma unroll
-                for (int w2 = 0; w2 < WPH; ++w2) {
-                    const int at = (buf * NW + h_kv + w2 * KVH) * 8 + v;
-                    if (red_s[at] > 0.f) Sx += red_s[at] * fast_exp2(red_m[at] - M);
+                    for (int w2 = 0; w2 < WPH; ++w2) {
+                        const int at = (pb * NW + h_kv + w2 * KVH) * 8 + v;
+                        if (red_s[at] > 0.f) Sx += red_s[at] * fast_exp2(red_m[at] - M);
+                    }
+                if (v < P.nv) {
+                    const uint32_t vg = P.v0 + v, r = vg / P.group, gg = vg % P.group;
+                    const uint32_t h = h_kv * P.group + gg;
+                    P.lse[((uint64_t(l) * P.rows + r) * P.q_heads + h) * P.pages + p] =
+                        Sx > 0.f ? (M + fast_log2(Sx)) * kLn2 : -INFINITY;
                 }
-            if (v < P.nv) {
-                const uint32_t vg = P.v0 + v, r = vg / P.group, gg = vg % P.group;
-                const uint32_t h = h_kv * P.group + gg;
-                P.lse[((uint64_t(l) * P.rows + r) * P.q_heads + h) * P.pages + p] =
-                    Sx > 0.f ? (M + fast_log2(Sx)) * kLn2 : -INFINITY;
             }
         }
+        if (++pb == kQPageBufs) pb = 0;
     }
 
     // After a timeout no copy may still be landing in this CTA's shared memory when it exits.
