@@ -220,12 +220,13 @@ void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
                     2 * 2 * kLseConsumerWarps * 8 * sizeof(float) + 16;
 }
 
-// Quantised-key scorer: the K heads of a token are split into groups of hpg
-// heads whose row bytes are a multiple of 16 and fit one TMA box row (<= 255
-// u64 elements with the pad); each group's rows land in shared memory at a
-// stride of an odd number of 16-byte units (pad = 0 or 16 zero-filled bytes).
-// A chunk is 8 tokens per warp of a KV head (2 octets when that keeps the
-// stage within 20 KiB); stages fill ~100 KiB so two CTAs share an SM.
+// Quantised-key scorer: the K heads of a token are split into the smallest
+// groups of hpg heads whose row bytes are a multiple of 16 and fit one TMA box
+// row (<= 255 u64 elements with the pad); each group has its own ring, its rows
+// land in shared memory at a stride of an odd number of 16-byte units (pad = 0
+// or 16 zero-filled bytes). A chunk is 8 tokens per warp of a KV head; the
+// rings and the kernel's other shared memory fill ~112 KiB so two CTAs share
+// an SM.
 void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
     if (force_simt() || scorer_is("mma_generic")) return;
     if (k->type != KVM_Q8_0 && k->type != KVM_Q4_0) return;
@@ -233,24 +234,23 @@ void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
     if (kvh == 0 || 8 % kvh) return;
     const uint64_t rb = row_bytes_of(k->type, d->head_dim);
     uint32_t hpg = 0, pad = 0;
-    for (uint32_t h = kvh; h >= 1; h >>= 1) {
+    for (uint32_t h = 1; h <= kvh; h <<= 1) {
         const uint64_t gb = h * rb;
         if (kvh % h || gb % 16) continue;
         const uint32_t pd = (gb / 16) % 2 ? 0 : 16;
-        if ((gb + pd) / 8 > 255) continue;
+        if ((gb + pd) / 8 > 255) break;
         hpg = h;
         pad = pd;
         break;
     }
     if (!hpg) return;
     const uint32_t slot = uint32_t(hpg * rb + pad), groups = kvh / hpg;
-    const uint32_t wph = kLseConsumerWarps / kvh;
-    uint32_t tpc = 8 * wph;
-    if (d->page_tokens % tpc || tpc > 256) return;
-    if (d->page_tokens % (2 * tpc) == 0 && 2 * tpc <= 256 && uint64_t(2 * tpc) * slot * groups <= 20 * 1024) tpc *= 2;
-    const uint64_t stage = uint64_t(tpc) * slot * groups;
+    const uint32_t tpc = 8 * (kLseConsumerWarps / kvh);
+    if (d->page_tokens % tpc || tpc > 256 || groups > uint32_t(kQMaxGroups)) return;
+    const uint64_t stage = uint64_t(tpc) * slot;
     const uint32_t stride = uint32_t((stage + 127) / 128 * 128);
-    const uint32_t stages = uint32_t(std::min<uint64_t>(kMmaMaxStages, (100 * 1024) / stride));
+    const uint64_t budget = 112 * 1024 - q_smem_extra();
+    const uint32_t stages = uint32_t(std::min<uint64_t>(kMmaMaxStages, budget / (uint64_t(groups) * stride)));
     if (stages < 2) return;
     cfg->q = true;
     cfg->q_tpc = tpc;
@@ -261,7 +261,7 @@ void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
     cfg->q_stage_stride = stride;
     cfg->q_stages = stages;
     cfg->q_tx = uint32_t(stage);
-    cfg->q_smem = size_t(stages) * stride + q_smem_extra();
+    cfg->q_smem = size_t(groups) * stages * stride + q_smem_extra();
 }
 
 bool supported_type(int t) { return t >= KVM_F32 && t <= KVM_Q5_0; }

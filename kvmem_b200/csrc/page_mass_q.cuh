@@ -125,10 +125,12 @@ constexpr int kQThreads = kLseConsumerWarps * 32;  // no producer warp: 16 warps
 // Per-page merge buffers: warps are at most (stages) chunks apart, so a buffer
 // is reused only after the page that last used it has been merged.
 constexpr int kQPageBufs = kMmaMaxStages + 2;
+constexpr int kQMaxGroups = 8;      // head groups, each with its own ring
+constexpr int kQCounterBytes = 1280;  // barriers and counters
 
 // Shared memory of page_lse_q_kernel beyond its S ring stages.
 __host__ __device__ constexpr size_t q_smem_extra() {
-    return 256 +                                                  // barriers and counters
+    return kQCounterBytes +                                       // barriers and counters
            kLseConsumerWarps * 8 * 8 * 8 * sizeof(float) +        // per-warp mma C / magic values [kk][g][8]
            kLseConsumerWarps * 2 * 64 * sizeof(float) +           // per-warp scale tables (double buffered)
            2 * kQPageBufs * kLseConsumerWarps * 8 * sizeof(float) +  // per-page merge buffers
@@ -151,16 +153,17 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     constexpr uint32_t kRow = uint32_t(kBlock * KK);
     static_assert(NW % KVH == 0 && (NW & (NW - 1)) == 0, "warps per KV head");
     const uint32_t S = P.stages;
-    uint8_t* stages = smem;
-    // After the ring (128-byte aligned): 256 bytes of barriers and counters, then
-    // 16-byte aligned float arrays.
-    uint8_t* extra = smem + S * P.stage_stride;
-    uint64_t* full = reinterpret_cast<uint64_t*>(extra);           // [kMmaMaxStages]
-    uint32_t* released = reinterpret_cast<uint32_t*>(full + kMmaMaxStages);
-    uint32_t* issued = released + kMmaMaxStages;
-    uint32_t* arrived = issued + kMmaMaxStages;                     // [kQPageBufs]
-    static_assert(kMmaMaxStages * 16 + kQPageBufs * 4 <= 256, "counter area");
-    float* cstart = reinterpret_cast<float*>(extra + 256);          // [NW][8][8][8]
+    const uint32_t NG = P.groups_tma;  // head groups: one ring of S stages each
+    uint8_t* stages = smem;            // [NG][S] stages of stage_stride bytes
+    // After the rings (128-byte aligned): barriers and counters, then 16-byte
+    // aligned float arrays.
+    uint8_t* extra = smem + NG * S * P.stage_stride;
+    uint64_t* full = reinterpret_cast<uint64_t*>(extra);  // [kQMaxGroups][kMmaMaxStages]
+    uint32_t* released = reinterpret_cast<uint32_t*>(full + kQMaxGroups * kMmaMaxStages);
+    uint32_t* issued = released + kQMaxGroups * kMmaMaxStages;
+    uint32_t* arrived = issued + kQMaxGroups * kMmaMaxStages;  // [kQPageBufs]
+    static_assert(kQMaxGroups * kMmaMaxStages * 16 + kQPageBufs * 4 <= kQCounterBytes, "counter area");
+    float* cstart = reinterpret_cast<float*>(extra + kQCounterBytes);  // [NW][8][8][8]
     float* tables = cstart + NW * 8 * 8 * 8;                        // [NW][2][8][8]
     float* red_m = tables + NW * 2 * 64;                            // [kQPageBufs][NW][8]
     float* red_s = red_m + kQPageBufs * NW * 8;
@@ -173,30 +176,30 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     const uint32_t total = (unit_end - unit_begin) * P.chunks;  // chunks of this CTA
     const uint64_t policy = policy_evict_first();
 
-    // Chunk ch of page unit_begin + u into stage s: one tiled box per head group,
-    // tokens x (the group's row bytes + zero-filled pad columns) -> rows of
-    // slot_stride bytes, group after group.
-    auto issue = [&](uint32_t s, uint32_t u, uint32_t ch) {
+    // Chunk ch of page unit_begin + u of head group gi into its stage s: one
+    // tiled box, tokens x (the group's row bytes [+ zero-filled pad columns]).
+    auto issue = [&](uint32_t gi, uint32_t s, uint32_t u, uint32_t ch) {
         const uint32_t unit = unit_begin + u;
         const uint32_t l = unit / P.pages, p = unit - l * P.pages;
         const int tok = int(p * P.page_tokens + ch * P.tpc);
-        uint8_t* dst = stages + s * P.stage_stride;
-        mbar_arrive_expect_tx(&full[s], P.chunk_bytes);
-        for (uint32_t grp = 0; grp < P.groups_tma; ++grp)
-            tma_load_4d(dst + grp * P.tpc * P.slot_stride, &kmap, 0, int(grp), tok, int(l), &full[s], policy);
-        ++issued[s];
+        const uint32_t at = gi * kMmaMaxStages + s;
+        mbar_arrive_expect_tx(&full[at], P.chunk_bytes);
+        tma_load_4d(stages + (gi * S + s) * P.stage_stride, &kmap, 0, int(gi), tok, int(l), &full[at], policy);
+        ++issued[at];
     };
 
     if (tid == 0) {
-        for (uint32_t s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            released[s] = 0;
-            issued[s] = 0;
-        }
+        for (uint32_t gi = 0; gi < NG; ++gi)
+            for (uint32_t s = 0; s < S; ++s) {
+                mbar_init(&full[gi * kMmaMaxStages + s], 1);
+                released[gi * kMmaMaxStages + s] = 0;
+                issued[gi * kMmaMaxStages + s] = 0;
+            }
         for (int b = 0; b < kQPageBufs; ++b) arrived[b] = 0;
         *abort_flag = 0;
         mbar_fence_init();
-        for (uint32_t i = 0; i < S && i < total; ++i) issue(i, i / P.chunks, i % P.chunks);
+        for (uint32_t gi = 0; gi < NG; ++gi)
+            for (uint32_t i = 0; i < S && i < total; ++i) issue(gi, i, i / P.chunks, i % P.chunks);
     }
     __syncthreads();
 
@@ -208,7 +211,12 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     const uint32_t myr = gvalid ? (P.v0 + g) / P.group : 0;
     const uint32_t slot = P.slot_stride;
     const uint32_t nj = P.tpc / (8 * WPH);
-    const uint32_t head_off = (kvh / P.hpg) * P.tpc * slot + (kvh % P.hpg) * kRow;
+    const uint32_t gi = kvh / P.hpg;                 // this warp's head group (ring)
+    const uint32_t gwarps = WPH * P.hpg;             // warps that release each stage of the ring
+    uint8_t* ring = stages + gi * S * P.stage_stride;
+    uint64_t* gfull = full + gi * kMmaMaxStages;
+    uint32_t* greleased = released + gi * kMmaMaxStages;
+    const uint32_t head_off = (kvh % P.hpg) * kRow;
     const uint32_t lane_b = (wsub * 8 + g) * slot + head_off;             // code row: token g of the octet
     const uint32_t tab_row = (wsub * 8 + (lane & 7)) * slot + head_off;  // scale-table fill: token lane % 8
     const uint32_t jstep = WPH * 8 * slot;
@@ -276,13 +284,13 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
 
         for (uint32_t ch = 0; ch < P.chunks; ++ch) {
             bool ok = !*reinterpret_cast<volatile int*>(abort_flag);
-            if (ok && !mbar_wait(&full[s], phase)) {
+            if (ok && !mbar_wait(&gfull[s], phase)) {
                 record_error(P.status, KVM_ERR_TIMEOUT, 6);
                 *reinterpret_cast<volatile int*>(abort_flag) = 1;
                 ok = false;
             }
             if (ok) {
-                const uint8_t* stage = stages + s * P.stage_stride;
+                const uint8_t* stage = ring + s * P.stage_stride;
                 const uint64_t ctok = tok0 + uint64_t(ch) * P.tpc;
                 const bool fast = !MASK && P.softcap <= 0.f && ctok + P.tpc <= P.tokens;
                 for (uint32_t j = 0; j < nj; ++j) {
@@ -360,16 +368,16 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
                     }
                 }
             }
-            // Release the stage; the last warp to release it refills it S chunks ahead.
+            // Release the stage; the last of the group's warps to release it refills it S chunks ahead.
             __syncwarp();
             if (lane == 0) {
                 __threadfence_block();
-                const uint32_t before = atomicAdd(&released[s], 1u);
-                if ((before & (NW - 1)) == NW - 1 && r_idx < total &&
+                const uint32_t before = atomicAdd(&greleased[s], 1u);
+                if ((before & (gwarps - 1)) == gwarps - 1 && r_idx < total &&
                     !*reinterpret_cast<volatile int*>(abort_flag)) {
                     __threadfence_block();
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue(s, r_u, r_ch);
+                    issue(gi, s, r_u, r_ch);
                 }
             }
             ++r_idx;
@@ -435,8 +443,12 @@ __global__ void __launch_bounds__(kQThreads, 2) page_lse_q_kernel(const __grid_c
     // After a timeout no copy may still be landing in this CTA's shared memory when it exits.
     __syncthreads();
     if (tid == 0 && *reinterpret_cast<volatile int*>(abort_flag)) {
-        for (uint32_t st = 0; st < S; ++st)
-            if (issued[st] && !mbar_wait(&full[st], (issued[st] - 1) & 1)) record_error(P.status, KVM_ERR_TIMEOUT, 5);
+        for (uint32_t gr = 0; gr < NG; ++gr)
+            for (uint32_t st = 0; st < S; ++st) {
+                const uint32_t at = gr * kMmaMaxStages + st;
+                if (issued[at] && !mbar_wait(&full[at], (issued[at] - 1) & 1))
+                    record_error(P.status, KVM_ERR_TIMEOUT, 5);
+            }
     }
 }
 

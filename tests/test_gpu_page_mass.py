@@ -139,6 +139,37 @@ def test_quantised_keys_with_mask(ctx, scorer, ktype):
     run_case(ctx, ktype=ktype, D=256, Hq=24, Hkv=4, R=R, page=page, T=T, mask=mask, seed=3)
 
 
+@pytest.mark.parametrize("ktype", [U.Q8_0, U.Q4_0])
+def test_quantised_keys_with_outlier_queries(ctx, scorer, ktype):
+    """Query channels 30x / 100x the rest, vectors scaled by 1e-3 and 30, and all-zero blocks:
+    the quantised-key scorer splits each 32-element query block into two int8 digits under
+    the block's own power of two, so small elements next to an outlier keep 2^-15 of the
+    outlier's magnitude; page masses must still meet the 1e-3 relative bound."""
+    import kvmem_b200 as K
+    rng = np.random.default_rng(11)
+    L, R, Hq, Hkv, D, T, page = 2, 2, 24, 4, 256, 1024, 256
+    q = rng.standard_normal((L, R, Hq, D)).astype(np.float32)
+    q[..., [5, 77, 200]] *= 30.0
+    q[..., 130] *= 100.0
+    q[:, 0, 0] *= 1e-3
+    q[:, 1, 1] *= 30.0
+    q[:, :, 2, 32:64] = 0.0  # one block of zeros
+    qb = U.encode(q, U.F32).reshape(L, R, Hq, -1)
+    kb = U.make_k(rng, ktype, L, T, Hkv, D)
+    dev = torch.device("cuda", 0)
+    k_d = torch.from_numpy(kb.reshape(-1).copy()).to(dev)
+    q_d = torch.from_numpy(q.copy()).to(dev)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=page)
+    rows, _ = ctx.score_pages(desc, K.RecallContext.make_query(q_d, R),
+                              K.RecallContext.make_kcache(k_d, ktype, kv_heads=Hkv, head_dim=D, capacity_tokens=T))
+    torch.cuda.synchronize()
+    ctx.check_status("score_pages")
+    exp = O.page_mass(qb, U.F32, kb, ktype, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                      page_tokens=page, scale=float(np.float32(1.0) / np.sqrt(np.float32(D))))
+    ok, worst, nbad = U.close(rows.cpu().numpy(), exp, REL, ABS)
+    assert ok, f"worst {worst:.3g}, {nbad} pages out of tolerance"
+
+
 def test_unsupported_layouts_are_rejected(ctx):
     import kvmem_b200 as K
     dev = torch.device("cuda", 0)
