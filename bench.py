@@ -297,7 +297,7 @@ def run_sharded(args, w, world, rank, local):
                    "step": "sharded selection (two NCCL all-gathers); stage-in not included",
                    "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)"},
         "clocks": clk.summary(), "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "page_lse_mma_kernel (local pages)", "kernel_ms": kernel_ms,
+        "roofline": {"bound": "hbm", "kernel": "page_lse_q_kernel (local pages)", "kernel_ms": kernel_ms,
                      "achieved": kbytes_local / (kernel_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
                      "frac": kbytes_local / (kernel_ms * 1e-3) / 1e9 / hbm_peak, "peak_source": src,
                      "algorithmic_bytes": kbytes_local, "step_GBps_all_ranks": total_bytes / (ms * 1e-3) / 1e9},
@@ -643,7 +643,9 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": world * token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "page_lse_kernel (+page_mass_normalize_kernel)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("page_lse_mma_kernel" if w.k_type == 1 else "page_lse_q_kernel")
+                               + " (+page_mass_normalize_kernel)",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": peak_src, "traffic": traffic, "kernel_ms": kernel_ms,
                      "algorithmic_bytes": kbytes},
