@@ -136,26 +136,32 @@ __device__ __forceinline__ uint32_t tc_sw128_offset(uint32_t row, uint32_t k) {
 __host__ __device__ constexpr int tc_layout_for(uint32_t nv) { return nv <= 128 ? 1 : 2; }
 constexpr uint32_t kTcMaxVectors = 160;
 
-// Tensor-memory columns (512 allocated): tile-0 accumulators double buffered
-// at [0, 256), the packed tile's accumulator at [256, 384), the tile-0 query
-// operand (fp16 hi at [384, 384 + D/2), lo after it) at the top.
+// Tensor-memory columns (512 allocated). Layout 1: tile-0 accumulators triple
+// buffered at [0, 384), the tile-0 query operand (fp16 hi at [384, 384 + D/2),
+// lo after it) at the top. Layout 2: tile-0 accumulators double buffered at
+// [0, 256), the packed tile's accumulators double buffered at [256, 384) and
+// [384, 512); the tile-0 query operand lives in shared memory.
 constexpr uint32_t kTcColPacked = 256;
 constexpr uint32_t kTcColQ = 384;
 
-// Shared memory of the packed tile's query operand (layout 2).
-__host__ __device__ constexpr uint32_t tc_q_bytes(int KA, int LM) { return LM == 2 ? uint32_t(KA) * kTcAtomBytes : 0u; }
+// Shared memory of the query operands of layout 2: the packed tile (KA atoms),
+// then the tile-0 hi parts (KA atoms) and lo parts (KA atoms).
+__host__ __device__ constexpr uint32_t tc_q_bytes(int KA, int LM) {
+    return LM == 2 ? 3u * uint32_t(KA) * kTcAtomBytes : 0u;
+}
 
 // Dynamic shared memory of the kernel: alignment pad, packed query tile, K
 // stages, mbarriers (2 x kTcMaxStages + 10), TMEM address slot and abort flag.
 constexpr size_t kTcSmemMax = 227 * 1024;
 __host__ __device__ constexpr size_t tc_smem_bytes(int KA, int LM, uint32_t stages) {
-    return 1024 + tc_q_bytes(KA, LM) + size_t(stages) * KA * kTcAtomBytes + (2 * kTcMaxStages + 10) * 8 + 16;
+    return 1024 + tc_q_bytes(KA, LM) + size_t(stages) * KA * kTcAtomBytes + (2 * kTcMaxStages + 12) * 8 + 16;
 }
 
-// Threads per CTA: producer warp, MMA warp, one tile-0 epilogue warp per TMEM
-// lane quadrant, and (layout 2) one packed-tile epilogue warp per quadrant
-// (at most 320 threads, so the compiler may use up to 168 registers).
-__host__ __device__ constexpr int tc_threads(int LM) { return LM == 1 ? 192 : 320; }
+// Threads per CTA: producer warp, MMA warp, two sets of tile-0 epilogue
+// warps (one warp per TMEM lane quadrant each; the sets take alternate units),
+// and (layout 2) one packed-tile epilogue warp per quadrant. At 448 threads
+// (four warps on two SM sub-partitions) each thread may use 128 registers.
+__host__ __device__ constexpr int tc_threads(int LM) { return LM == 1 ? 320 : 448; }
 
 // Units per (layer, KV head): one 128-token tile when pages are <= 128 tokens,
 // one page (page_tokens / 128 tiles) when they are larger.
@@ -382,16 +388,18 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
     constexpr uint32_t NB = LM == 1 ? 3 : 2;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-    uint8_t* qsm = smem_raw + pad;  // packed query tile (layout 2)
+    uint8_t* qsm = smem_raw + pad;                 // packed query tile (layout 2)
+    uint8_t* q0hi = qsm + KA * kTcAtomBytes;       // tile-0 query operand, hi parts (layout 2)
+    uint8_t* q0lo = q0hi + KA * kTcAtomBytes;      // tile-0 query operand, lo parts (layout 2)
     uint8_t* ksm = qsm + kQBytes;
     const uint32_t S = P.stages;
     uint64_t* kfull = reinterpret_cast<uint64_t*>(ksm + S * kStageBytes);
     uint64_t* kempty = kfull + kTcMaxStages;
     uint64_t* tfull = kempty + kTcMaxStages;  // [NB] tile-0 accumulators written
     uint64_t* tempty = tfull + 3;             // [NB] tile-0 accumulators read
-    uint64_t* pfull = tempty + 3;             // packed accumulator written
-    uint64_t* pempty = pfull + 1;             // packed accumulator read
-    uint64_t* qfree = pempty + 1;             // MMAs reading the tile-0 query operand are done
+    uint64_t* pfull = tempty + 3;             // [2] packed accumulators written
+    uint64_t* pempty = pfull + 2;             // [2] packed accumulators read
+    uint64_t* qfree = pempty + 2;             // MMAs reading the tile-0 query operand are done
     uint64_t* qready = qfree + 1;             // tile-0 query operand written
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qready + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -409,17 +417,19 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], warps0);
         }
-        mbar_init(pfull, 1);
-        mbar_init(pempty, warps1 ? warps1 : 1);
+        for (int pb = 0; pb < 2; ++pb) {
+            mbar_init(&pfull[pb], 1);
+            mbar_init(&pempty[pb], warps1 ? warps1 : 1);
+        }
         mbar_init(qfree, 1);
         mbar_init(qready, warps0 + warps1);
         *abort_flag = 0;
         mbar_fence_init();
     }
     if constexpr (LM == 2) {
-        // Rows of the packed query tile that no vector uses stay zero.
+        // Rows of the query tiles that no vector uses stay zero.
         uint4* z = reinterpret_cast<uint4*>(qsm);
-        for (uint32_t i = tid; i < KA * kTcAtomBytes / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+        for (uint32_t i = tid; i < kQBytes / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == 1) {
@@ -487,7 +497,9 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
             bool pend = false;
             int err = 0;
             auto issue_packed = [&]() -> bool {
-                if (pend_it >= 1 && !mbar_wait(pempty, (pend_it - 1) & 1)) return false;
+                // Packed accumulator pend_it % 2, free once the epilogue read its use two tiles ago.
+                const uint32_t pb = pend_it & 1;
+                if (pend_it >= 2 && !mbar_wait(&pempty[pb], ((pend_it - 2) >> 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t kbase = smem_u32(ksm + pend_s * kStageBytes), qp0 = smem_u32(qsm);
 #pragma unroll
@@ -495,10 +507,10 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t off = a * kTcAtomBytes + kk * 32;
-                        tc_mma(tmem + kTcColPacked, tc_desc_sw128(qp0 + off), tc_desc_sw128(kbase + off), idesc,
+                        tc_mma(tmem + kTcColPacked + pb * kTcTile, tc_desc_sw128(qp0 + off), tc_desc_sw128(kbase + off), idesc,
                                (a | kk) != 0);
                     }
-                tc_commit(pfull);
+                tc_commit(&pfull[pb]);
                 tc_commit(&kempty[pend_s]);
                 last = pend_it;
                 pend = false;
@@ -543,16 +555,29 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     tc_fence_after();
                     const uint32_t kbase = smem_u32(ksm + s * kStageBytes);
                     const uint32_t d0 = tmem + b * kTcTile;
-                    const uint32_t qhi = tmem + kTcColQ, qlo = tmem + kTcColQ + D / 2;
+                    if constexpr (LM == 1) {
+                        const uint32_t qhi = tmem + kTcColQ, qlo = tmem + kTcColQ + D / 2;
 #pragma unroll
-                    for (int a = 0; a < KA; ++a)
+                        for (int a = 0; a < KA; ++a)
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const uint64_t bd = tc_desc_sw128(kbase + a * kTcAtomBytes + kk * 32);
-                            const uint32_t acol = (a * 4 + kk) * 8;  // 16 fp16 = 8 columns per k-step
-                            tc_mma_ts(d0, qhi + acol, bd, idesc, (a | kk) != 0);
-                            tc_mma_ts(d0, qlo + acol, bd, idesc, 1);
-                        }
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint64_t bd = tc_desc_sw128(kbase + a * kTcAtomBytes + kk * 32);
+                                const uint32_t acol = (a * 4 + kk) * 8;  // 16 fp16 = 8 columns per k-step
+                                tc_mma_ts(d0, qhi + acol, bd, idesc, (a | kk) != 0);
+                                tc_mma_ts(d0, qlo + acol, bd, idesc, 1);
+                            }
+                    } else {
+                        const uint32_t qh = smem_u32(q0hi), ql = smem_u32(q0lo);
+#pragma unroll
+                        for (int a = 0; a < KA; ++a)
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint32_t off = a * kTcAtomBytes + kk * 32;
+                                const uint64_t bd = tc_desc_sw128(kbase + off);
+                                tc_mma(d0, tc_desc_sw128(qh + off), bd, idesc, (a | kk) != 0);
+                                tc_mma(d0, tc_desc_sw128(ql + off), bd, idesc, 1);
+                            }
+                    }
                     tc_commit(&tfull[b]);  // tile-0 accumulator ready for the epilogue
                     if constexpr (LM == 2) {
                         if (pend && !issue_packed()) {
@@ -587,13 +612,16 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
         }
     } else {
         // ---- epilogue ----
-        // Warps 2..5: tile 0, one thread per query vector (TMEM lane), all
-        // 128 columns of every tile; they also write the tile-0 query operand
-        // of their vectors. Warps 6..9 (layout 2): the packed vectors
-        // 128+8q+g, four threads per vector (token pairs 2(t%4)+j of every 8
-        // columns), and the packed query rows.
+        // Warps 2..5 and 6..9: tile 0, one thread per query vector (TMEM lane),
+        // all 128 columns of a tile; the two sets take alternate units (whole
+        // pages), so each has two tiles' time per tile and no page is split
+        // between warps. Warps 2..5 also write the tile-0 query operand of their
+        // vectors. Warps 10..13 (layout 2): the packed vectors 128+8q+g, four
+        // threads per vector (token pairs 2(t%4)+j of every 8 columns), and the
+        // packed query rows.
         const int q = warp % 4;
-        const bool packed = warp >= 6;
+        const bool packed = warp >= 10;
+        const uint32_t set = (!packed && warp >= 6) ? 1u : 0u;
         const int g = packed ? lane >> 2 : lane, c4 = lane & 3;
         const uint32_t v = packed ? kTcTile + 8 * q + g : 32 * q + lane;
         const bool warp_active = packed ? kTcTile + 8 * q < V : 32u * q < V;
@@ -614,7 +642,9 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
             float* lse_row = P.lse;
             TcUnit un(ub, upl, P.kv_heads);
             bool stop = false;
-            for (uint64_t u = ub; u < ue && !stop; ++u, un.next()) {
+            uint32_t k = 0;  // unit ordinal in this CTA (its parity picks the tile-0 set)
+            for (uint64_t u = ub; u < ue && !stop; ++u, un.next(), ++k) {
+                const bool mine = packed || (k & 1u) == set;
                 if (u == ub || un.j == 0) {
                     const uint32_t hq = un.h * G + gsub;
                     const uint8_t* qp = P.q + un.l * P.q_layer + r * P.q_row + hq * P.q_head;
@@ -660,7 +690,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                         __syncwarp();
                         if (lane == 0) mbar_arrive(qready);
                     }
-                    if (!packed) {
+                    if (!packed && set == 0) {
                         // Tile-0 query operand of this lane's vector (zeros past V),
                         // once the MMAs reading the previous one are done.
                         int ok = 1;
@@ -672,10 +702,36 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                             *abort_flag = 1;
                             break;
                         }
-                        tc_fence_after();
-                        tc_write_query_row<D>(qbase, qp, P.q_type, shift, vvalid);
-                        tc_wait_st();
-                        tc_fence_before();
+                        if constexpr (LM == 1) {
+                            tc_fence_after();
+                            tc_write_query_row<D>(qbase, qp, P.q_type, shift, vvalid);
+                            tc_wait_st();
+                            tc_fence_before();
+                        } else {
+                            // Row v of the shared-memory tile-0 operand: hi and lo parts,
+                            // 16-byte swizzled pieces (zeros when !vvalid).
+                            const float qs = ldexpf(1.f, shift);
+                            const uint32_t esz = type_bytes(P.q_type);
+#pragma unroll 1
+                            for (uint32_t d8 = 0; d8 < D; d8 += 8) {
+                                const uint32_t at = d8 / 64, k0 = d8 % 64;
+                                uint32_t hw[4], lw[4];
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    float x0 = 0.f, x1 = 0.f;
+                                    if (vvalid) {
+                                        x0 = load_scalar(qp + (d8 + 2 * i) * esz, P.q_type) * qs;
+                                        x1 = load_scalar(qp + (d8 + 2 * i + 1) * esz, P.q_type) * qs;
+                                    }
+                                    tc_split2(x0, x1, hw[i], lw[i]);
+                                }
+                                const uint32_t off = at * kTcAtomBytes + tc_sw128_offset(v, k0);
+                                *reinterpret_cast<uint4*>(q0hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                                *reinterpret_cast<uint4*>(q0lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                            }
+                            // Generic-proxy stores -> visible to the tensor cores (async proxy).
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(qready);
                     }
@@ -686,8 +742,9 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                         tb = 0;
                         ++tround;
                     }
-                    uint64_t* full = packed ? pfull : &tfull[b];
-                    const uint32_t parity = packed ? (it & 1) : ((it - b) / NB) & 1;
+                    if (!mine) continue;  // the other tile-0 set's unit
+                    uint64_t* full = packed ? &pfull[it & 1] : &tfull[b];
+                    const uint32_t parity = packed ? (it >> 1) & 1 : ((it - b) / NB) & 1;
                     int ok = 1;
                     if (lane == 0) {
                         if (*abort_flag) ok = 0;
@@ -705,7 +762,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     tc_fence_after();
                     const uint64_t tok0 = (uint64_t(un.j) * ut + t) * kTcTile;
                     const uint32_t tbase =
-                        tmem + (uint32_t(32 * q) << 16) + (packed ? kTcColPacked : b * kTcTile);
+                        tmem + (uint32_t(32 * q) << 16) + (packed ? kTcColPacked + (it & 1) * kTcTile : b * kTcTile);
                     const bool fast = !MASK && !(P.softcap > 0.f) && tok0 + kTcTile <= P.tokens;
                     const bool last_tile = t + 1 == ut;
                     // Folds one 32-token chunk `ch` of this tile (n dots of this thread, or,
@@ -744,19 +801,32 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                             st = TcLse{};
                         }
                     };
-                    uint32_t ra[32], rb[32];
+                    uint32_t ra[32];
                     if (!packed) {
-                        // Four 32-column chunks, each loaded while the one before is folded.
-                        tc_ld32(tbase, ra);
-                        tc_wait_ld(ra);
+                        if constexpr (LM == 1) {
+                            // Four 32-column chunks, each loaded while the one before is folded.
+                            uint32_t rb[32];
+                            tc_ld32(tbase, ra);
+                            tc_wait_ld(ra);
 #pragma unroll 1
-                        for (int ch = 0; ch < 4; ch += 2) {
-                            tc_ld32(tbase + (ch + 1) * 32, rb);
-                            chunk(reinterpret_cast<const float*>(ra), 32, ch, false, tbase + ch * 32, 0);
-                            tc_wait_ld_after(rb, st.m, st.s);
-                            if (ch + 2 < 4) tc_ld32(tbase + (ch + 2) * 32, ra);
-                            chunk(reinterpret_cast<const float*>(rb), 32, ch + 1, false, tbase + (ch + 1) * 32, 0);
-                            if (ch + 2 < 4) tc_wait_ld_after(ra, st.m, st.s);
+                            for (int ch = 0; ch < 4; ch += 2) {
+                                tc_ld32(tbase + (ch + 1) * 32, rb);
+                                chunk(reinterpret_cast<const float*>(ra), 32, ch, false, tbase + ch * 32, 0);
+                                tc_wait_ld_after(rb, st.m, st.s);
+                                if (ch + 2 < 4) tc_ld32(tbase + (ch + 2) * 32, ra);
+                                chunk(reinterpret_cast<const float*>(rb), 32, ch + 1, false, tbase + (ch + 1) * 32,
+                                      0);
+                                if (ch + 2 < 4) tc_wait_ld_after(ra, st.m, st.s);
+                            }
+                        } else {
+                            // 128 registers per thread at 448 threads: one chunk at a time (the
+                            // other tile-0 set and the packed warp cover the load latency).
+#pragma unroll 1
+                            for (int ch = 0; ch < 4; ++ch) {
+                                tc_ld32(tbase + ch * 32, ra);
+                                tc_wait_ld_after(ra, st.m, st.s);
+                                chunk(reinterpret_cast<const float*>(ra), 32, ch, false, tbase + ch * 32, 0);
+                            }
                         }
                     } else {
                         // 16x256b loads of 64 columns; hi (lane g) + lo (lane g+8) per dot.
@@ -779,7 +849,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     }
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(packed ? pempty : &tempty[b]);
+                    if (lane == 0) mbar_arrive(packed ? &pempty[it & 1] : &tempty[b]);
                 }
             }
         }
