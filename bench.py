@@ -67,7 +67,12 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms around the timed region.
+
+    The timed region starts only after the first sample has arrived and the sampler
+    keeps running until one sample after the region has arrived, so even a region
+    shorter than the sampling period is bracketed by samples; the summary uses the
+    samples taken within 250 ms of the region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -76,28 +81,44 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.rows = []  # (host time, csv fields)
+        self.t_begin = self.t_end = 0.0
+
+    def _read(self):
+        for line in self.proc.stdout:
+            r = next(csv.reader([line]), [])
+            if len(r) >= 9:
+                self.rows.append((time.time(), r))
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+        self.t_begin = time.time()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        self.t_end = time.time()
         if self.proc:
+            while not any(t >= self.t_end for t, _ in self.rows) and time.time() - self.t_end < 1.0:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
 
     def summary(self):
-        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        near = [r for t, r in self.rows if self.t_begin - 0.25 <= t <= self.t_end + 0.25]
+        rows = near or [r for _, r in self.rows]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
