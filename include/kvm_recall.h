@@ -290,7 +290,11 @@ int kvm_stagein_pool(kvm_ctx* ctx, kvm_pool* pool, const kvm_stage_layout* layou
 
 /* Explicit copy list (the form of kvmem_stagein_enqueue_v / kvmem_d2d_batched,
  * src/adapter/llama-kvmem-stagein.cu:861,1006): n host ops {src, dst, bytes};
- * src may be mapped pinned host or device memory, dst device memory. */
+ * src may be mapped pinned host or device memory, dst device memory.
+ * Asynchronous on `stream`: the ops are copied into one of the context's two
+ * mapped pinned lists (the caller's array may be reused on return); a call
+ * waits only when both lists are still read by gathers in flight (bounded:
+ * KVM_ERR_TIMEOUT after 30 s). */
 typedef struct kvm_copy {
     const void* src;
     void* dst;

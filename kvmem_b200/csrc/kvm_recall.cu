@@ -645,6 +645,10 @@ int kvm_ctx_destroy(kvm_ctx* c) {
     if (c->ws && !c->ws_borrowed) cudaFree(c->ws);
     if (c->small) cudaFree(c->small);
     if (c->aux) cudaFree(c->aux);
+    for (auto& L : c->copy_lists) {
+        if (L.done) cudaEventDestroy(L.done);
+        if (L.host) cudaFreeHost(L.host);
+    }
     delete c;
     return KVM_OK;
 }
@@ -803,18 +807,43 @@ int kvm_stagein_copies(kvm_ctx* c, const kvm_copy* ops, uint32_t n, uint32_t cta
         if (!ops[i].src || !ops[i].dst || !ops[i].bytes) return KVM_ERR_INVALID_ARGUMENT;
     DeviceGuard guard(c->device);
     auto s = static_cast<cudaStream_t>(stream);
-    const size_t off = keep_area(c);
-    KVM_TRY(ensure_small(c, off + size_t(n) * sizeof(CopyOp)));
-    auto* dev_ops = reinterpret_cast<CopyOp*>(static_cast<uint8_t*>(c->small) + off);
     static_assert(sizeof(CopyOp) == sizeof(kvm_copy), "copy op layout");
-    // The previous list may still be read by a launch in flight; the upload is
-    // synchronous so the caller's host list may be reused on return.
-    KVM_CUDA(cudaDeviceSynchronize());
-    KVM_CUDA(cudaMemcpy(dev_ops, ops, size_t(n) * sizeof(CopyOp), cudaMemcpyHostToDevice));
+    // The list is copied into one of two mapped pinned lists that the gather reads
+    // directly, so the caller's array may be reused on return and nothing waits for
+    // the device unless both lists are still in flight.
+    auto& L = c->copy_lists[c->copy_next];
+    if (L.pending) {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            const cudaError_t e = cudaEventQuery(L.done);
+            if (e == cudaSuccess) break;
+            if (e != cudaErrorNotReady) {
+                cudaGetLastError();
+                return KVM_ERR_CUDA;
+            }
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(30)) return KVM_ERR_TIMEOUT;
+        }
+        L.pending = false;
+    }
+    if (!L.done) KVM_CUDA(cudaEventCreateWithFlags(&L.done, cudaEventDisableTiming));
+    if (L.cap < n) {
+        if (L.host) cudaFreeHost(L.host);
+        L.host = nullptr;
+        L.cap = 0;
+        const uint32_t cap = std::max<uint32_t>(256, n);
+        KVM_CUDA(cudaHostAlloc(&L.host, size_t(cap) * sizeof(CopyOp), cudaHostAllocMapped | cudaHostAllocPortable));
+        L.cap = cap;
+    }
+    std::memcpy(L.host, ops, size_t(n) * sizeof(CopyOp));
+    CopyOp* dev_ops = nullptr;
+    KVM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_ops), L.host, 0));
     const uint32_t grid = std::min<uint32_t>(n, ctas ? ctas : 64);
     copy_ops_kernel<<<grid, kGatherThreads, 0, s>>>(dev_ops, n);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
+    KVM_CUDA(cudaEventRecord(L.done, s));
+    L.pending = true;
+    c->copy_next ^= 1;
     return KVM_OK;
 }
 

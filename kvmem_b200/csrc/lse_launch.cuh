@@ -29,6 +29,15 @@ struct kvm_ctx {
     std::vector<uint32_t> keep_cached;
     bool keep_valid = false;
     uint64_t launches = 0;
+    // kvm_stagein_copies: two op lists in mapped pinned memory, used in turn; a list
+    // is rewritten only after the gather that read it (its event) is done.
+    struct CopyList {
+        void* host = nullptr;  // kvmb::CopyOp[cap], mapped
+        uint32_t cap = 0;
+        cudaEvent_t done = nullptr;
+        bool pending = false;
+    } copy_lists[2];
+    int copy_next = 0;
 };
 
 namespace kvmb {

@@ -107,3 +107,29 @@ def test_copy_list(ctx):
     for i in range(0, 256, 17):
         assert np.array_equal(d[4096 * (255 - i): 4096 * (256 - i)], s[4096 * i: 4096 * (i + 1)])
     assert np.array_equal(d[(1 << 20) + 5:(1 << 20) + 22], s[3:20])
+
+
+def test_copy_lists_back_to_back(ctx):
+    """Several lists enqueued without waiting (the two op lists are reused in turn), of growing
+    length, each list's host array dropped as soon as the call returns."""
+    rng = np.random.default_rng(2)
+    src = torch.from_numpy(rng.integers(0, 256, 8 << 20, dtype=np.uint8)).pin_memory()
+    dst = torch.zeros(8 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    expect = np.zeros(8 << 20, np.uint8)
+    s = src.numpy()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for call in range(6):
+            n = 64 * (call + 1)  # the third list outgrows the first allocation
+            chunk = (8 << 20) // (6 * 384)
+            base = call * 384 * chunk
+            ops = []
+            for i in range(n):
+                so = int(rng.integers(0, (8 << 20) - chunk))
+                do = base + i * chunk
+                ops.append((src.data_ptr() + so, dst.data_ptr() + do, chunk))
+                expect[do:do + chunk] = s[so:so + chunk]
+            ctx.stagein_copies(ops, ctas=8, stream=stream)
+    ctx.wait(30.0, stream=stream)
+    np.testing.assert_array_equal(dst.cpu().numpy(), expect)
