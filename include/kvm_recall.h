@@ -361,6 +361,59 @@ int kvm_stageout_clear(kvm_stageout* so);
  * slot_of[rows][pages] (-1 = not resident) and page_of[rows][slots]. */
 int kvm_pool_read(kvm_pool* pool, int32_t* slot_of, int32_t* page_of, void* stream);
 
+/* ------------------------------------------------- working-set transfers */
+
+/* A working-set transfer over a pool, the GPU side of kvmem::MemoryTransfer
+ * (kvmem/include/kvmem/memory_contract.hpp:171-185) as kvmem::MemorySession
+ * drives it (kvmem/src/host/memory_contract.cpp:245-365):
+ *   prepare  -> start_spill -> poll until KVM_OK -> start_restore -> poll until
+ *   KVM_OK -> publish, or abort at any point.
+ * prepare reserves everything the transfer needs and plans the residency delta
+ * (plan_residency, memory_contract.cpp:135-150) into a shadow copy of the
+ * pool's tables: on any error nothing was started and the published view is
+ * intact (the strong guarantee of MemoryBackend::prepare). One transfer per
+ * pool at a time (KVM_ERR_PENDING otherwise); kvm_plan_residency and
+ * kvm_stagein_pool must not be used on the pool while it is pending. */
+typedef struct kvm_transfer kvm_transfer;
+int kvm_transfer_prepare(kvm_ctx* ctx, kvm_pool* pool, const uint32_t* sel_ids, const uint32_t* sel_n,
+                         uint32_t sel_stride, int force_reload, void* stream, kvm_transfer** out);
+
+/* Spill: evicted pages whose host copy is stale (device u8 stale[rows][pages]
+ * != 0; NULL = every host copy is current, nothing to copy) are written from
+ * their device slots back to their host records (layout: host_base = mapped
+ * pinned records, dev_base = the cache), before any slot is reused
+ * (MemoryTransfer::start_spill; "start_spill cannot reclaim source pages"). */
+int kvm_transfer_start_spill(kvm_transfer* t, const kvm_stage_layout* layout, const uint8_t* stale, uint32_t ctas,
+                             void* stream);
+
+/* Non-blocking poll of the current step (MemoryTransfer::poll): KVM_OK when it
+ * is complete, KVM_ERR_PENDING while it runs, KVM_ERR_TRANSFER_FAILED on a CUDA
+ * failure, KVM_ERR_INVALID_SESSION after an abort. */
+int kvm_transfer_poll(kvm_transfer* t);
+
+/* Restore: the planned pages are gathered from their host records into their
+ * new slots (MemoryTransfer::start_restore, "called only after spill
+ * completes": KVM_ERR_PENDING while the spill runs, KVM_ERR_INVALID_PLAN out of
+ * order). From here on an abort cannot preserve the previous view. */
+int kvm_transfer_start_restore(kvm_transfer* t, const kvm_stage_layout* layout, uint32_t ctas, void* stream);
+
+/* Publish: once the restore is complete, the shadow tables become the pool's
+ * view (MemoryTransfer::publish); synchronises `stream`. KVM_ERR_PENDING before
+ * the restore completes; KVM_ERR_TRANSFER_FAILED (or KVM_ERR_BUDGET_EXCEEDED for a
+ * selection larger than the pool) when a device step failed. */
+int kvm_transfer_publish(kvm_transfer* t, void* stream);
+
+/* Abort (MemoryTransfer::abort): drains every step already issued (bounded by
+ * timeout_us, KVM_ERR_TIMEOUT otherwise) before anything is released, then
+ * drops the transfer. *previous_view_preserved = 1 when no restore had started
+ * (bytes and tables of the previous view intact:
+ * AbortResult::PreviousViewPreserved), else 0 (SessionInvalidated). */
+int kvm_transfer_abort(kvm_transfer* t, uint64_t timeout_us, int* previous_view_preserved);
+
+/* Frees a published or aborted transfer (a pending one is aborted first);
+ * KVM_ERR_TIMEOUT and nothing freed when device work could not be drained. */
+int kvm_transfer_destroy(kvm_transfer* t);
+
 /* Raw-K restore transform of stage-in, fused: each item's `tokens` packed K
  * rows (q8_0 or q4_0, n_head * head_dim elements per row, rows contiguous)
  * are dequantised, rotated by NeoX RoPE on the first n_rot dims of every head

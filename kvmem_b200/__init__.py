@@ -9,8 +9,8 @@ host-side binding.
 """
 from . import _abi
 from ._abi import KvmError, F32, F16, BF16, Q8_0, Q4_0, Q5_0
-from .recall import (AttentionCuda, PageSoftmaxCuda, RecallContext, ResidencyPool, StageOut, TensorView,
+from .recall import (AttentionCuda, PageSoftmaxCuda, RecallContext, ResidencyPool, StageOut, TensorView, Transfer,
                      pick_scored_blocks, row_bytes, stage_layout)
 
 __all__ = ["KvmError", "F32", "F16", "BF16", "Q8_0", "Q4_0", "Q5_0", "AttentionCuda", "PageSoftmaxCuda",
-           "RecallContext", "ResidencyPool", "StageOut", "TensorView", "pick_scored_blocks", "row_bytes", "stage_layout"]
+           "RecallContext", "ResidencyPool", "StageOut", "TensorView", "Transfer", "pick_scored_blocks", "row_bytes", "stage_layout"]

@@ -137,6 +137,13 @@ SIGNATURES = {
     "kvm_stageout_slot_base": ([_vp, _i], _vp),
     "kvm_stageout_clear": ([_vp], _i),
     "kvm_pool_read": ([_vp, _vp, _vp, _vp], _i),
+    "kvm_transfer_prepare": ([_vp, _vp, _vp, _vp, _u32, _i, _vp, C.POINTER(C.c_void_p)], _i),
+    "kvm_transfer_start_spill": ([_vp, C.POINTER(StageLayout), _vp, _u32, _vp], _i),
+    "kvm_transfer_poll": ([_vp], _i),
+    "kvm_transfer_start_restore": ([_vp, C.POINTER(StageLayout), _u32, _vp], _i),
+    "kvm_transfer_publish": ([_vp, _vp], _i),
+    "kvm_transfer_abort": ([_vp, _u64, C.POINTER(C.c_int)], _i),
+    "kvm_transfer_destroy": ([_vp], _i),
     "kvm_restore_k": ([_vp, _i, C.POINTER(RestoreItem), _u32, _u32, _u32, _u32, C.POINTER(C.c_float), _u32, _vp],
                       _i),
     "kvm_propagate_scores": ([_vp, _vp, _u32, _vp, _vp, _u64, C.POINTER(Graph), C.c_double, C.c_double, _vp, _vp],

@@ -22,10 +22,27 @@
 
 using namespace kvmb;
 
+struct kvm_transfer;
+
 struct kvm_pool {
     kvm_ctx* ctx = nullptr;
     PoolView view{};
     void* mem = nullptr;
+    kvm_transfer* pending = nullptr;  // the prepared, not yet published or aborted transfer
+};
+
+// A working-set transfer over a pool (kvm_transfer_*): the plan, the restore
+// lists and the new residency tables live in a shadow copy until publish.
+struct kvm_transfer {
+    kvm_ctx* ctx = nullptr;
+    kvm_pool* pool = nullptr;
+    void* mem = nullptr;  // shadow tables, same layout as the pool's
+    PoolView shadow{};
+    int force = 0;
+    enum Phase { Prepared, Spilling, Restoring, Published, Aborted } phase = Prepared;
+    bool restore_started = false;
+    bool drained = true;  // false when an abort could not drain the device work
+    cudaEvent_t planned = nullptr, spill_done = nullptr, restore_done = nullptr;
 };
 
 namespace {
@@ -753,6 +770,7 @@ int kvm_pool_create(kvm_ctx* c, uint32_t rows, uint32_t pages, uint32_t slots, k
 
 int kvm_pool_destroy(kvm_pool* p) {
     if (!p) return KVM_OK;
+    if (p->pending) return KVM_ERR_PENDING;  // destroy (or abort) the transfer first
     DeviceGuard guard(p->ctx->device);
     cudaDeviceSynchronize();
     if (p->mem) cudaFree(p->mem);
@@ -768,6 +786,213 @@ int kvm_pool_reset(kvm_pool* p, void* stream) {
     KVM_CUDA(cudaMemsetAsync(v.slot_of, 0xff, size_t(v.rows) * v.pages * 4, s));
     KVM_CUDA(cudaMemsetAsync(v.page_of, 0xff, size_t(v.rows) * v.slots * 4, s));
     KVM_CUDA(cudaMemsetAsync(v.n_restore, 0, size_t(v.rows) * 4, s));
+    return KVM_OK;
+}
+
+namespace {
+
+// Bounded host wait for an event: KVM_OK, KVM_ERR_TIMEOUT or KVM_ERR_CUDA.
+int event_wait(cudaEvent_t e, uint64_t timeout_us) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t r = cudaEventQuery(e);
+        if (r == cudaSuccess) return KVM_OK;
+        if (r != cudaErrorNotReady) {
+            cudaGetLastError();
+            return KVM_ERR_CUDA;
+        }
+        const auto us =
+            std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (uint64_t(us) >= timeout_us) return KVM_ERR_TIMEOUT;
+    }
+}
+
+int event_ready(cudaEvent_t e) {
+    const cudaError_t r = cudaEventQuery(e);
+    if (r == cudaSuccess) return KVM_OK;
+    if (r == cudaErrorNotReady) return KVM_ERR_PENDING;
+    cudaGetLastError();
+    return KVM_ERR_TRANSFER_FAILED;
+}
+
+void transfer_free(kvm_transfer* t) {
+    if (t->planned) cudaEventDestroy(t->planned);
+    if (t->spill_done) cudaEventDestroy(t->spill_done);
+    if (t->restore_done) cudaEventDestroy(t->restore_done);
+    if (t->mem) cudaFree(t->mem);
+    delete t;
+}
+
+}  // namespace
+
+int kvm_transfer_prepare(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, const uint32_t* sel_n,
+                         uint32_t sel_stride, int force_reload, void* stream, kvm_transfer** out) {
+    if (!out) return KVM_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (!c || !pool || pool->ctx != c || !sel_ids || !sel_n || !sel_stride) return KVM_ERR_INVALID_ARGUMENT;
+    if (pool->pending) return KVM_ERR_PENDING;
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    auto* t = new (std::nothrow) kvm_transfer;
+    if (!t) return KVM_ERR_CUDA;
+    t->ctx = c;
+    t->pool = pool;
+    t->force = force_reload;
+    const auto& v = pool->view;
+    const size_t a = align256(size_t(v.rows) * v.pages * 4), b = align256(size_t(v.rows) * v.slots * 4),
+                 n = align256(size_t(v.rows) * 4);
+    // Everything the transfer needs is reserved here; the pool's tables are only read.
+    if (cudaMalloc(&t->mem, a + 3 * b + n) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->planned, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->spill_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->restore_done, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        transfer_free(t);
+        return KVM_ERR_CUDA;
+    }
+    auto* base = static_cast<uint8_t*>(t->mem);
+    t->shadow = v;
+    t->shadow.slot_of = reinterpret_cast<int32_t*>(base);
+    t->shadow.page_of = reinterpret_cast<int32_t*>(base + a);
+    t->shadow.restore = reinterpret_cast<uint32_t*>(base + a + b);
+    t->shadow.restore_slot = reinterpret_cast<uint32_t*>(base + a + 2 * b);
+    t->shadow.n_restore = reinterpret_cast<uint32_t*>(base + a + 3 * b);
+    int rc = KVM_OK;
+    if (cudaMemcpyAsync(t->shadow.slot_of, v.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess ||
+        cudaMemcpyAsync(t->shadow.page_of, v.page_of, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess) {
+        cudaGetLastError();
+        rc = KVM_ERR_CUDA;
+    }
+    if (rc == KVM_OK) {
+        kvm_pool shadow_pool;
+        shadow_pool.ctx = c;
+        shadow_pool.view = t->shadow;
+        rc = plan_rows(c, &shadow_pool, 0, v.rows, sel_ids, sel_n, sel_stride, force_reload, nullptr, nullptr, s);
+    }
+    if (rc == KVM_OK && cudaEventRecord(t->planned, s) != cudaSuccess) {
+        cudaGetLastError();
+        rc = KVM_ERR_CUDA;
+    }
+    if (rc != KVM_OK) {
+        cudaStreamSynchronize(s);  // nothing may still read the shadow when it is freed
+        cudaGetLastError();
+        transfer_free(t);
+        return rc;
+    }
+    pool->pending = t;
+    *out = t;
+    return KVM_OK;
+}
+
+int kvm_transfer_start_spill(kvm_transfer* t, const kvm_stage_layout* layout, const uint8_t* stale, uint32_t ctas,
+                             void* stream) {
+    if (!t) return KVM_ERR_INVALID_ARGUMENT;
+    if (t->phase != kvm_transfer::Prepared) return KVM_ERR_INVALID_PLAN;
+    DeviceGuard guard(t->ctx->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_CUDA(cudaStreamWaitEvent(s, t->planned, 0));
+    if (stale) {
+        GatherLayout g{};
+        KVM_TRY(gather_layout(layout, &g));
+        const auto& v = t->pool->view;
+        spill_gather_kernel<<<ctas ? ctas : 32, kGatherThreads, 0, s>>>(v.page_of, t->shadow.slot_of, stale, v.rows,
+                                                                        v.pages, v.slots, t->force, g);
+        ++t->ctx->launches;
+        KVM_CUDA(cudaGetLastError());
+    }
+    KVM_CUDA(cudaEventRecord(t->spill_done, s));
+    t->phase = kvm_transfer::Spilling;
+    return KVM_OK;
+}
+
+int kvm_transfer_poll(kvm_transfer* t) {
+    if (!t) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(t->ctx->device);
+    switch (t->phase) {
+        case kvm_transfer::Prepared: return event_ready(t->planned);
+        case kvm_transfer::Spilling: return event_ready(t->spill_done);
+        case kvm_transfer::Restoring: return event_ready(t->restore_done);
+        case kvm_transfer::Published: return KVM_OK;
+        default: return KVM_ERR_INVALID_SESSION;
+    }
+}
+
+int kvm_transfer_start_restore(kvm_transfer* t, const kvm_stage_layout* layout, uint32_t ctas, void* stream) {
+    if (!t) return KVM_ERR_INVALID_ARGUMENT;
+    if (t->phase != kvm_transfer::Spilling) return KVM_ERR_INVALID_PLAN;
+    GatherLayout g{};
+    KVM_TRY(gather_layout(layout, &g));
+    DeviceGuard guard(t->ctx->device);
+    const int ready = event_ready(t->spill_done);  // slots of evicted pages are reused only after the spill
+    if (ready != KVM_OK) return ready;
+    auto s = static_cast<cudaStream_t>(stream);
+    kvm_pool shadow_pool;
+    shadow_pool.ctx = t->ctx;
+    shadow_pool.view = t->shadow;
+    t->restore_started = true;
+    KVM_TRY(gather_rows(t->ctx, &shadow_pool, 0, t->shadow.rows, g, ctas, s));
+    KVM_CUDA(cudaEventRecord(t->restore_done, s));
+    t->phase = kvm_transfer::Restoring;
+    return KVM_OK;
+}
+
+int kvm_transfer_publish(kvm_transfer* t, void* stream) {
+    if (!t) return KVM_ERR_INVALID_ARGUMENT;
+    if (t->phase != kvm_transfer::Restoring) return KVM_ERR_PENDING;
+    DeviceGuard guard(t->ctx->device);
+    const int ready = event_ready(t->restore_done);
+    if (ready != KVM_OK) return ready;
+    auto s = static_cast<cudaStream_t>(stream);
+    // A device-side failure of the plan or the copies fails the transfer; its
+    // restore has already reused slots, so the previous view is not preserved.
+    const int st = kvm_ctx_status(t->ctx, stream);
+    if (st != KVM_OK) return st == KVM_ERR_BUDGET_EXCEEDED ? st : KVM_ERR_TRANSFER_FAILED;
+    const auto& v = t->pool->view;
+    const auto& w = t->shadow;
+    KVM_CUDA(cudaMemcpyAsync(v.slot_of, w.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToDevice, s));
+    KVM_CUDA(cudaMemcpyAsync(v.page_of, w.page_of, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToDevice, s));
+    KVM_CUDA(cudaMemcpyAsync(v.restore, w.restore, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToDevice, s));
+    KVM_CUDA(cudaMemcpyAsync(v.restore_slot, w.restore_slot, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToDevice,
+                             s));
+    KVM_CUDA(cudaMemcpyAsync(v.n_restore, w.n_restore, size_t(v.rows) * 4, cudaMemcpyDeviceToDevice, s));
+    KVM_CUDA(cudaStreamSynchronize(s));  // the new view is in place before the call returns
+    t->phase = kvm_transfer::Published;
+    t->pool->pending = nullptr;
+    return KVM_OK;
+}
+
+int kvm_transfer_abort(kvm_transfer* t, uint64_t timeout_us, int* previous_view_preserved) {
+    if (previous_view_preserved) *previous_view_preserved = 0;
+    if (!t) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(t->ctx->device);
+    if (t->phase == kvm_transfer::Published) {
+        if (previous_view_preserved) *previous_view_preserved = 0;  // the new view is the current one
+        return KVM_OK;
+    }
+    // Drain every recorded step before anything is released.
+    int rc = KVM_OK;
+    for (cudaEvent_t e : {t->planned, t->spill_done, t->restore_done}) {
+        const int w = event_wait(e, timeout_us);
+        if (w != KVM_OK) rc = w;
+    }
+    t->drained = rc == KVM_OK;
+    if (previous_view_preserved) *previous_view_preserved = (!t->restore_started && t->drained) ? 1 : 0;
+    t->phase = kvm_transfer::Aborted;
+    if (t->pool->pending == t) t->pool->pending = nullptr;
+    return rc;
+}
+
+int kvm_transfer_destroy(kvm_transfer* t) {
+    if (!t) return KVM_OK;
+    DeviceGuard guard(t->ctx->device);
+    if (t->phase != kvm_transfer::Published && t->phase != kvm_transfer::Aborted) {
+        int preserved = 0;
+        kvm_transfer_abort(t, 30ull * 1000 * 1000, &preserved);
+    }
+    if (!t->drained) return KVM_ERR_TIMEOUT;  // device work may still use the buffers: keep them
+    transfer_free(t);
     return KVM_OK;
 }
 

@@ -157,6 +157,32 @@ __global__ void __launch_bounds__(kGatherThreads) stagein_gather_kernel(PoolView
     }
 }
 
+// Write-back before a restore may reuse slots (the spill of a working-set
+// transfer): for every (row, slot, plane) whose published page p is evicted by
+// the new plan (not at that slot in new_slot_of, or force_reload) and whose host
+// copy is stale (stale[row][p] != 0), the device slot's bytes are copied to the
+// page's host record (mapped pinned memory). Items are spread over the CTAs.
+__global__ void __launch_bounds__(kGatherThreads) spill_gather_kernel(const int32_t* old_page_of,
+                                                                       const int32_t* new_slot_of,
+                                                                       const uint8_t* stale, uint32_t rows,
+                                                                       uint32_t pages, uint32_t slots, int force,
+                                                                       GatherLayout lay) {
+    const uint64_t items = uint64_t(rows) * slots * lay.planes;
+    for (uint64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const uint32_t j = uint32_t(item % lay.planes);
+        const uint64_t rs = item / lay.planes;
+        const uint32_t r = uint32_t(rs / slots), s = uint32_t(rs % slots);
+        const int32_t p = old_page_of[rs];
+        if (p < 0 || uint32_t(p) >= pages) continue;
+        const uint64_t rp = uint64_t(r) * pages + uint32_t(p);
+        if (!(force || new_slot_of[rp] != int32_t(s)) || !stale[rp]) continue;
+        const uint8_t* src = lay.dev_base[j] + uint64_t(r) * lay.dev_row_stride[j] + uint64_t(s) * lay.dev_slot_stride[j];
+        uint8_t* dst = const_cast<uint8_t*>(lay.host_base[j]) + uint64_t(r) * lay.host_row_stride[j] +
+                       uint64_t(p) * lay.host_page_stride[j];
+        copy_item(src, dst, lay.bytes[j]);
+    }
+}
+
 struct CopyOp {
     const uint8_t* src;
     uint8_t* dst;

@@ -310,6 +310,70 @@ class ResidencyPool:
         return slot_of, page_of
 
 
+class Transfer:
+    """A working-set transfer over a ResidencyPool (kvm_transfer): the GPU side of
+    kvmem::MemoryTransfer (kvmem/include/kvmem/memory_contract.hpp:171-185). The
+    plan goes into a shadow of the pool's tables; start_spill / poll / start_restore /
+    publish / abort keep the reference's names and order; failures raise KvmError
+    (the reference's MemoryError codes)."""
+
+    def __init__(self, pool: "ResidencyPool", sel_ids: torch.Tensor, sel_n: torch.Tensor, *,
+                 force_reload: bool = False, stream=None):
+        self.pool, self.lib = pool, pool.ctx.lib
+        h = C.c_void_p()
+        rc = self.lib.kvm_transfer_prepare(pool.ctx.h, pool.h, sel_ids.data_ptr(), sel_n.data_ptr(),
+                                           sel_ids.stride(0), int(force_reload), _stream_ptr(stream), C.byref(h))
+        A.check(rc, "kvm_transfer_prepare")
+        self.h = h
+
+    def start_spill(self, layout: Optional[A.StageLayout] = None, stale: Optional[torch.Tensor] = None,
+                    ctas: int = 0, stream=None) -> None:
+        rc = self.lib.kvm_transfer_start_spill(self.h, C.byref(layout) if layout is not None else None,
+                                               stale.data_ptr() if stale is not None else None, ctas,
+                                               _stream_ptr(stream))
+        A.check(rc, "kvm_transfer_start_spill")
+
+    def poll(self) -> str:
+        """'Complete' or 'Pending' (TransferStatus); a failed step raises."""
+        rc = self.lib.kvm_transfer_poll(self.h)
+        if rc == A.ERR_PENDING:
+            return "Pending"
+        A.check(rc, "kvm_transfer_poll")
+        return "Complete"
+
+    def wait(self, timeout_s: float = 30.0) -> None:
+        import time
+        t0 = time.time()
+        while self.poll() == "Pending":
+            if time.time() - t0 > timeout_s:
+                raise A.KvmError(A.ERR_TIMEOUT, "kvm_transfer_poll")
+            time.sleep(0.0005)
+
+    def start_restore(self, layout: A.StageLayout, ctas: int = 0, stream=None) -> None:
+        A.check(self.lib.kvm_transfer_start_restore(self.h, C.byref(layout), ctas, _stream_ptr(stream)),
+                "kvm_transfer_start_restore")
+
+    def publish(self, stream=None) -> None:
+        A.check(self.lib.kvm_transfer_publish(self.h, _stream_ptr(stream)), "kvm_transfer_publish")
+
+    def abort(self, timeout_s: float = 30.0) -> bool:
+        """Drains, then drops the transfer; True when the previous view is preserved."""
+        kept = C.c_int(0)
+        A.check(self.lib.kvm_transfer_abort(self.h, int(timeout_s * 1e6), C.byref(kept)), "kvm_transfer_abort")
+        return bool(kept.value)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.kvm_transfer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class StageOut:
     """Double-buffered stage-out (kvm_stageout): device regions gathered into
     two pinned host slots in turn. Method names follow the reference's
