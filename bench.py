@@ -165,8 +165,56 @@ def barrier(world):
 
 # --------------------------------------------------------------------------- data
 
-def build_history(w, seed, device, need_host=True):
-    """K score mirror on the device, pinned host K/V pages, device paged cache."""
+class HostStore:
+    """Pinned, device-mapped host memory for the K / V page records.
+
+    One process: torch pinned memory. Several ranks on one node (replicas of the same
+    history): one POSIX shared-memory segment per node, filled by local rank 0 and
+    registered as mapped pinned memory by every rank, so the node holds one copy of the
+    records instead of one per rank (a config-2 history is 34 GB of K and V records;
+    eight private copies would not fit a 251 GB host)."""
+
+    def __init__(self, nbytes: int, tag: str, world: int, local: int):
+        import torch
+        self.shm, self.registered, self.owner = None, False, False
+        if world == 1:
+            self.tensor = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+            return
+        from multiprocessing import resource_tracker, shared_memory
+        name = f"kvm_{tag}_{os.environ.get('MASTER_PORT', '0')}_{os.getppid()}"
+        if local == 0:
+            self.shm = shared_memory.SharedMemory(name=name, create=True, size=nbytes)
+            self.owner = True
+        barrier(world)
+        if local != 0:
+            self.shm = shared_memory.SharedMemory(name=name)
+            # Only the creating rank removes the segment (attachers would unlink it at exit).
+            resource_tracker.unregister(self.shm._name, "shared_memory")
+        self.tensor = torch.frombuffer(self.shm.buf, dtype=torch.uint8)
+        err = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 3)  # portable | mapped
+        if int(err) != 0:
+            raise RuntimeError(f"cudaHostRegister of the shared page records failed ({int(err)})")
+        self.registered = True
+
+    def close(self, world: int):
+        import torch
+        if self.shm is None:
+            return
+        if self.registered:
+            torch.cuda.cudart().cudaHostUnregister(self.tensor.data_ptr())
+        del self.tensor
+        barrier(world)
+        self.shm.close()
+        if self.owner:
+            self.shm.unlink()
+        self.shm = None
+
+
+def build_history(w, seed, device, need_host=True, world=1, local=0):
+    """K score mirror on the device, pinned host K/V pages, device paged cache.
+
+    With world > 1 every rank builds the same history (same seed) and the host page
+    records are one node-shared store written by local rank 0."""
     import torch
     from kvmem_b200 import row_bytes, synth
     rbk = row_bytes(w.k_type, w.head_dim)
@@ -177,24 +225,29 @@ def build_history(w, seed, device, need_host=True):
     q_base, drift = synth.make_queries(w, seed, device, drift_steps=8)
     k_dev = torch.empty(w.layers * layer_k, dtype=torch.uint8, device=device)
     host_k = host_v = None
+    stores = []
+    write_host = need_host and local == 0
     if need_host:
-        host_k = torch.empty(w.layers * layer_k, dtype=torch.uint8, pin_memory=True)
-        host_v = torch.empty(w.layers * layer_v, dtype=torch.uint8, pin_memory=True)
+        sk, sv = HostStore(w.layers * layer_k, "k", world, local), HostStore(w.layers * layer_v, "v", world, local)
+        stores = [sk, sv]
+        host_k, host_v = sk.tensor, sv.tensor
     for l in range(w.layers):
         if w.k_type == 1:
             kl = synth.fp16_layer(w, seed, l, q_base, device).view(torch.uint8).reshape(-1)
         else:
             kl = synth.q8_0_layer(w, seed, l, q_base, device).reshape(-1)
         k_dev[l * layer_k:(l + 1) * layer_k].copy_(kl)
-        if need_host:
+        if write_host:
             host_k[l * layer_k:(l + 1) * layer_k].copy_(kl)
             vl = (synth.fp16_v_layer(w, seed, l, device).view(torch.uint8).reshape(-1) if w.v_type == 1
                   else synth.q4_0_v_layer(w, seed, l, device).reshape(-1))
             host_v[l * layer_v:(l + 1) * layer_v].copy_(vl)
         del kl
     torch.cuda.synchronize()
+    if need_host and world > 1:
+        barrier(world)  # the records are written before any rank stages from them
     return dict(q_base=q_base, drift=drift, k_dev=k_dev, host_k=host_k, host_v=host_v, layer_k=layer_k,
-                layer_v=layer_v, rbk=rbk, rbv=rbv)
+                layer_v=layer_v, rbk=rbk, rbv=rbv, stores=stores)
 
 
 # --------------------------------------------------------------------------- our arm
@@ -469,8 +522,8 @@ def run_ours(args, world, rank, local):
     if args.config == "c4":
         return run_replay(args, w, world, rank, local)
     dev = torch.device("cuda", local)
-    seed = args.seed + rank
-    h = build_history(w, seed, dev)
+    seed = args.seed  # replicas run the same history (the node shares its host page records)
+    h = build_history(w, seed, dev, world=world, local=local)
     ctx = K.RecallContext(local)
     P, L = w.pages, w.layers
     srows = L * w.groups
@@ -645,6 +698,8 @@ def run_ours(args, world, rank, local):
 
     pool.close()
     ctx.close()
+    for st in h["stores"]:
+        st.close(world)
     if rank != 0:
         return
     line = {
