@@ -170,9 +170,11 @@ struct LseConfig {
 
 // Scorer selection: KVM_SCORER=simt forces the FP32 SIMT kernel and
 // KVM_SCORER=mma the mma.sync kernel wherever it applies; KVM_SCORER=tc
-// requires the tcgen05 kernel (KVM_ERR_UNSUPPORTED where it does not apply).
-// The tests use them to check every kernel against the oracle; anything else
-// picks the tcgen05 kernel, then the mma.sync kernel, wherever they apply.
+// requires the tcgen05 kernel (KVM_ERR_UNSUPPORTED where it does not apply);
+// KVM_SCORER=mma_generic scores q8_0 / q4_0 keys with the fp16 mma.sync kernel
+// instead of the integer-tensor-core one. The tests use them to check every
+// kernel against the oracle; anything else picks the tcgen05 kernel, then the
+// quantised-key kernel, then the mma.sync kernel, wherever they apply.
 bool scorer_is(const char* name) {
     const char* e = std::getenv("KVM_SCORER");
     return e && std::strcmp(e, name) == 0;

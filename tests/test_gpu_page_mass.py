@@ -16,9 +16,10 @@ REL, ABS = 1e-3, 1e-6
 QT = {U.F32: torch.float32, U.F16: torch.float16, U.BF16: torch.bfloat16}
 
 
-@pytest.fixture(params=["auto", "simt"])
+@pytest.fixture(params=["auto", "simt", "mma_generic"])
 def scorer(request, monkeypatch):
-    """Both page scorers: the tensor-core kernel (auto, where it applies) and the FP32 SIMT kernel."""
+    """Every page scorer: the tensor-core kernels (auto, where they apply), the FP32 SIMT kernel,
+    and the fp16 mma.sync kernel for quantised keys (mma_generic)."""
     monkeypatch.setenv("KVM_SCORER", request.param)
     return request.param
 
