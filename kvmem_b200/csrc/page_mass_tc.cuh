@@ -337,9 +337,10 @@ __device__ __noinline__ float2 tc_fold_slow(const TcSlowArgs a, float m, float s
 // [qbase + D/2, qbase + D) of the lane's row. Warp-collective; out of line
 // (it runs once per (layer, KV head)).
 template <uint32_t D>
-__device__ __noinline__ void tc_write_query_row(uint32_t qbase, const uint8_t* qp, int q_type, int shift, bool valid) {
+__device__ __noinline__ bool tc_write_query_row(uint32_t qbase, const uint8_t* qp, int q_type, int shift, bool valid) {
     const float qs = ldexpf(1.f, shift);
     const uint32_t esz = type_bytes(q_type);
+    uint32_t lo_bits = 0;
 #pragma unroll
     for (uint32_t d0 = 0; d0 < D; d0 += 64) {
         uint32_t hw[32], lw[32];
@@ -351,10 +352,12 @@ __device__ __noinline__ void tc_write_query_row(uint32_t qbase, const uint8_t* q
                 x1 = load_scalar(qp + (d0 + 2 * i + 1) * esz, q_type) * qs;
             }
             tc_split2(x0, x1, hw[i], lw[i]);
+            lo_bits |= lw[i] & 0x7FFF7FFFu;  // -0 counts as zero
         }
         tc_st32(qbase + d0 / 2, hw);
         tc_st32(qbase + D / 2 + d0 / 2, lw);
     }
+    return lo_bits != 0;
 }
 
 // Walks units (layer, KV head, u) in order without 64-bit divisions per step.
@@ -403,6 +406,9 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
     uint64_t* qready = qfree + 1;             // tile-0 query operand written
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qready + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // Set by the tile-0 query writers when any lo part of the (layer, KV head)'s
+    // operand is nonzero; read and cleared by the MMA issuer after qready.
+    volatile uint32_t* lo_any = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t V = P.nv;  // query vectors per KV head (rows * group)
@@ -424,6 +430,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
         mbar_init(qfree, 1);
         mbar_init(qready, warps0 + warps1);
         *abort_flag = 0;
+        *lo_any = 0;
         mbar_fence_init();
     }
     if constexpr (LM == 2) {
@@ -494,7 +501,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
             // issued one tile late so they never hold up the next tile-0 MMAs.
             int64_t last = -1;
             uint32_t pend_it = 0, pend_s = 0;
-            bool pend = false;
+            bool pend = false, use_lo = true;
             int err = 0;
             auto issue_packed = [&]() -> bool {
                 // Packed accumulator pend_it % 2, free once the epilogue read its use two tiles ago.
@@ -537,6 +544,8 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     }
                     ++nq;
                     tc_fence_after();
+                    use_lo = *lo_any != 0;  // all-zero lo parts (fp16 queries): skip their MMAs
+                    *lo_any = 0;
                 }
                 for (uint32_t t = 0; t < ut; ++t, ++it) {
                     const uint32_t b = tb, s = ks;
@@ -564,7 +573,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                                 const uint64_t bd = tc_desc_sw128(kbase + a * kTcAtomBytes + kk * 32);
                                 const uint32_t acol = (a * 4 + kk) * 8;  // 16 fp16 = 8 columns per k-step
                                 tc_mma_ts(d0, qhi + acol, bd, idesc, (a | kk) != 0);
-                                tc_mma_ts(d0, qlo + acol, bd, idesc, 1);
+                                if (use_lo) tc_mma_ts(d0, qlo + acol, bd, idesc, 1);
                             }
                     } else {
                         const uint32_t qh = smem_u32(q0hi), ql = smem_u32(q0lo);
@@ -575,7 +584,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                                 const uint32_t off = a * kTcAtomBytes + kk * 32;
                                 const uint64_t bd = tc_desc_sw128(kbase + off);
                                 tc_mma(d0, tc_desc_sw128(qh + off), bd, idesc, (a | kk) != 0);
-                                tc_mma(d0, tc_desc_sw128(ql + off), bd, idesc, 1);
+                                if (use_lo) tc_mma(d0, tc_desc_sw128(ql + off), bd, idesc, 1);
                             }
                     }
                     tc_commit(&tfull[b]);  // tile-0 accumulator ready for the epilogue
@@ -702,9 +711,10 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                             *abort_flag = 1;
                             break;
                         }
+                        bool lo_nz = false;
                         if constexpr (LM == 1) {
                             tc_fence_after();
-                            tc_write_query_row<D>(qbase, qp, P.q_type, shift, vvalid);
+                            lo_nz = tc_write_query_row<D>(qbase, qp, P.q_type, shift, vvalid);
                             tc_wait_st();
                             tc_fence_before();
                         } else {
@@ -728,10 +738,12 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                                 const uint32_t off = at * kTcAtomBytes + tc_sw128_offset(v, k0);
                                 *reinterpret_cast<uint4*>(q0hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                                 *reinterpret_cast<uint4*>(q0lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                                lo_nz |= ((lw[0] | lw[1] | lw[2] | lw[3]) & 0x7FFF7FFFu) != 0;
                             }
                             // Generic-proxy stores -> visible to the tensor cores (async proxy).
                             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                         }
+                        if (__any_sync(0xffffffffu, lo_nz) && lane == 0) atomicOr(const_cast<uint32_t*>(lo_any), 1u);
                         __syncwarp();
                         if (lane == 0) mbar_arrive(qready);
                     }

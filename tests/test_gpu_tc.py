@@ -43,6 +43,9 @@ CASES = [
     dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=4, page=128, T=640, qtype=U.F16),
     dict(ktype=U.F16, D=64, Hq=40, Hkv=8, R=8, page=128, T=640, qtype=U.BF16, scale=0.2),
     dict(ktype=U.F16, D=128, Hq=16, Hkv=4, R=8, page=64, T=512, softcap=30.0, scale=0.25),
+    # f16 queries on the 129..160-vector layout (the tile-0 lo MMAs are skipped: every lo part is 0)
+    dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=32, page=128, T=512, L=2, qtype=U.F16),
+    dict(ktype=U.F16, D=64, Hq=40, Hkv=8, R=30, page=64, T=384, qtype=U.BF16),
 ]
 
 
