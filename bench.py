@@ -614,6 +614,46 @@ def run_ours(args, world, rank, local):
         g_ms.append(ev0.elapsed_time(ev1))
     gather_ms = statistics.median(g_ms)
 
+    # The reference's stage-in route for the same cold set, restated: each page record is
+    # copied out of the store into a host vector (src/adapter/llama-memory-kvmem.cpp:4501-4502),
+    # then into a 32 MiB pinned slab; a full slab goes to a device staging buffer with one
+    # H2D copy and an event wait, then one D2D copy per item into its cache slot
+    # (src/adapter/llama-kvmem-stagein.cu:673-794). Python drives the item loop.
+    slot_of, _ = pool.read()
+    slab_bytes = 32 << 20
+    slab = torch.empty(slab_bytes, dtype=torch.uint8, pin_memory=True)
+    slab_np = slab.numpy()
+    dev_q = torch.empty(slab_bytes, dtype=torch.uint8, device=dev)
+    items = []
+    hk, hv = h["host_k"].numpy(), h["host_v"].numpy()
+    for r in range(srows):
+        for p in np.nonzero(slot_of[r] >= 0)[0]:
+            s_ = int(slot_of[r, p])
+            items.append((hk, r * h["layer_k"] + int(p) * page_k, cache_k, (r * slots + s_) * page_k, page_k))
+            items.append((hv, r * h["layer_v"] + int(p) * page_v, cache_v, (r * slots + s_) * page_v, page_v))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    used, pending = 0, []
+
+    def flush():
+        dev_q[:used].copy_(slab[:used], non_blocking=True)
+        torch.cuda.synchronize()  # the slab is reused by the next batch
+        for dst, doff, off, n in pending:
+            dst[doff:doff + n].copy_(dev_q[off:off + n], non_blocking=True)
+
+    for src, soff, dst, doff, n in items:
+        if used + n > slab_bytes:
+            flush()
+            used, pending = 0, []
+        slab_np[used:used + n] = src[soff:soff + n].copy()
+        pending.append((dst, doff, used, n))
+        used += n
+    if pending:
+        flush()
+    torch.cuda.synchronize()
+    ref_route_ms = (time.perf_counter() - t0) * 1e3
+    del slab, dev_q
+
     # Stage-out (harvest) of one filled block per layer: its K and V bytes from the
     # device cache into the two 32 MiB pinned slots in turn -> D2H link GB/s.
     so = K.StageOut(local)
@@ -729,6 +769,11 @@ def run_ours(args, world, rank, local):
                  "note": "every selected page staged every step (force_reload)"},
         "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
                     "ctas": args.stage_ctas, "link": "PCIe Gen5 x16 (mapped pinned host reads)"},
+        "stagein_reference_route": {"ms": ref_route_ms, "bytes": cold_bytes,
+                                    "GB/s": cold_bytes / (ref_route_ms * 1e-3) / 1e9,
+                                    "route": "two host memcpys per record (store -> vector -> 32 MiB pinned slab), "
+                                             "one H2D per slab, one D2D per item (the reference's slab "
+                                             "route, restated; host clock)"},
         "stageout": {"ms": stageout_ms, "bytes": out_bytes, "GB/s": out_bytes / (stageout_ms * 1e-3) / 1e9,
                      "what": "K+V of one block per layer into two 32 MiB pinned slots in turn (host clock, "
                              "submit to last slot observed)", "ctas": args.stage_ctas},
