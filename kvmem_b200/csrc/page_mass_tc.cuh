@@ -32,6 +32,7 @@
 #include <cuda.h>
 
 #include "page_mass.cuh"
+#include "page_mass_mma.cuh"  // pack_half2
 
 namespace kvmb {
 
