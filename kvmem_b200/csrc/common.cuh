@@ -83,7 +83,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-// Tiled 4-D TMA load of one box into this CTA's shared memory (no multicast).
+// Tiled 4-D TMA load of one box into this CTA's shared memory (this CTA only).
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
                                             uint64_t* bar, uint64_t policy) {
     asm volatile(
