@@ -165,56 +165,86 @@ def barrier(world):
 
 # --------------------------------------------------------------------------- data
 
+def _mem_available_bytes() -> int:
+    with open("/proc/meminfo") as f:
+        for line in f:
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    return 0
+
+
 class HostStore:
     """Pinned, device-mapped host memory for the K / V page records.
 
     One process: torch pinned memory. Several ranks on one node (replicas of the same
-    history): one POSIX shared-memory segment per node, filled by local rank 0 and
+    history): one anonymous shared-memory file (memfd) per node, created by local rank 0,
+    opened by the other ranks through /proc/<pid>/fd, filled by local rank 0 and
     registered as mapped pinned memory by every rank, so the node holds one copy of the
     records instead of one per rank (a config-2 history is 34 GB of K and V records;
-    eight private copies would not fit a 251 GB host)."""
+    eight private copies would not fit a 251 GB host). A memfd is not bounded by the
+    size of /dev/shm, which some containers keep small."""
 
     def __init__(self, nbytes: int, tag: str, world: int, local: int):
+        import mmap
+
         import torch
-        self.shm, self.registered, self.owner = None, False, False
+        self.mm, self.fd, self.registered, self.shared = None, None, False, world > 1
         if world == 1:
             self.tensor = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
             return
-        from multiprocessing import resource_tracker, shared_memory
-        name = f"kvm_{tag}_{os.environ.get('MASTER_PORT', '0')}_{os.getppid()}"
+        import torch.distributed as dist
+        info = [None]
         if local == 0:
-            self.shm = shared_memory.SharedMemory(name=name, create=True, size=nbytes)
-            self.owner = True
-        barrier(world)
+            self.fd = os.memfd_create(f"kvm_{tag}", 0)
+            os.ftruncate(self.fd, nbytes)
+            info = [(os.getpid(), self.fd)]
+        dist.broadcast_object_list(info, src=0)
         if local != 0:
-            self.shm = shared_memory.SharedMemory(name=name)
-            # Only the creating rank removes the segment (attachers would unlink it at exit).
-            resource_tracker.unregister(self.shm._name, "shared_memory")
-        self.tensor = torch.frombuffer(self.shm.buf, dtype=torch.uint8)
+            pid, fd = info[0]
+            self.fd = os.open(f"/proc/{pid}/fd/{fd}", os.O_RDWR)
+        self.mm = mmap.mmap(self.fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+        self.tensor = torch.frombuffer(self.mm, dtype=torch.uint8)
         err = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 3)  # portable | mapped
-        if int(err) != 0:
-            raise RuntimeError(f"cudaHostRegister of the shared page records failed ({int(err)})")
-        self.registered = True
+        ok = torch.tensor([int(err) == 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank takes the same path
+        if int(err) == 0:
+            self.registered = True
+        barrier(world)  # every rank has opened the file before rank 0 may drop its descriptor
+        if not int(ok.item()):
+            # Shared registration refused on some rank: private pinned records per rank,
+            # only when all of them fit well inside the host's available memory.
+            self.close(world)
+            avail = [_mem_available_bytes()] if local == 0 else [0]
+            dist.broadcast_object_list(avail, src=0)
+            if world * nbytes > 0.35 * avail[0]:
+                raise RuntimeError(f"cudaHostRegister of the shared page records failed (here: {int(err)}) and "
+                                   f"{world} private copies of {nbytes / 1e9:.1f} GB do not fit the host")
+            self.shared = False
+            self.tensor = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
 
     def close(self, world: int):
         import torch
-        if self.shm is None:
+        if self.mm is None:
             return
         if self.registered:
             torch.cuda.cudart().cudaHostUnregister(self.tensor.data_ptr())
+            self.registered = False
         del self.tensor
         barrier(world)
-        self.shm.close()
-        if self.owner:
-            self.shm.unlink()
-        self.shm = None
+        try:
+            self.mm.close()
+        except BufferError:
+            pass  # views of the records are still alive; the mapping goes at exit
+        os.close(self.fd)
+        self.mm = None
 
 
 def build_history(w, seed, device, need_host=True, world=1, local=0):
     """K score mirror on the device, pinned host K/V pages, device paged cache.
 
     With world > 1 every rank builds the same history (same seed) and the host page
-    records are one node-shared store written by local rank 0."""
+    records are one node-shared store written by local rank 0 (private per rank only
+    when the shared store cannot be registered)."""
     import torch
     from kvmem_b200 import row_bytes, synth
     rbk = row_bytes(w.k_type, w.head_dim)
@@ -226,19 +256,22 @@ def build_history(w, seed, device, need_host=True, world=1, local=0):
     k_dev = torch.empty(w.layers * layer_k, dtype=torch.uint8, device=device)
     host_k = host_v = None
     stores = []
-    write_host = need_host and local == 0
+    write_k = write_v = False
     if need_host:
         sk, sv = HostStore(w.layers * layer_k, "k", world, local), HostStore(w.layers * layer_v, "v", world, local)
         stores = [sk, sv]
         host_k, host_v = sk.tensor, sv.tensor
+        # A shared store is written once per node, a private one by its rank.
+        write_k, write_v = local == 0 or not sk.shared, local == 0 or not sv.shared
     for l in range(w.layers):
         if w.k_type == 1:
             kl = synth.fp16_layer(w, seed, l, q_base, device).view(torch.uint8).reshape(-1)
         else:
             kl = synth.q8_0_layer(w, seed, l, q_base, device).reshape(-1)
         k_dev[l * layer_k:(l + 1) * layer_k].copy_(kl)
-        if write_host:
+        if write_k:
             host_k[l * layer_k:(l + 1) * layer_k].copy_(kl)
+        if write_v:
             vl = (synth.fp16_v_layer(w, seed, l, device).view(torch.uint8).reshape(-1) if w.v_type == 1
                   else synth.q4_0_v_layer(w, seed, l, device).reshape(-1))
             host_v[l * layer_v:(l + 1) * layer_v].copy_(vl)
