@@ -173,6 +173,14 @@ def _mem_available_bytes() -> int:
     return 0
 
 
+def _clear_cuda_error() -> None:
+    """Reads and clears the CUDA runtime's last-error state (the library torch loaded)."""
+    try:
+        C.CDLL("libcudart.so.12").cudaGetLastError()
+    except OSError:
+        pass
+
+
 class HostStore:
     """Pinned, device-mapped host memory for the K / V page records.
 
@@ -209,6 +217,8 @@ class HostStore:
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank takes the same path
         if int(err) == 0:
             self.registered = True
+        else:
+            _clear_cuda_error()  # a refused registration must not surface at the next launch check
         barrier(world)  # every rank has opened the file before rank 0 may drop its descriptor
         if not int(ok.item()):
             # Shared registration refused on some rank: private pinned records per rank,
