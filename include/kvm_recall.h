@@ -62,12 +62,27 @@ typedef struct kvm_pool kvm_pool;
 
 /* Current-step queries: element (l, r, h, d) at
  * data + l*layer_stride + r*row_stride + h*head_stride + d*sizeof(type).
- * type F32, F16 or BF16; device memory. */
+ * type F32, F16 or BF16; device memory; data and strides 2-byte aligned.
+ *
+ * Sampled rows (the reference's `rows` list of
+ * llama_kvmem_attention_cuda::score, src/adapter/llama-kvmem-attention-cuda.cu:146-190):
+ * with row_ids != NULL, scored row i (i < rows) is query row row_ids[i] of the
+ * tensor and reads mask row row_ids[i]; outputs are indexed by i. row_ids is a
+ * HOST array of at most 512 entries, each below row_count (the rows the tensor
+ * holds, the reference's q->ne[1]), else KVM_ERR_INVALID_ARGUMENT. Only
+ * kvm_score_pages and kvm_score_pages_noalloc take a row list (others return
+ * KVM_ERR_UNSUPPORTED). The listed query rows, and their mask rows, are packed
+ * densely into the scoring workspace first: it then needs, beyond
+ * kvm_score_workspace_bytes, layers*rows*q_heads*head_dim*sizeof(type) plus,
+ * with a mask, rows*tokens*sizeof(mask type) bytes, each rounded up to 256. */
 typedef struct kvm_query {
     const void* data;
     int32_t type;
     uint32_t rows;
     uint64_t layer_stride, row_stride, head_stride;
+    const uint32_t* row_ids; /* optional host u32 [rows]; NULL = rows 0 .. rows-1 */
+    uint32_t row_count;      /* rows held by the tensor (used with row_ids) */
+    uint32_t reserved;
 } kvm_query;
 
 /* K history in HBM, token-major rows as in the engine's K cache view
@@ -152,8 +167,9 @@ int kvm_score_pages(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q
  *  - Runs on the current device. The first call on a device looks up the
  *    array's device address; make that first call before any stream capture.
  *  - Needs layers * rows * q_heads * pages * 4 bytes (rounded up to 256) of
- *    scratch, at most 8 MiB - 256 B; larger problems return KVM_ERR_LENGTH
- *    before any launch.
+ *    scratch, plus the packed rows of a row list (see kvm_query), at most
+ *    8 MiB - 256 B in all; larger problems return KVM_ERR_LENGTH before any
+ *    launch.
  *  - Every call uses the same array; the status word is cleared on each call,
  *    the rest is fully rewritten. Calls that overlap on the GPU (two streams,
  *    two threads) race on it: order them on one stream.

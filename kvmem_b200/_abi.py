@@ -49,7 +49,8 @@ class KvmError(RuntimeError):
 
 class Query(C.Structure):
     _fields_ = [("data", C.c_void_p), ("type", C.c_int32), ("rows", C.c_uint32),
-                ("layer_stride", C.c_uint64), ("row_stride", C.c_uint64), ("head_stride", C.c_uint64)]
+                ("layer_stride", C.c_uint64), ("row_stride", C.c_uint64), ("head_stride", C.c_uint64),
+                ("row_ids", C.POINTER(C.c_uint32)), ("row_count", C.c_uint32), ("reserved", C.c_uint32)]
 
 
 class KCache(C.Structure):

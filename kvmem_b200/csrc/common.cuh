@@ -6,9 +6,30 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "kvm_recall.h"
 
 namespace kvmb {
+
+// Raises the dynamic shared-memory limit of kernel `fn` to `bytes` on the
+// current device, once per (kernel, device). The attribute belongs to the
+// device, so a process that drives several GPUs sets it on each of them.
+inline cudaError_t smem_attr(const void* fn, int bytes) {
+    int device = -1;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return e;
+    static std::mutex m;
+    static std::set<std::pair<const void*, int>> done;
+    std::lock_guard<std::mutex> lock(m);
+    if (done.count({fn, device})) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({fn, device});
+    else cudaGetLastError();
+    return e;
+}
 
 // Upper bound on polls of one mbarrier / flag before a kernel gives up,
 // records KVM_ERR_TIMEOUT and unwinds (a few seconds at the longest).

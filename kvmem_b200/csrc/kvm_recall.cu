@@ -16,6 +16,7 @@
 #include "page_norm.cuh"
 #include "post.cuh"
 #include "restore.cuh"
+#include "rows.cuh"
 #include "select.cuh"
 #include "shard.cuh"
 #include "stagein.cuh"
@@ -530,10 +531,7 @@ int normalize_layers(kvm_ctx* c, const kvm_score_desc* d, uint32_t rows, uint32_
     const uint32_t heads_per = d->groups == 1 ? d->q_heads : G;
     const size_t nsmem = size_t(rows) * heads_per * sizeof(float2);
     if (nsmem > 200 * 1024) return KVM_ERR_LENGTH;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(page_mass_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(page_mass_normalize_kernel), 200 * 1024));
     page_mass_normalize_kernel<<<nl * d->groups, 256, nsmem, s>>>(lse, rows, d->q_heads, G, d->groups, pages,
                                                                  mass_rows, mass_mean, l0, given);
     ++c->launches;
@@ -548,6 +546,65 @@ int score_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const 
     const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
     KVM_TRY(lse_layers(c, d, q, k, cfg, l0, nl, pages, d->tokens, lse, s));
     return normalize_layers(c, d, q->rows, l0, nl, pages, lse, nullptr, mass_rows, mass_mean, s);
+}
+
+// Workspace bytes of a sampled-row call's packed query rows and mask rows
+// (both 0 without a row list); validates the list and the alignment the
+// packing kernels need.
+int row_pack_bytes(const kvm_score_desc* d, const kvm_query* q, size_t* qbytes, size_t* mbytes) {
+    *qbytes = *mbytes = 0;
+    if (!q->row_ids) return KVM_OK;
+    if (q->rows > kMaxRowIds) return KVM_ERR_LENGTH;
+    for (uint32_t i = 0; i < q->rows; ++i)
+        if (q->row_ids[i] >= q->row_count) return KVM_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(q->data) | q->layer_stride | q->row_stride | q->head_stride) & 1)
+        return KVM_ERR_INVALID_ARGUMENT;
+    *qbytes = align256(size_t(d->layers) * q->rows * d->q_heads * d->head_dim * type_bytes(q->type));
+    if (d->mask) {
+        if ((reinterpret_cast<uintptr_t>(d->mask) | d->mask_row_stride) & 1) return KVM_ERR_INVALID_ARGUMENT;
+        const uint64_t rb = d->tokens * type_bytes(d->mask_type);
+        if (rb > 0x7fffffffull) return KVM_ERR_LENGTH;
+        *mbytes = align256(size_t(q->rows) * rb);
+    }
+    return KVM_OK;
+}
+
+// Packs the listed query rows (and their mask rows) densely at `dst` (query
+// rows first, `qbytes` of them, then mask rows) and points `dd` / `qq` at the
+// copies, so the scorers see rows 0 .. n-1.
+int pack_rows(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, uint8_t* dst, size_t qbytes,
+              kvm_score_desc* dd, kvm_query* qq, cudaStream_t s) {
+    RowIds ids{};
+    ids.n = q->rows;
+    for (uint32_t i = 0; i < q->rows; ++i) ids.id[i] = q->row_ids[i];
+    const uint32_t head_bytes = d->head_dim * type_bytes(q->type);
+    const uint64_t chunks = uint64_t(d->layers) * q->rows * d->q_heads;
+    const uint32_t grid = uint32_t(std::min<uint64_t>(chunks, uint64_t(c->num_sms) * 8));
+    pack_query_rows_kernel<<<grid, 128, 0, s>>>(static_cast<const uint8_t*>(q->data), q->layer_stride,
+                                                q->row_stride, q->head_stride, d->q_heads, head_bytes, d->layers,
+                                                ids, dst);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    *qq = *q;
+    qq->data = dst;
+    qq->row_ids = nullptr;
+    qq->row_count = q->rows;
+    qq->head_stride = head_bytes;
+    qq->row_stride = uint64_t(d->q_heads) * head_bytes;
+    qq->layer_stride = uint64_t(q->rows) * qq->row_stride;
+    *dd = *d;
+    if (d->mask) {
+        const uint32_t rb = uint32_t(d->tokens * type_bytes(d->mask_type));
+        uint8_t* mdst = dst + qbytes;
+        const dim3 mgrid(std::max<uint32_t>(1, std::min<uint32_t>((rb / 2 + 255) / 256, 64)), q->rows);
+        pack_mask_rows_kernel<<<mgrid, 256, 0, s>>>(static_cast<const uint8_t*>(d->mask), d->mask_row_stride, rb,
+                                                    ids, mdst);
+        ++c->launches;
+        KVM_CUDA(cudaGetLastError());
+        dd->mask = mdst;
+        dd->mask_row_stride = rb;
+    }
+    return KVM_OK;
 }
 
 int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
@@ -566,10 +623,7 @@ int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages,
     }
     if (distinct > budget) return KVM_ERR_BUDGET_EXCEEDED;
     KVM_TRY(upload_keep(c, keep, nkeep));
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(select_topk_kernel), 200 * 1024));
     select_topk_kernel<<<nrows, kSelectThreads, pages, s>>>(scores, pages, score_stride,
                                                              static_cast<const uint32_t*>(c->small), nkeep, budget,
                                                              signed_scores, out_ids, out_n, out_stride, c->status);
@@ -581,10 +635,7 @@ int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages,
 int plan_rows(kvm_ctx* c, kvm_pool* pool, uint32_t row0, uint32_t nrows, const uint32_t* sel_ids,
               const uint32_t* sel_n, uint32_t sel_stride, int force, uint32_t* n_restore, uint32_t* n_evict,
               cudaStream_t s) {
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(plan_residency_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(plan_residency_kernel), 200 * 1024));
     plan_residency_kernel<<<nrows, kPlanThreads, pool->view.pages, s>>>(pool->view, row0, sel_ids, sel_n, sel_stride,
                                                                          force, n_restore, n_evict, c->status);
     ++c->launches;
@@ -722,10 +773,16 @@ int kvm_score_pages(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, con
     if (!c) return KVM_ERR_INVALID_ARGUMENT;
     LseConfig cfg;
     KVM_TRY(validate_score(d, q, k, &cfg));
+    size_t qb = 0, mb = 0;
+    KVM_TRY(row_pack_bytes(d, q, &qb, &mb));
     DeviceGuard guard(c->device);
     auto s = static_cast<cudaStream_t>(stream);
-    KVM_TRY(ensure_ws(c, lse_bytes(d, d->layers, q->rows)));
-    return score_layers(c, d, q, k, cfg, 0, d->layers, static_cast<float*>(c->ws), mass_rows, mass_mean, s);
+    const size_t lb = lse_bytes(d, d->layers, q->rows);
+    KVM_TRY(ensure_ws(c, lb + qb + mb));
+    kvm_score_desc dd = *d;
+    kvm_query qq = *q;
+    if (q->row_ids) KVM_TRY(pack_rows(c, d, q, static_cast<uint8_t*>(c->ws) + lb, qb, &dd, &qq, s));
+    return score_layers(c, &dd, &qq, k, cfg, 0, d->layers, static_cast<float*>(c->ws), mass_rows, mass_mean, s);
 }
 
 int kvm_select_topk(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
@@ -1130,11 +1187,8 @@ int kvm_restore_k(kvm_ctx* c, int type, const kvm_restore_item* items, uint32_t 
     const auto* di = reinterpret_cast<const RestoreItem*>(a + o_items);
     const auto* db = reinterpret_cast<const uint64_t*>(a + o_base);
     const auto* dt = reinterpret_cast<const float*>(a + o_theta);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(restore_k_kernel<KVM_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-        cudaFuncSetAttribute(restore_k_kernel<KVM_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(restore_k_kernel<KVM_Q8_0>), 64 * 1024));
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(restore_k_kernel<KVM_Q4_0>), 64 * 1024));
     if (type == KVM_Q8_0)
         restore_k_kernel<KVM_Q8_0><<<grid, kRestoreThreads, smem, s>>>(di, n_items, db, n_head, head_dim, n_rot, dt,
                                                                        nrot, scale);
@@ -1409,6 +1463,7 @@ int kvm_recall_step(kvm_ctx* c, const kvm_step_desc* st, kvm_pool* pool, const k
                     float* mass_mean, uint32_t* sel_ids, uint32_t* sel_n, void* stream) {
     if (!c || !st || !st->score || !mass_mean || !sel_ids || !sel_n || !st->budget) return KVM_ERR_INVALID_ARGUMENT;
     const kvm_score_desc* d = st->score;
+    if (st->q && st->q->row_ids) return KVM_ERR_UNSUPPORTED;  // decode rows are dense
     LseConfig cfg;
     KVM_TRY(validate_score(d, st->q, st->k, &cfg));
     const uint32_t pages = uint32_t((d->tokens + d->page_tokens - 1) / d->page_tokens);
@@ -1498,7 +1553,10 @@ extern "C" int kvm_score_pages_noalloc(const kvm_score_desc* d, const kvm_query*
                                        float* mass_rows, float* mass_mean, void* stream) {
     LseConfig cfg;
     KVM_TRY(validate_score(d, q, k, &cfg));
-    if (kNoAllocStatusBytes + lse_bytes(d, d->layers, q->rows) > kNoAllocScratchBytes) return KVM_ERR_LENGTH;
+    size_t qb = 0, mb = 0;
+    KVM_TRY(row_pack_bytes(d, q, &qb, &mb));
+    const size_t lb = lse_bytes(d, d->layers, q->rows);
+    if (kNoAllocStatusBytes + lb + qb + mb > kNoAllocScratchBytes) return KVM_ERR_LENGTH;
     int device = -1;
     KVM_CUDA(cudaGetDevice(&device));
     if (device < 0 || device >= kNoAllocMaxDevices) return KVM_ERR_UNSUPPORTED;
@@ -1512,9 +1570,11 @@ extern "C" int kvm_score_pages_noalloc(const kvm_score_desc* d, const kvm_query*
     KVM_CUDA(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
     c.status = static_cast<DeviceStatus*>(base);
     KVM_CUDA(cudaMemsetAsync(base, 0, sizeof(DeviceStatus), s));
-    return score_layers(&c, d, q, k, cfg, 0, d->layers,
-                        reinterpret_cast<float*>(static_cast<uint8_t*>(base) + kNoAllocStatusBytes), mass_rows,
-                        mass_mean, s);
+    uint8_t* lse = static_cast<uint8_t*>(base) + kNoAllocStatusBytes;
+    kvm_score_desc dd = *d;
+    kvm_query qq = *q;
+    if (q->row_ids) KVM_TRY(pack_rows(&c, d, q, lse + lb, qb, &dd, &qq, s));
+    return score_layers(&c, &dd, &qq, k, cfg, 0, d->layers, reinterpret_cast<float*>(lse), mass_rows, mass_mean, s);
 }
 
 // ------------------------------------------------------------- page-range sharding
@@ -1535,6 +1595,7 @@ extern "C" {
 int kvm_shard_score_partial(kvm_ctx* c, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
                             uint32_t page0, uint32_t local_pages, float* stats, void* stream) {
     if (!c || !desc || !q || !stats || !local_pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (q->row_ids) return KVM_ERR_UNSUPPORTED;
     // Validate and plan with the local slice; visibility follows the global token count.
     kvm_score_desc local = *desc;
     local.tokens = uint64_t(local_pages) * desc->page_tokens;
@@ -1589,10 +1650,7 @@ int kvm_shard_candidates(kvm_ctx* c, const float* scores, uint32_t nrows, uint32
     DeviceGuard guard(c->device);
     KVM_TRY(upload_keep(c, kd.data(), uint32_t(kd.size())));
     auto s = static_cast<cudaStream_t>(stream);
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(shard_candidates_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(shard_candidates_kernel), 200 * 1024));
     shard_candidates_kernel<<<nrows, kSelectThreads, local_pages, s>>>(
         scores, local_pages, score_stride, page0, static_cast<const uint32_t*>(c->small), uint32_t(kd.size()), k,
         cand_scores, cand_ids, c->status);
@@ -1616,10 +1674,7 @@ int kvm_shard_merge(kvm_ctx* c, const float* cand_scores, const uint32_t* cand_i
     auto s = static_cast<cudaStream_t>(stream);
     const size_t smem = size_t(ranks) * k * 8 + (size_t(budget) + kd.size()) * 4;
     if (smem > 200 * 1024) return KVM_ERR_LENGTH;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(shard_merge_kernel), 200 * 1024));
     shard_merge_kernel<<<nrows, kSelectThreads, smem, s>>>(cand_scores, cand_ids, ranks, k, nrows,
                                                             static_cast<const uint32_t*>(c->small),
                                                             uint32_t(kd.size()), budget, out_ids, out_n, out_stride);

@@ -45,12 +45,7 @@ namespace kvmb {
 template <int KT, int LPR, int VP, bool MASK>
 int launch_lse_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
     auto fn = page_lse_kernel<KT, LPR, VP, MASK>;
-    static std::once_flag once;  // one attribute set per instantiation
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
-    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    if (smem_attr(reinterpret_cast<const void*>(fn), 200 * 1024) != cudaSuccess) return KVM_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLseThreads, smem) != cudaSuccess) {
         cudaGetLastError();
@@ -92,12 +87,7 @@ int launch_lse_kt(kvm_ctx* c, const LseParams& p, int lpr, int vp, size_t smem, 
 template <int KT, int KK, bool MASK>
 int launch_lse_mma_t(kvm_ctx* c, const LseParams& p, size_t smem, cudaStream_t s) {
     auto fn = page_lse_mma_kernel<KT, KK, MASK>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
-    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    if (smem_attr(reinterpret_cast<const void*>(fn), 200 * 1024) != cudaSuccess) return KVM_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLseThreads, smem) != cudaSuccess) {
         cudaGetLastError();
@@ -129,12 +119,7 @@ int launch_lse_mma_kt(kvm_ctx* c, const LseParams& p, int kk, size_t smem, cudaS
 template <int KT, int KK, int KVH, bool MASK>
 int launch_lse_q_t(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, size_t smem, cudaStream_t s) {
     auto fn = page_lse_q_kernel<KT, KK, KVH, MASK>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    });
-    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    if (smem_attr(reinterpret_cast<const void*>(fn), 200 * 1024) != cudaSuccess) return KVM_ERR_CUDA;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kQThreads, smem) != cudaSuccess) {
         cudaGetLastError();

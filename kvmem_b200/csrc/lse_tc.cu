@@ -12,12 +12,7 @@ namespace {
 template <int KA, int LM, bool MASK>
 int launch_tc_t(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, size_t smem, cudaStream_t s) {
     auto fn = page_lse_tc_kernel<KA, LM, MASK>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmemMax));
-    });
-    if (attr_err != cudaSuccess) return KVM_ERR_CUDA;
+    if (smem_attr(reinterpret_cast<const void*>(fn), int(kTcSmemMax)) != cudaSuccess) return KVM_ERR_CUDA;
     if (smem > kTcSmemMax) return KVM_ERR_UNSUPPORTED;
     const uint64_t units = uint64_t(p.layers) * p.kv_heads * tc_units_per_head(p.pages, p.page_tokens);
     if (!units) return KVM_OK;

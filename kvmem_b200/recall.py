@@ -89,8 +89,11 @@ class RecallContext:
         return d
 
     @staticmethod
-    def make_query(q: torch.Tensor, rows: int, *, strides=None, data_ptr: Optional[int] = None) -> A.Query:
-        """q dense [layers][rows][heads][dim] unless strides=(layer, row, head) bytes."""
+    def make_query(q: torch.Tensor, rows: int, *, strides=None, data_ptr: Optional[int] = None,
+                   row_ids: Optional[Sequence[int]] = None, row_count: int = 0) -> A.Query:
+        """q dense [layers][rows][heads][dim] unless strides=(layer, row, head) bytes.
+        row_ids: score only these rows of the tensor (the reference's sampled `rows`);
+        `rows` is then len(row_ids) and row_count the rows the tensor holds."""
         qq = A.Query()
         qq.data = data_ptr if data_ptr is not None else q.data_ptr()
         qq.type = _TORCH_QTYPE[q.dtype]
@@ -100,6 +103,12 @@ class RecallContext:
             L, R, H, D = q.shape
             strides = (R * H * D * es, H * D * es, D * es)
         qq.layer_stride, qq.row_stride, qq.head_stride = strides
+        if row_ids is not None:
+            ids = (C.c_uint32 * max(1, len(row_ids)))(*row_ids)
+            qq.row_ids = C.cast(ids, C.POINTER(C.c_uint32))
+            qq._ids = ids  # keeps the host list alive with the descriptor
+            qq.rows = len(row_ids)
+            qq.row_count = row_count or (q.shape[1] if q.dim() == 4 else 0)
         return qq
 
     @staticmethod
@@ -490,26 +499,28 @@ class AttentionCuda:
         kc.data, kc.type = k.data.data_ptr(), k.type
         kc.layer_stride, kc.token_stride, kc.head_stride = 0, k.nb[1], k.nb[2]
         kc.capacity_tokens = T
-        out = []
-        for r in rows:
-            qq = A.Query()
-            qq.data = q.data.data_ptr() + r * q.nb[1]
-            qq.type, qq.rows = q.type, 1
-            qq.layer_stride, qq.row_stride, qq.head_stride = 0, q.nb[1], q.nb[2]
-            if mask is not None:
-                desc.mask = mask.data.data_ptr() + r * mask.nb[1]
-                desc.mask_type = mask.type
-                desc.mask_row_stride = mask.nb[1]
-            _, mean = None, None
-            try:
-                _, mean = self.ctx.score_pages(desc, qq, kc, want_rows=False)
-            except A.KvmError as e:
-                if e.code == A.ERR_UNSUPPORTED:
-                    return None
-                raise
-            out.append(mean.view(pages).tolist())
+        if not rows:
+            return []
+        # Every sampled row in one call (one pass over K), as the reference's batch.
+        qq = A.Query()
+        qq.data = q.data.data_ptr()
+        qq.type = q.type
+        qq.layer_stride, qq.row_stride, qq.head_stride = 0, q.nb[1], q.nb[2]
+        ids = (C.c_uint32 * len(rows))(*rows)
+        qq.row_ids = C.cast(ids, C.POINTER(C.c_uint32))
+        qq.rows, qq.row_count = len(rows), q.ne[1]
+        if mask is not None:
+            desc.mask = mask.data.data_ptr()
+            desc.mask_type = mask.type
+            desc.mask_row_stride = mask.nb[1]
+        try:
+            out_rows, _ = self.ctx.score_pages(desc, qq, kc, want_mean=False)
+        except A.KvmError as e:
+            if e.code == A.ERR_UNSUPPORTED:
+                return None
+            raise
         self.ctx.check_status("llama_kvmem_attention_cuda::score")
-        return out
+        return out_rows.view(len(rows), pages).tolist()
 
 
 class PageSoftmaxCuda:

@@ -436,38 +436,60 @@ int kvo_page_mass(const uint8_t* q, int q_type, uint64_t q_layer, uint64_t q_row
     const uint64_t pages = (tokens + page_tokens - 1) / page_tokens;
     const uint32_t group = heads / kv_heads;
     const uint32_t per_group = groups == 1 ? heads : group;
-    double* logits = (double*)malloc(sizeof(double) * (tokens ? tokens : 1));
-    double* qv = (double*)malloc(sizeof(double) * dim);
-    if (!logits || !qv) { free(logits); free(qv); return KVO_ERR_RUNTIME; }
+    /* Each K row is decoded once and dotted with the `group` query heads that
+     * share its KV head; every dot is the same FP64 sum in dimension order. */
+    const uint64_t nt = tokens ? tokens : 1;
+    double* logits = (double*)malloc(sizeof(double) * nt * group);
+    double* qv = (double*)malloc(sizeof(double) * dim * group);
+    double* kv = (double*)malloc(sizeof(double) * dim);
+    double* maxima = (double*)malloc(sizeof(double) * group);
+    if (!logits || !qv || !kv || !maxima) {
+        free(logits); free(qv); free(kv); free(maxima);
+        return KVO_ERR_RUNTIME;
+    }
     memset(out, 0, sizeof(double) * layers * groups * rows * pages);
     for (uint32_t l = 0; l < layers; ++l)
         for (uint32_t r = 0; r < rows; ++r)
-            for (uint32_t h = 0; h < heads; ++h) {
-                const uint8_t* qb = q + l * q_layer + r * q_row + h * q_head;
-                for (uint32_t d = 0; d < dim; ++d) qv[d] = kvo_decode(q_type, qb, d);
-                const uint32_t kvh = h / group;
-                double maximum = -INFINITY;
+            for (uint32_t kvh = 0; kvh < kv_heads; ++kvh) {
+                for (uint32_t g = 0; g < group; ++g) {
+                    const uint8_t* qb = q + l * q_layer + r * q_row + (kvh * group + g) * q_head;
+                    for (uint32_t d = 0; d < dim; ++d) qv[g * dim + d] = kvo_decode(q_type, qb, d);
+                    maxima[g] = -INFINITY;
+                }
                 for (uint64_t t = 0; t < tokens; ++t) {
                     const double bias = mask ? (double)mask[r * mask_row + t] : 0.0;
-                    if (!isfinite(bias)) { logits[t] = -INFINITY; continue; }
+                    if (!isfinite(bias)) {
+                        for (uint32_t g = 0; g < group; ++g) logits[g * nt + t] = -INFINITY;
+                        continue;
+                    }
                     const uint8_t* kb = k + l * k_layer + t * k_row + kvh * k_head;
-                    double dot = 0;
-                    for (uint32_t d = 0; d < dim; ++d) dot += qv[d] * kvo_decode(k_type, kb, d);
-                    dot *= scale;
-                    if (softcap > 0) dot = softcap * tanh(dot / softcap);
-                    logits[t] = dot + bias;
-                    if (logits[t] > maximum) maximum = logits[t];
+                    for (uint32_t d = 0; d < dim; ++d) kv[d] = kvo_decode(k_type, kb, d);
+                    for (uint32_t g = 0; g < group; ++g) {
+                        const double* qg = qv + g * dim;
+                        double dot = 0;
+                        for (uint32_t d = 0; d < dim; ++d) dot += qg[d] * kv[d];
+                        dot *= scale;
+                        if (softcap > 0) dot = softcap * tanh(dot / softcap);
+                        const double logit = dot + bias;
+                        logits[g * nt + t] = logit;
+                        if (logit > maxima[g]) maxima[g] = logit;
+                    }
                 }
-                double* row_out = out + (((uint64_t)l * groups + (groups == 1 ? 0 : kvh)) * rows + r) * pages;
-                if (maximum == -INFINITY) {
-                    for (uint64_t p = 0; p < pages; ++p) row_out[p] = NAN;
-                    continue;
+                for (uint32_t g = 0; g < group; ++g) {
+                    double* lg = logits + g * nt;
+                    double* row_out = out + (((uint64_t)l * groups + (groups == 1 ? 0 : kvh)) * rows + r) * pages;
+                    if (maxima[g] == -INFINITY) {
+                        for (uint64_t p = 0; p < pages; ++p) row_out[p] = NAN;
+                        continue;
+                    }
+                    double denominator = 0;
+                    for (uint64_t t = 0; t < tokens; ++t) denominator += lg[t] = exp(lg[t] - maxima[g]);
+                    for (uint64_t t = 0; t < tokens; ++t)
+                        row_out[t / page_tokens] += lg[t] / denominator / per_group;
                 }
-                double denominator = 0;
-                for (uint64_t t = 0; t < tokens; ++t) denominator += logits[t] = exp(logits[t] - maximum);
-                for (uint64_t t = 0; t < tokens; ++t)
-                    row_out[t / page_tokens] += logits[t] / denominator / per_group;
             }
+    free(kv);
+    free(maxima);
     free(logits);
     free(qv);
     return KVO_OK;

@@ -6,7 +6,10 @@ ctypes wrappers over
   algorithms (``oracle/kvm_oracle.c``), and
 * ``oracle/_ref/libkvref.so`` — the reference's own CPU selection code compiled
   from its sources (``oracle/Makefile`` target ``ref``; present only where the
-  reference sources were available when it was built).
+  reference sources were available when it was built), and
+* ``oracle/_ref/libkvref_cuda.so`` — the reference's own GPU scorers compiled
+  from its sources for sm_100a (target ``refcuda``): the per-token page mass
+  ``llama_kvmem_attention_cuda::score`` and the Mean-K ``PageSoftmaxCuda::score``.
 
 Only tests, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference
 arm may import this module. The product package ``kvmem_b200`` never does.
@@ -21,7 +24,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, "_ref")
-REFERENCE_SRC = os.environ.get("KVM_REFERENCE_SRC", "/root/reference")
+# The reference checkout: $KVM_REFERENCE_SRC, else the sibling directory
+# "reference" of the repository root.
+REFERENCE_SRC = os.environ.get("KVM_REFERENCE_SRC") or os.path.normpath(
+    os.path.join(HERE, os.pardir, os.pardir, "reference"))
 
 F32, F16, BF16, Q8_0, Q4_0, Q5_0 = 0, 1, 2, 3, 4, 5
 OK, ERR_INVALID, ERR_RUNTIME = 0, 1, 2
@@ -40,6 +46,9 @@ def build(ref: bool = False) -> None:
     if ref and os.path.isdir(os.path.join(REFERENCE_SRC, "kvmem", "src", "host")):
         subprocess.check_call(["make", "-s", "-j8", "-C", HERE, "ref", f"REF={REFERENCE_SRC}"],
                               stdout=subprocess.DEVNULL)
+        if os.path.exists(os.path.join(REFERENCE_SRC, "src", "adapter", "llama-kvmem-attention-cuda.cu")):
+            subprocess.check_call(["make", "-s", "-j8", "-C", HERE, "refcuda", f"REF={REFERENCE_SRC}"],
+                                  stdout=subprocess.DEVNULL)
 
 
 _PROPAGATE_ARGS = [_f64p, C.c_uint32, _u64p, _u8p, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint64,
@@ -49,6 +58,7 @@ _LRFU_ARGS = [_f64p, C.c_uint32, _f64p, C.c_uint32, C.c_double, C.c_double, _f64
 
 _lib = None
 _ref = None
+_refcuda = None
 
 
 def lib():
@@ -110,6 +120,67 @@ def ref():
         L.kvref_lrfu_preview.argtypes = _LRFU_ARGS
         _ref = L
     return _ref
+
+
+def ref_cuda():
+    """The reference's compiled GPU scorers, or None when absent."""
+    global _refcuda
+    if _refcuda is None:
+        path = os.path.join(REF_DIR, "libkvref_cuda.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        L.kvref_attention_score.argtypes = [
+            C.c_void_p, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint64,
+            C.c_void_p, C.c_int, C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint64,
+            C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_float, C.c_uint32,
+            _u32p, C.c_uint32, _f32p, C.POINTER(C.c_double)]
+        L.kvref_page_softmax_cuda.argtypes = [C.c_int] + ref().kvref_page_softmax_scores.argtypes + [
+            C.POINTER(C.c_double)]
+        L.kvref_cuda_release.argtypes = []
+        _refcuda = L
+    return _refcuda
+
+
+def ref_attention_score(q_ptr: int, q_type: int, *, dim: int, q_rows: int, heads: int, q_row_stride: int,
+                        q_head_stride: int, k_ptr: int, k_type: int, tokens: int, kv_heads: int,
+                        k_token_stride: int, k_head_stride: int, mask_ptr: int, mask_type: int,
+                        mask_row_stride: int, scale: float, softcap: float, block: int, rows) -> tuple:
+    """The reference's llama_kvmem_attention_cuda::score on device buffers (raw
+    pointers of the current CUDA device). Returns (mass [len(rows)][pages] f32,
+    host ms of the call). The reference always takes a mask; pass a zero one
+    for "no mask". Raises on a rejected or unsupported input."""
+    rows = np.ascontiguousarray(rows, np.uint32)
+    pages = -(-tokens // block)
+    out = np.zeros(len(rows) * pages, np.float32)
+    ms = C.c_double()
+    rc = ref_cuda().kvref_attention_score(q_ptr, q_type, dim, q_rows, heads, q_row_stride, q_head_stride, k_ptr,
+                                          k_type, tokens, kv_heads, k_token_stride, k_head_stride, mask_ptr,
+                                          mask_type, mask_row_stride, scale, softcap, block, rows, len(rows), out,
+                                          C.byref(ms))
+    if rc:
+        raise ValueError(f"reference attention score failed (rc={rc})")
+    return out.reshape(len(rows), pages), ms.value
+
+
+def ref_page_softmax_cuda(device, sums, counts, q, layer_rows, *, heads, kv_heads, dim, block, accepted, budget,
+                          sink, recent, fixed=(), aggregation=0, scale=0.0) -> tuple:
+    """The reference's PageSoftmaxCuda::score on `device` over a RawKvStore built
+    from K sums (as ref_page_softmax_scores). Returns (scores [P] f64, host ms)."""
+    sums = np.ascontiguousarray(sums, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    L, P, _ = sums.shape
+    R = q.shape[1]
+    out = np.zeros(P + 1, np.float64)
+    fx = np.ascontiguousarray(list(fixed) or [0], np.uint32)
+    ms = C.c_double()
+    rc = ref_cuda().kvref_page_softmax_cuda(device, sums.reshape(-1), np.ascontiguousarray(counts, np.uint32),
+                                            q.reshape(-1), np.ascontiguousarray(layer_rows, np.uint32), L, R,
+                                            heads, kv_heads, dim, block, accepted, budget, sink, recent, fx,
+                                            len(fixed), aggregation, scale, out, P, C.byref(ms))
+    if rc:
+        raise ValueError(f"reference PageSoftmaxCuda::score failed (rc={rc})")
+    return out[:P], ms.value
 
 
 def row_bytes(ktype: int, dim: int) -> int:

@@ -7,7 +7,7 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.environ.get("KVM_REFERENCE_SRC", "/root/reference")
+REF = os.environ.get("KVM_REFERENCE_SRC") or os.path.normpath(os.path.join(ROOT, os.pardir, "reference"))
 
 
 def test_adapter_compiles_against_the_reference_contract(tmp_path):

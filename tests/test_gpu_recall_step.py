@@ -1,0 +1,165 @@
+"""GPU parity of the product step ``kvm_recall_step`` (score -> per-row top-k ->
+residency plan -> side-stream stage-in, pipelined over layer chunks) at the
+BASELINE configurations, against the oracle and the reference's own picker.
+
+Per step and per selection row:
+
+* page masses within 1e-3 relative (1e-6 absolute) of the FP64 oracle
+  (``kvo_page_mass``, pinned to the reference's kernel by test_gpu_ref_pin.py);
+* the selected page set equal to the compiled reference's ``pick_scored_blocks``
+  (kvmem/src/host/kvmem_store.cpp:418-451, oracle/_ref/libkvref.so) on the oracle's
+  masses wherever the score gap at the k-th boundary exceeds 1e-3 relative (the
+  north-star rule), and always equal to it on the device's own masses;
+* the pool's resident set equal to the selection, and every resident slot of the
+  device cache byte-identical to its host page record (K and V planes).
+
+Configs: 1 at full size (4 layers x 16,384 tokens, 32/8 heads, D 128, per-KV-head
+selection, top-16 + first/last), 2 with 2 of its 64 layers at the full 131,072
+fp16 tokens (top-32 + first/last), 3 with 1 layer at the full 262,144 q8_0 tokens
+(q4_0 V, top-64 + first/last; and once more at top-32). The queries change between
+steps (the workload's query, then one of another seed, then the first again) so
+later steps restore and evict pages, not only the cold first step.
+
+Which rows the gap rule leaves to check: with the workload's own queries the needle
+pages stand far above the rest, so where the selection width does not exceed the
+needle count (configs 2 and 3 at top-32) every row must pass the rule and is
+compared; config 3's top-64 boundary, config 1's top-16 over 8 needles and the
+other seed's queries put the boundary among noise pages, where a row is compared
+only when its gap happens to exceed 1e-3 (the device's pick on its own masses is
+compared in every row).
+"""
+import dataclasses
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GAP = 1e-3
+
+
+def _build(cfg, layers, seed=0):
+    import torch
+    from kvmem_b200 import row_bytes, synth
+    dev = torch.device("cuda", 0)
+    w = dataclasses.replace(synth.CONFIGS[cfg], layers=layers)
+    T = w.pages * w.page_tokens
+    rbk, rbv = row_bytes(w.k_type, w.head_dim), row_bytes(w.v_type, w.head_dim)
+    q0, _ = synth.make_queries(w, seed, dev)
+    q1, _ = synth.make_queries(w, seed + 101, dev)
+    k_dev = torch.empty((layers, T, w.kv_heads, rbk), dtype=torch.uint8, device=dev)
+    v_dev = torch.empty((layers, T, w.kv_heads, rbv), dtype=torch.uint8, device=dev)
+    for l in range(layers):
+        kl = synth.fp16_layer(w, seed, l, q0, dev).view(torch.uint8) if w.k_type == 1 \
+            else synth.q8_0_layer(w, seed, l, q0, dev)
+        k_dev[l] = kl.reshape(T, w.kv_heads, rbk)
+        vl = synth.fp16_v_layer(w, seed, l, dev).view(torch.uint8) if w.v_type == 1 \
+            else synth.q4_0_v_layer(w, seed, l, dev)
+        v_dev[l] = vl.reshape(T, w.kv_heads, rbv)
+    return w, k_dev, v_dev, [q0, q1, q0], rbk, rbv
+
+
+def _records(x, groups):
+    """Host page records of one plane: per selection row (layer, or (layer, KV head) when
+    groups > 1) a contiguous [tokens][...] byte array, pinned."""
+    import torch
+    if groups > 1:
+        x = x.permute(0, 2, 1, 3)  # [L][Hkv][T][row]
+    return x.contiguous().cpu().reshape(-1).pin_memory()
+
+
+def _gap_ok(scores, keep, k):
+    rest = np.sort(np.delete(scores, keep))[::-1]
+    if k >= len(rest):
+        return True
+    top = rest[k - 1]
+    return top > 0 and (top - rest[k]) / top > GAP
+
+
+@pytest.mark.parametrize("cfg,layers,chunks,top_k", [("c1", 4, 2, 0), ("c2", 2, 2, 0), ("c3", 1, 1, 0),
+                                                     ("c3", 1, 1, 32)])
+def test_recall_step_parity(ctx, cfg, layers, chunks, top_k):
+    import torch
+
+    import kvmem_b200 as K
+    from oracle import oracle as O
+    from tests import util as U
+    w, k_dev, v_dev, qs, rbk, rbv = _build(cfg, layers)
+    if top_k:
+        w = dataclasses.replace(w, top_k=top_k)
+    must_check = w.top_k <= w.needles
+    L, P, B, G = w.layers, w.pages, w.page_tokens, w.groups
+    T = P * B
+    srows = L * G
+    slots = w.budget
+    heads_per_rec = 1 if G > 1 else w.kv_heads
+    page_k, page_v = B * heads_per_rec * rbk, B * heads_per_rec * rbv
+    host_k, host_v = _records(k_dev, G), _records(v_dev, G)
+    rec_k = T * heads_per_rec * rbk  # bytes of one selection row's records
+    rec_v = T * heads_per_rec * rbv
+    dev = k_dev.device
+    cache_k = torch.zeros(srows * slots * page_k, dtype=torch.uint8, device=dev)
+    cache_v = torch.zeros(srows * slots * page_v, dtype=torch.uint8, device=dev)
+    layout = K.stage_layout([
+        dict(host_base=host_k.data_ptr(), host_row_stride=rec_k, host_page_stride=page_k,
+             dev_base=cache_k.data_ptr(), dev_row_stride=slots * page_k, dev_slot_stride=page_k, bytes=page_k),
+        dict(host_base=host_v.data_ptr(), host_row_stride=rec_v, host_page_stride=page_v,
+             dev_base=cache_v.data_ptr(), dev_row_stride=slots * page_v, dev_slot_stride=page_v, bytes=page_v)])
+    pool = K.ResidencyPool(ctx, srows, P, slots)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=B, groups=G)
+    kc = K.RecallContext.make_kcache(k_dev, w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim, capacity_tokens=T)
+    mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
+    sel_ids = torch.empty((srows, w.budget), dtype=torch.int32, device=dev)
+    sel_n = torch.empty((srows,), dtype=torch.int32, device=dev)
+    kb = k_dev.cpu().numpy()
+    hk = host_k.numpy().reshape(srows, P, page_k)
+    hv = host_v.numpy().reshape(srows, P, page_v)
+    scale = float(np.float32(1) / np.sqrt(np.float32(w.head_dim)))
+    checked = total = restored = 0
+    prev = None
+    for step, q in enumerate(qs):
+        ctx.recall_step(desc, K.RecallContext.make_query(q, w.rows), kc, w.keep, w.budget, mass_mean=mass,
+                        sel_ids=sel_ids, sel_n=sel_n, pool=pool, layout=layout, chunks=chunks)
+        ctx.wait(120.0)
+        got = mass.cpu().numpy()
+        ids, n = sel_ids.cpu().numpy(), sel_n.cpu().numpy()
+        qb = q.cpu().numpy().view(np.uint8).reshape(L, w.rows, w.q_heads, -1)
+        exp = O.page_mass(qb, U.F32, kb, w.k_type, layers=L, rows=w.rows, heads=w.q_heads, kv_heads=w.kv_heads,
+                          dim=w.head_dim, tokens=w.tokens, page_tokens=B, scale=scale, groups=G)
+        exp = exp.mean(axis=2).reshape(srows, P)
+        ok, worst, nbad = U.close(got, exp, 1e-3, 1e-6)
+        assert ok, f"step {step}: {nbad} masses off the oracle, worst |d| {worst:.3g}"
+        slot_of, page_of = pool.read()
+        cur = []
+        for r in range(srows):
+            sel = ids[r, : n[r]].tolist()
+            cur.append(set(sel))
+            # the device's pick equals the reference picker on the device's own masses
+            rc, want_dev = O.pick_scored(P, list(range(P)), got[r].astype(np.float64), w.keep, w.budget,
+                                         use_ref=True)
+            assert rc == 0 and sel == want_dev.tolist(), f"step {step} row {r}: pick on device masses"
+            # ... and on the oracle's masses wherever the k-th boundary gap exceeds 1e-3
+            total += 1
+            if step != 1 and must_check:
+                assert _gap_ok(exp[r], w.keep, w.top_k), f"step {step} row {r}: needle boundary gap below {GAP}"
+            if _gap_ok(exp[r], w.keep, w.top_k):
+                checked += 1
+                rc, want = O.pick_scored(P, list(range(P)), exp[r], w.keep, w.budget, use_ref=True)
+                assert rc == 0 and sel == want.tolist(), f"step {step} row {r}: page set differs from reference"
+            # residency equals the selection; resident slots hold their host records byte for byte
+            assert sorted(np.nonzero(slot_of[r] >= 0)[0].tolist()) == sel
+            ck = cache_k.view(srows, slots, page_k)[r].cpu().numpy()
+            cv = cache_v.view(srows, slots, page_v)[r].cpu().numpy()
+            for p in sel:
+                s = int(slot_of[r, p])
+                assert page_of[r, s] == p
+                assert np.array_equal(ck[s], hk[r, p]), f"step {step} row {r} page {p}: K bytes differ"
+                assert np.array_equal(cv[s], hv[r, p]), f"step {step} row {r} page {p}: V bytes differ"
+        if prev is not None:
+            restored += sum(len(c - p) for c, p in zip(cur, prev))
+        prev = cur
+    ctx.check_status("recall steps")
+    pool.close()
+    print(f"{cfg} top-{w.top_k}: {checked} of {total} selections compared under the gap rule")
+    assert restored > 0, "the query changes restored no page after the first step"

@@ -1,5 +1,5 @@
-"""CPU: every Python file of the repository byte-compiles (scripts run under
-torchrun or gpurun are not imported by the other tests)."""
+"""CPU: every Python file of the repository byte-compiles (scripts that only run
+under torchrun or on a GPU are not imported by the other tests)."""
 import os
 import py_compile
 
