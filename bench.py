@@ -4,16 +4,23 @@ Default workload: config 2 of the reference's headline (a 128K-token fp16
 history, 64 layers, 24/4 heads, head_dim 256, pages of 256 tokens, top-32 plus
 first/last page, stage-in of the selected pages' K and V from pinned host
 memory into a device paged cache). One step = one decode step's recall over
-all 64 layers, steady state: queries drift per step (seeded) and only pages
-not already resident are staged. Prints one JSON line (rank 0).
+all 64 layers, steady state: each step's query favours the next group of
+rotating needle pages, so 3 of each layer's 32 pages turn over per step and
+are staged (kvmem_b200.synth). Prints one JSON line (rank 0).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3|c4|c5] [--impl ours|reference]
 
-Config 4 (multi-lane query replay) times selection only on the tcgen05
-scorer; config 5 shards one 1M-token history by page range over the ranks.
-
-Multi-GPU (torchrun): every rank runs an independent decode lane (replica) of
-the workload; value = all ranks' token-layers / max-over-ranks time.
+N = 1: the fused step kvm_recall_step (layer chunks; the stage-in of chunk i on
+a side stream overlaps the scoring of chunk i + 1).
+N > 1 (torchrun, one rank per GPU): the same history partitioned by page range
+over the ranks (strong scaling, kvmem_b200.shard.ShardedRecall): local scoring,
+two NCCL all-gathers of small tensors per layer chunk, a replicated residency
+plan, and each rank's restored pages written from its own pinned records into
+the decode GPU's (rank 0's) cache over NVLink; value = token-layers of the
+whole history / max-over-ranks time.
+Both also report config 5 (a 1M-token q8_0 history, sharded selection) under
+"c5_sharded". Config 4 (multi-lane query replay) times selection only on the
+tcgen05 scorer.
 """
 from __future__ import annotations
 
@@ -49,8 +56,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--chunks", type=int, default=4)
-    ap.add_argument("--stage-ctas", type=int, default=32)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--stage-ctas", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU baseline and the reference GPU timings")
+    ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sharded-selection key")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the page scorer (no host history, no stage-in); for ncu captures")
@@ -165,135 +174,44 @@ def barrier(world):
 
 # --------------------------------------------------------------------------- data
 
-def _mem_available_bytes() -> int:
-    with open("/proc/meminfo") as f:
-        for line in f:
-            if line.startswith("MemAvailable:"):
-                return int(line.split()[1]) * 1024
-    return 0
+# --------------------------------------------------------------------------- data
 
+def build_history(w, seed, device, need_host=True, page_range=None):
+    """K score mirror on the device and (need_host) pinned host K / V page records.
 
-def _clear_cuda_error() -> None:
-    """Reads and clears the CUDA runtime's last-error state (the library torch loaded)."""
-    try:
-        C.CDLL("libcudart.so.12").cudaGetLastError()
-    except OSError:
-        pass
-
-
-class HostStore:
-    """Pinned, device-mapped host memory for the K / V page records.
-
-    One process: torch pinned memory. Several ranks on one node (replicas of the same
-    history): one anonymous shared-memory file (memfd) per node, created by local rank 0,
-    opened by the other ranks through /proc/<pid>/fd, filled by local rank 0 and
-    registered as mapped pinned memory by every rank, so the node holds one copy of the
-    records instead of one per rank (a config-2 history is 34 GB of K and V records;
-    eight private copies would not fit a 251 GB host). A memfd is not bounded by the
-    size of /dev/shm, which some containers keep small."""
-
-    def __init__(self, nbytes: int, tag: str, world: int, local: int):
-        import mmap
-
-        import torch
-        self.mm, self.fd, self.registered, self.shared = None, None, False, world > 1
-        if world == 1:
-            self.tensor = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-            return
-        import torch.distributed as dist
-        info = [None]
-        if local == 0:
-            self.fd = os.memfd_create(f"kvm_{tag}", 0)
-            os.ftruncate(self.fd, nbytes)
-            info = [(os.getpid(), self.fd)]
-        dist.broadcast_object_list(info, src=0)
-        if local != 0:
-            pid, fd = info[0]
-            self.fd = os.open(f"/proc/{pid}/fd/{fd}", os.O_RDWR)
-        self.mm = mmap.mmap(self.fd, nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
-        self.tensor = torch.frombuffer(self.mm, dtype=torch.uint8)
-        err = torch.cuda.cudart().cudaHostRegister(self.tensor.data_ptr(), nbytes, 3)  # portable | mapped
-        ok = torch.tensor([int(err) == 0], dtype=torch.int32, device="cuda")
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank takes the same path
-        if int(err) == 0:
-            self.registered = True
-        else:
-            _clear_cuda_error()  # a refused registration must not surface at the next launch check
-        barrier(world)  # every rank has opened the file before rank 0 may drop its descriptor
-        if not int(ok.item()):
-            # Shared registration refused on some rank: private pinned records per rank,
-            # only when all of them fit well inside the host's available memory.
-            self.close(world)
-            avail = [_mem_available_bytes()] if local == 0 else [0]
-            dist.broadcast_object_list(avail, src=0)
-            if world * nbytes > 0.35 * avail[0]:
-                raise RuntimeError(f"cudaHostRegister of the shared page records failed (here: {int(err)}) and "
-                                   f"{world} private copies of {nbytes / 1e9:.1f} GB do not fit the host")
-            self.shared = False
-            self.tensor = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
-
-    def close(self, world: int):
-        import torch
-        if self.mm is None:
-            return
-        if self.registered:
-            torch.cuda.cudart().cudaHostUnregister(self.tensor.data_ptr())
-            self.registered = False
-        del self.tensor
-        barrier(world)
-        try:
-            self.mm.close()
-        except BufferError:
-            pass  # views of the records are still alive; the mapping goes at exit
-        os.close(self.fd)
-        self.mm = None
-
-
-def build_history(w, seed, device, need_host=True, world=1, local=0):
-    """K score mirror on the device, pinned host K/V pages, device paged cache.
-
-    With world > 1 every rank builds the same history (same seed) and the host page
-    records are one node-shared store written by local rank 0 (private per rank only
-    when the shared store cannot be registered)."""
+    page_range = (p0, p1): only that range of every layer (a rank of a page-range
+    partition), as [L][p1 - p0 pages] on the device and in the records."""
     import torch
     from kvmem_b200 import row_bytes, synth
     rbk = row_bytes(w.k_type, w.head_dim)
     rbv = row_bytes(w.v_type, w.head_dim)
-    T = w.pages * w.page_tokens
-    layer_k = T * w.kv_heads * rbk
-    layer_v = T * w.kv_heads * rbv
-    q_base, drift = synth.make_queries(w, seed, device, drift_steps=8)
+    p0, p1 = page_range or (0, w.pages)
+    page_k = w.page_tokens * w.kv_heads * rbk
+    page_v = w.page_tokens * w.kv_heads * rbv
+    layer_k, layer_v = (p1 - p0) * page_k, (p1 - p0) * page_v
+    q_base, drift = synth.make_queries(w, seed, device, drift_steps=max(8, 2 * w.rot_groups))
     k_dev = torch.empty(w.layers * layer_k, dtype=torch.uint8, device=device)
     host_k = host_v = None
-    stores = []
-    write_k = write_v = False
     if need_host:
-        sk, sv = HostStore(w.layers * layer_k, "k", world, local), HostStore(w.layers * layer_v, "v", world, local)
-        stores = [sk, sv]
-        host_k, host_v = sk.tensor, sv.tensor
-        # A shared store is written once per node, a private one by its rank.
-        write_k, write_v = local == 0 or not sk.shared, local == 0 or not sv.shared
+        host_k = torch.empty(w.layers * layer_k, dtype=torch.uint8, pin_memory=True)
+        host_v = torch.empty(w.layers * layer_v, dtype=torch.uint8, pin_memory=True)
     for l in range(w.layers):
         if w.k_type == 1:
             kl = synth.fp16_layer(w, seed, l, q_base, device).view(torch.uint8).reshape(-1)
         else:
             kl = synth.q8_0_layer(w, seed, l, q_base, device).reshape(-1)
+        kl = kl[p0 * page_k:p1 * page_k]
         k_dev[l * layer_k:(l + 1) * layer_k].copy_(kl)
-        if write_k:
+        if need_host:
             host_k[l * layer_k:(l + 1) * layer_k].copy_(kl)
-        if write_v:
             vl = (synth.fp16_v_layer(w, seed, l, device).view(torch.uint8).reshape(-1) if w.v_type == 1
                   else synth.q4_0_v_layer(w, seed, l, device).reshape(-1))
-            host_v[l * layer_v:(l + 1) * layer_v].copy_(vl)
+            host_v[l * layer_v:(l + 1) * layer_v].copy_(vl[p0 * page_v:p1 * page_v])
         del kl
     torch.cuda.synchronize()
-    if need_host and world > 1:
-        barrier(world)  # the records are written before any rank stages from them
     return dict(q_base=q_base, drift=drift, k_dev=k_dev, host_k=host_k, host_v=host_v, layer_k=layer_k,
-                layer_v=layer_v, rbk=rbk, rbv=rbv, stores=stores)
+                layer_v=layer_v, rbk=rbk, rbv=rbv, page_k=page_k, page_v=page_v, page0=p0, local_pages=p1 - p0)
 
-
-# --------------------------------------------------------------------------- our arm
 
 def workload(args):
     import dataclasses
@@ -303,6 +221,650 @@ def workload(args):
         w = dataclasses.replace(w, layers=args.layers)
     return w
 
+
+def cpu_info():
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return model, os.cpu_count() or 1
+
+
+def traffic_of(config):
+    """DRAM bytes per scorer launch from the committed ncu summary, with its source."""
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(tp) as f:
+            t = json.load(f)
+        return t.get(f"page_lse_{config}"), "profiles/traffic.json: " + str(t.get("note"))
+    except Exception:
+        return None, None
+
+
+def step_stats(w, ctx, desc, kc, qdescs, start, count, mass, sel_ids, sel_n, chunks):
+    """Pages restored per step under the step-to-step query change: selection-only replays of
+    `count` consecutive steps (the pool holds exactly the previous step's selection, so the
+    restores of a step are its selected pages not selected the step before)."""
+    import numpy as np
+    restored, prev = [], None
+    srows = w.layers * w.groups
+    for i in range(start, start + count + 1):
+        ctx.recall_step(desc, qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
+                        sel_n=sel_n, chunks=chunks)
+        ids, n = sel_ids.cpu().numpy(), sel_n.cpu().numpy()
+        cur = [set(ids[r, : n[r]].tolist()) for r in range(srows)]
+        if prev is not None:
+            restored.append(sum(len(c - p) for c, p in zip(cur, prev)))
+        prev = cur
+    return float(np.mean(restored)) if restored else 0.0
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    import kvmem_b200 as K
+    w = workload(args)
+    if args.kernel_only:
+        return run_kernel_only(args, w, local)
+    if args.config == "c4":
+        return run_replay(args, w, world, rank, local)
+    if args.config == "c5":
+        line = sharded_selection(args, w, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        return run_sharded_recall(args, w, world, rank, local)
+    assert w.groups == 1, "stage-in geometry of this bench is per-layer selection"
+    dev = torch.device("cuda", local)
+    h = build_history(w, args.seed, dev)
+    ctx = K.RecallContext(local)
+    P, L = w.pages, w.layers
+    srows = L * w.groups
+    page_k, page_v = h["page_k"], h["page_v"]
+    slots = w.budget
+    cache_k = torch.zeros(srows * slots * page_k, dtype=torch.uint8, device=dev)
+    cache_v = torch.zeros(srows * slots * page_v, dtype=torch.uint8, device=dev)
+    layout = K.stage_layout([
+        dict(host_base=h["host_k"].data_ptr(), host_row_stride=h["layer_k"], host_page_stride=page_k,
+             dev_base=cache_k.data_ptr(), dev_row_stride=slots * page_k, dev_slot_stride=page_k, bytes=page_k),
+        dict(host_base=h["host_v"].data_ptr(), host_row_stride=h["layer_v"], host_page_stride=page_v,
+             dev_base=cache_v.data_ptr(), dev_row_stride=slots * page_v, dev_slot_stride=page_v, bytes=page_v)])
+    pool = K.ResidencyPool(ctx, srows, P, slots)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=P * w.page_tokens)
+    qs = h["drift"]  # the query of step s: the rotating needle group s mod rot_groups is favoured
+    qdescs = [K.RecallContext.make_query(q, w.rows) for q in qs]
+    mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
+    sel_ids = torch.empty((srows, w.budget), dtype=torch.int32, device=dev)
+    sel_n = torch.empty((srows,), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i, force=False, with_pool=True, qd=None):
+        ctx.recall_step(desc, qd or qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
+                        sel_n=sel_n, pool=pool if with_pool else None, layout=layout if with_pool else None,
+                        chunks=args.chunks, stage_ctas=args.stage_ctas, force_reload=force)
+
+    def timed(n, fn):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(n):
+            fn(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / n
+
+    # Warm-up, then the timed steady state: every step restores the pages of the next
+    # rotating needle group and evicts the previous group's.
+    for i in range(args.warmup):
+        step(i)
+    ctx.wait(120.0)
+    a0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    launches = ctx.launches - a0
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+    ctx.check_status("timed steps")
+    # The last plan's restores, gathered again alone: the stage-in half of a steady step.
+    pool.stage_in(layout, ctas=args.stage_ctas)
+    gather_steady_ms = timed(5, lambda i: pool.stage_in(layout, ctas=args.stage_ctas))
+    start = args.warmup + args.steps
+
+    # End to end through the C ABI with host buffers: H2D of the step's queries, the step
+    # (with its stage-in), D2H of the selection.
+    q_host = [q.cpu().pin_memory() for q in qs]
+    q_dev = torch.empty_like(qs[0])
+    qd_e2e = K.RecallContext.make_query(q_dev, w.rows)
+    ids_host = torch.empty(sel_ids.shape, dtype=torch.int32, pin_memory=True)
+    n_host = torch.empty(sel_n.shape, dtype=torch.int32, pin_memory=True)
+    h2d = q_host[0].numel() * 4
+    d2h = ids_host.numel() * 4 + n_host.numel() * 4
+
+    def e2e_step(i):
+        j = start + i
+        q_dev.copy_(q_host[j % len(q_host)], non_blocking=True)
+        step(j, qd=qd_e2e)
+        ids_host.copy_(sel_ids, non_blocking=True)
+        n_host.copy_(sel_n, non_blocking=True)
+
+    e2e_step(0)
+    start += 1
+    e2e_ms = timed(args.steps, e2e_step)
+    start += args.steps
+    ctx.check_status("e2e steps")
+
+    # Selection alone (score -> top-k, no residency plan or stage-in) on the same queries.
+    select_ms = timed(args.steps, lambda i: step(start + i, with_pool=False))
+    restored = step_stats(w, ctx, desc, kc, qdescs, start, min(args.steps, 8), mass, sel_ids, sel_n, args.chunks)
+
+    # Cold worst case: every selected page staged every step.
+    n_cold = max(3, min(10, args.steps))
+    step(0, force=True)
+    ms_cold = timed(n_cold, lambda i: step(i, force=True))
+    cold_bytes = srows * w.budget * (page_k + page_v)
+
+    # Stage-in alone (the gather of a full cold plan) -> link GB/s.
+    g_ms = []
+    for _ in range(3):
+        pool.plan(sel_ids, sel_n, force_reload=True)
+        g_ms.append(timed(1, lambda i: pool.stage_in(layout, ctas=args.stage_ctas)))
+    gather_ms = statistics.median(g_ms)
+    ref_route_ms = reference_stagein_route(w, h, pool, cache_k, cache_v, slots, dev)
+    stageout_ms, out_bytes = stageout_harvest(args, w, cache_k, cache_v, slots, page_k, page_v, local)
+
+    # Dominant kernel alone: the page log-sum-exp pass over all layers (+ its tiny normaliser).
+    kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
+    for _ in range(2):
+        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
+    kernel_ms = timed(10, lambda i: ctx.score_pages(desc, qdescs[0], kc, want_rows=False,
+                                                    out_mean=mass.view(L, w.groups, P)))
+    hbm_peak, peak_src = peaks()
+    achieved = kbytes / (kernel_ms * 1e-3) / 1e9
+    traffic, traffic_src = traffic_of(args.config)
+
+    token_layers = L * w.tokens
+    cpu = None if args.no_cpu_baseline else cpu_baseline_port(w, h)
+    ref_gpu = None if args.no_cpu_baseline else reference_gpu_timings(w, h, qs[0], dev)
+    pool.close()
+    ctx.close()
+    del cache_k, cache_v, h
+    torch.cuda.empty_cache()
+    c5 = None if args.no_c5 else sharded_selection(args, workload_named("c5"), world, rank, local)
+    line = {
+        "metric": METRIC, "value": token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16" if w.k_type == 1 else "q8_0",
+        "data": "synthetic: seeded on-device N(0,1) K/V with per-channel scale U(0.5,2), planted fixed and "
+                "rotating needle pages",
+        "config": {"workload": w.name, "layers": L, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
+                   "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": w.page_tokens, "pages": P,
+                   "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
+                   "parallelism": "single GPU", "chunks": args.chunks,
+                   "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
+                   "step": "score all pages -> top-k -> residency plan -> stage-in of non-resident pages (K+V) "
+                           f"from pinned host; the query of each step favours the next rotating needle group, "
+                           f"so {w.rotating} of each layer's {w.top_k} pages turn over per step"},
+        "restored_pages_per_step": restored,
+        "stage_bytes_per_step": restored * (page_k + page_v),
+        "select_ms": select_ms, "gather_steady_ms": gather_steady_ms,
+        "clocks": clk.summary(),
+        "e2e": {"value": token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm",
+                     "kernel": ("page_lse_mma_kernel" if w.k_type == 1 else "page_lse_q_kernel")
+                               + " (+page_mass_normalize_kernel)",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "peak_source": peak_src, "traffic": traffic, "traffic_source": traffic_src,
+                     "kernel_ms": kernel_ms, "algorithmic_bytes": kbytes},
+        "cold": {"ms_per_step": ms_cold, "stage_bytes_per_step": cold_bytes,
+                 "note": "every selected page staged every step (force_reload)"},
+        "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
+                    "ctas": args.stage_ctas, "link": "PCIe Gen5 x16 (mapped pinned host reads)"},
+        "stagein_reference_route": {"ms": ref_route_ms, "bytes": cold_bytes,
+                                    "GB/s": cold_bytes / (ref_route_ms * 1e-3) / 1e9,
+                                    "route": "two host memcpys per record (store -> vector -> 32 MiB pinned slab), "
+                                             "one H2D per slab, one D2D per item (the reference's slab "
+                                             "route, restated; host clock)"},
+        "stageout": {"ms": stageout_ms, "bytes": out_bytes, "GB/s": out_bytes / (stageout_ms * 1e-3) / 1e9,
+                     "what": "K+V of one block per layer into two 32 MiB pinned slots in turn (host clock, "
+                             "submit to last slot observed)", "ctas": args.stage_ctas},
+        "cpu_baseline": cpu,
+        "reference_gpu": ref_gpu,
+        "c5_sharded": c5,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_named(name):
+    from kvmem_b200 import synth
+    return synth.CONFIGS[name]
+
+
+def reference_stagein_route(w, h, pool, cache_k, cache_v, slots, dev):
+    """The reference's stage-in route for the current plan's cold set, restated: each page record
+    is copied out of the store into a host vector (src/adapter/llama-memory-kvmem.cpp:4501-4502),
+    then into a 32 MiB pinned slab; a full slab goes to a device staging buffer with one H2D copy
+    and an event wait, then one D2D copy per item into its cache slot
+    (src/adapter/llama-kvmem-stagein.cu:673-794). Python drives the item loop. Host ms."""
+    import numpy as np
+    import torch
+    page_k, page_v = h["page_k"], h["page_v"]
+    slot_of, _ = pool.read()
+    slab_bytes = 32 << 20
+    slab = torch.empty(slab_bytes, dtype=torch.uint8, pin_memory=True)
+    slab_np = slab.numpy()
+    dev_q = torch.empty(slab_bytes, dtype=torch.uint8, device=dev)
+    items = []
+    hk, hv = h["host_k"].numpy(), h["host_v"].numpy()
+    for r in range(slot_of.shape[0]):
+        for p in np.nonzero(slot_of[r] >= 0)[0]:
+            s_ = int(slot_of[r, p])
+            items.append((hk, r * h["layer_k"] + int(p) * page_k, cache_k, (r * slots + s_) * page_k, page_k))
+            items.append((hv, r * h["layer_v"] + int(p) * page_v, cache_v, (r * slots + s_) * page_v, page_v))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    used, pending = 0, []
+
+    def flush():
+        dev_q[:used].copy_(slab[:used], non_blocking=True)
+        torch.cuda.synchronize()  # the slab is reused by the next batch
+        for dst, doff, off, n in pending:
+            dst[doff:doff + n].copy_(dev_q[off:off + n], non_blocking=True)
+
+    for src, soff, dst, doff, n in items:
+        if used + n > slab_bytes:
+            flush()
+            used, pending = 0, []
+        slab_np[used:used + n] = src[soff:soff + n].copy()
+        pending.append((dst, doff, used, n))
+        used += n
+    if pending:
+        flush()
+    torch.cuda.synchronize()
+    return (time.perf_counter() - t0) * 1e3
+
+
+def stageout_harvest(args, w, cache_k, cache_v, slots, page_k, page_v, local):
+    """Stage-out (harvest) of one filled block per layer: its K and V bytes from the device cache
+    into the two 32 MiB pinned slots in turn -> (host ms, bytes)."""
+    import torch
+    import kvmem_b200 as K
+    so = K.StageOut(local)
+    L = w.layers
+
+    def harvest():
+        pending = -1
+        for l in range(L):
+            for cache, pb in ((cache_k, page_k), (cache_v, page_v)):
+                src = cache.data_ptr() + l * slots * pb
+                if so.enqueue(src, pb) is None:
+                    slot = so.submit(ctas=args.stage_ctas)
+                    so.wait(pending)
+                    pending = slot
+                    so.enqueue(src, pb)
+        slot = so.submit(ctas=args.stage_ctas)
+        so.wait(pending)
+        so.wait(slot)
+
+    harvest()
+    o_ms = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        harvest()
+        o_ms.append((time.perf_counter() - t0) * 1e3)
+    so.close()
+    return statistics.median(o_ms), L * (page_k + page_v)
+
+
+def sharded_selection(args, w, world, rank, local):
+    """Config 5: one 1M-token q8_0 history partitioned by page range over the ranks (strong
+    scaling). A step = sharded selection on every rank: local page LSE, all-gather of softmax
+    statistics, local masses, local candidates, all-gather, global top-k. No stage-in (its
+    host records would be 111 GB of pinned K and V). Returns the line as a dict (rank 0)."""
+    import torch
+    import kvmem_b200 as K
+    from kvmem_b200.shard import ShardCompute, ShardedSelector, ShardGeometry, page_ranges
+    dev = torch.device("cuda", local)
+    P, L, B = w.pages, w.layers, w.page_tokens
+    p0, p1 = page_ranges(P, world)[rank]
+    lp = p1 - p0
+    h = build_history(w, args.seed, dev, need_host=False, page_range=(p0, p1))
+    page_bytes = h["page_k"]
+    ctx = K.RecallContext(local)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=B, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=lp * B)
+    qds = [K.RecallContext.make_query(q, w.rows) for q in h["drift"]]
+    geo = ShardGeometry(layers=L, rows=w.rows, q_heads=w.q_heads, kv_heads=w.kv_heads, groups=w.groups,
+                        total_pages=P, page0=p0, local_pages=lp)
+    sel = ShardedSelector(ShardCompute(ctx))
+    warm = max(3, min(args.warmup, 5))
+    steps = max(5, min(args.steps, 10))
+    for i in range(warm):
+        sel.select(desc, qds[i % len(qds)], kc, geo, w.keep, w.budget)
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0 = ctx.launches
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for i in range(steps):
+            sel.select(desc, qds[(warm + i) % len(qds)], kc, geo, w.keep, w.budget)
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / steps, world)
+    launches = ctx.launches - a0
+    ctx.check_status("sharded steps")
+    # The local scorer alone (this rank's pages), for the roofline.
+    ldesc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                      tokens=lp * B, page_tokens=B)
+    ctx.score_pages(ldesc, qds[0], kc, want_rows=False)
+    torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(5):
+        ctx.score_pages(ldesc, qds[0], kc, want_rows=False)
+    ev1.record()
+    torch.cuda.synchronize()
+    kernel_ms = max_over_ranks(ev0.elapsed_time(ev1) / 5, world)
+    kbytes_local = L * lp * page_bytes
+    hbm_peak, src = peaks()
+    ctx.close()
+    del h
+    torch.cuda.empty_cache()
+    return {
+        "metric": METRIC, "value": L * w.tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q8_0" if w.k_type == 3 else "f16",
+        "data": "synthetic: seeded on-device q8_0 K (codes round(N(0,1)*40), scales U(0.005,0.03)), "
+                "fixed and rotating needle pages",
+        "config": {"workload": w.name, "layers": L, "tokens": w.tokens, "pages": P, "top_k": w.top_k,
+                   "parallelism": f"page-range shards x{world}", "pages_per_rank": lp,
+                   "step": "sharded selection (two NCCL all-gathers); stage-in not included",
+                   "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)"},
+        "clocks": clk.summary(), "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "page_lse_q_kernel (local pages)", "kernel_ms": kernel_ms,
+                     "achieved": kbytes_local / (kernel_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": kbytes_local / (kernel_ms * 1e-3) / 1e9 / hbm_peak, "peak_source": src,
+                     "algorithmic_bytes": kbytes_local,
+                     "step_GBps_all_ranks": L * P * page_bytes / (ms * 1e-3) / 1e9},
+    }
+
+
+def run_sharded_recall(args, w, world, rank, local):
+    """N > 1: one history partitioned by page range over the ranks (strong scaling), the whole
+    decode-step recall on every rank (kvmem_b200.shard.ShardedRecall): local page LSE, two NCCL
+    all-gathers of small tensors per layer chunk, the replicated residency plan, and the stage-in
+    of each rank's restored pages from its own pinned records (its own PCIe link) into the decode
+    GPU's (rank 0's) paged cache through a CUDA-IPC peer mapping (NVLink); a one-element
+    all-reduce ends the step. value = token-layers of the whole history / max-over-ranks ms."""
+    import torch
+    import torch.distributed as dist
+    import kvmem_b200 as K
+    from kvmem_b200.shard import ShardCompute, ShardedRecall, ShardedSelector, ShardGeometry, page_ranges
+    assert w.groups == 1, "stage-in geometry of this bench is per-layer selection"
+    dev = torch.device("cuda", local)
+    P, L, B = w.pages, w.layers, w.page_tokens
+    p0, p1 = page_ranges(P, world)[rank]
+    lp = p1 - p0
+    h = build_history(w, args.seed, dev, page_range=(p0, p1))
+    page_k, page_v = h["page_k"], h["page_v"]
+    slots = w.budget
+    # The decode GPU (rank 0) owns the paged cache of every layer; the others map it.
+    if rank == 0:
+        cache_k = torch.zeros(L * slots * page_k, dtype=torch.uint8, device=dev)
+        cache_v = torch.zeros(L * slots * page_v, dtype=torch.uint8, device=dev)
+        handles = [K.ipc_export(cache_k), K.ipc_export(cache_v)]
+    else:
+        handles = None
+    box = [handles]
+    dist.broadcast_object_list(box, src=0)
+    if rank == 0:
+        ck, cv = cache_k.data_ptr(), cache_v.data_ptr()
+    else:
+        ck, cv = K.ipc_open(local, box[0][0]), K.ipc_open(local, box[0][1])
+    ctx = K.RecallContext(local)
+    chunks = max(1, min(args.chunks, L))
+    per = -(-L // chunks)
+    chunk_layers = [(l0, min(per, L - l0)) for l0 in range(0, L, per)]
+    pools, layouts = [], []
+    for l0, nl in chunk_layers:
+        pools.append(K.ResidencyPool(ctx, nl, P, slots))
+        layouts.append(K.stage_layout([
+            dict(host_base=h["host_k"].data_ptr() + l0 * h["layer_k"], host_row_stride=h["layer_k"],
+                 host_page_stride=page_k, dev_base=ck + l0 * slots * page_k, dev_row_stride=slots * page_k,
+                 dev_slot_stride=page_k, bytes=page_k),
+            dict(host_base=h["host_v"].data_ptr() + l0 * h["layer_v"], host_row_stride=h["layer_v"],
+                 host_page_stride=page_v, dev_base=cv + l0 * slots * page_v, dev_row_stride=slots * page_v,
+                 dev_slot_stride=page_v, bytes=page_v)]))
+    geo = ShardGeometry(layers=L, rows=w.rows, q_heads=w.q_heads, kv_heads=w.kv_heads, groups=w.groups,
+                        total_pages=P, page0=p0, local_pages=lp)
+    rec = ShardedRecall(ShardedSelector(ShardCompute(ctx)), pools, layouts, chunk_layers, geo,
+                        stage_ctas=args.stage_ctas)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     tokens=w.tokens, page_tokens=B, groups=w.groups)
+    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                     capacity_tokens=lp * B)
+    qs = h["drift"]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        rec.step(desc, qs[i % len(qs)], kc, w.keep, w.budget)
+    torch.cuda.synchronize()
+    barrier(world)
+    a0 = ctx.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
+        ev0.record(stream)
+        for i in range(args.steps):
+            rec.step(desc, qs[(args.warmup + i) % len(qs)], kc, w.keep, w.budget)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    launches = ctx.launches - a0
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    ctx.check_status("sharded recall steps")
+    start = args.warmup + args.steps
+
+    # Pages restored per step (every rank holds the same selection): selection differences.
+    import numpy as np
+    restored, prev = [], None
+    for i in range(start, start + min(args.steps, 8) + 1):
+        ids, n = rec.step(desc, qs[i % len(qs)], kc, w.keep, w.budget)
+        ih, nh = ids.cpu().numpy(), n.cpu().numpy()
+        cur = [set(ih[r, : nh[r]].tolist()) for r in range(L)]
+        if prev is not None:
+            restored.append(sum(len(c - p) for c, p in zip(cur, prev)))
+        prev = cur
+    start += min(args.steps, 8) + 1
+    restored_per_step = float(np.mean(restored)) if restored else 0.0
+
+    # End to end: every rank copies the step's queries from pinned host memory, rank 0 reads
+    # the selection back.
+    q_host = [q.cpu().pin_memory() for q in qs]
+    q_dev = torch.empty_like(qs[0])
+    ids_host = torch.empty((L, w.budget), dtype=torch.int32, pin_memory=True)
+    n_host = torch.empty((L,), dtype=torch.int32, pin_memory=True)
+
+    def e2e_step(j):
+        q_dev.copy_(q_host[j % len(q_host)], non_blocking=True)
+        ids, n = rec.step(desc, q_dev, kc, w.keep, w.budget)
+        if rank == 0:
+            ids_host.copy_(ids, non_blocking=True)
+            n_host.copy_(n, non_blocking=True)
+
+    e2e_step(start)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0.record(stream)
+    for i in range(args.steps):
+        e2e_step(start + 1 + i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    h2d = world * q_host[0].numel() * 4
+    d2h = ids_host.numel() * 4 + n_host.numel() * 4
+
+    # The local scorer alone (this rank's pages), for the roofline.
+    ldesc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                      tokens=lp * B, page_tokens=B)
+    qd0 = K.RecallContext.make_query(qs[0], w.rows)
+    ctx.score_pages(ldesc, qd0, kc, want_rows=False)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(5):
+        ctx.score_pages(ldesc, qd0, kc, want_rows=False)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = max_over_ranks(ev0.elapsed_time(ev1) / 5, world)
+    kbytes_local = L * lp * page_k
+    hbm_peak, peak_src = peaks()
+    for p in pools:
+        p.close()
+    ctx.close()
+    barrier(world)  # no rank writes the decode cache any more
+    if rank != 0:
+        K.ipc_close(local, ck)
+        K.ipc_close(local, cv)
+    barrier(world)
+    del h
+    torch.cuda.empty_cache()
+    c5 = None if args.no_c5 else sharded_selection(args, workload_named("c5"), world, rank, local)
+    if rank != 0:
+        return
+    token_layers = L * w.tokens
+    print(json.dumps({
+        "metric": METRIC, "value": token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16" if w.k_type == 1 else "q8_0",
+        "data": "synthetic: seeded on-device N(0,1) K/V with per-channel scale U(0.5,2), planted fixed and "
+                "rotating needle pages",
+        "config": {"workload": w.name, "layers": L, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
+                   "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": B, "pages": P,
+                   "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
+                   "parallelism": f"page-range shards x{world}", "pages_per_rank": lp, "chunks": len(chunk_layers),
+                   "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)",
+                   "step": "per layer chunk: local page LSE, NCCL all-gather of softmax statistics, local "
+                           "masses and candidates, NCCL all-gather of candidates, global top-k, replicated "
+                           "residency plan; stage-in of each rank's restored pages (K+V) from its own pinned "
+                           "records into rank 0's paged cache over NVLink (CUDA IPC peer writes); one "
+                           "all-reduce ends the step"},
+        "restored_pages_per_step": restored_per_step,
+        "stage_bytes_per_step": restored_per_step * (page_k + page_v),
+        "clocks": clk.summary(),
+        "e2e": {"value": token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "page_lse_mma_kernel (local pages, +normaliser)",
+                     "kernel_ms": kernel_ms, "achieved": kbytes_local / (kernel_ms * 1e-3) / 1e9,
+                     "peak": hbm_peak, "unit": "GB/s",
+                     "frac": kbytes_local / (kernel_ms * 1e-3) / 1e9 / hbm_peak, "peak_source": peak_src,
+                     "traffic": None, "algorithmic_bytes": kbytes_local,
+                     "step_GBps_all_ranks": L * P * page_k / (ms_step * 1e-3) / 1e9},
+        "c5_sharded": c5,
+    }), flush=True)
+
+
+def cpu_baseline_port(w, h):
+    """The FP64 per-token page mass of the oracle restatement (the reference's dense oracle,
+    src/adapter/llama-kvmem-attention.cpp:61-94) plus the reference's picker, over all host
+    cores: one layer per task (the C calls release the interpreter lock). Bounded sample: the
+    first min(layers, 4 x cores) layers of one step's history (a whole config-2 step on 16+
+    cores); value = token-layers / wall second."""
+    import numpy as np
+    from oracle import oracle as O
+    model, cores = cpu_info()
+    n_layers = min(w.layers, 4 * cores)
+    rb = h["rbk"]
+    T = w.pages * w.page_tokens
+    hk = h["host_k"].numpy()
+    q = h["drift"][0].cpu().numpy().astype(np.float32)
+    use_ref = O.ref() is not None
+
+    def one(l):
+        k0 = hk[l * h["layer_k"]:(l + 1) * h["layer_k"]]
+        m = O.page_mass(q[l:l + 1], O.F32, k0, w.k_type, layers=1, rows=w.rows, heads=w.q_heads,
+                        kv_heads=w.kv_heads, dim=w.head_dim, tokens=w.tokens, page_tokens=w.page_tokens,
+                        scale=1 / np.sqrt(w.head_dim), k_strides=(T * w.kv_heads * rb, w.kv_heads * rb, rb))
+        O.pick_scored(w.pages, list(range(w.pages)), m[0, 0].mean(axis=0), w.keep, w.budget, use_ref=use_ref)
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
+        list(ex.map(one, range(n_layers)))
+    dt = time.perf_counter() - t0
+    return {"value": n_layers * w.tokens / dt, "unit": UNIT, "cores": cores, "cpu_model": model, "kind": "port",
+            "sample": f"{n_layers} of {w.layers} layers x {w.tokens} tokens x {w.q_heads} heads of one step: "
+                      f"FP64 per-token page mass (AttentionSampler::qualify restated) + pick_scored_blocks, "
+                      f"one layer per thread, {dt:.1f} s wall"}
+
+
+def reference_gpu_timings(w, h, q, dev):
+    """The reference's own GPU scorers (oracle/_ref/libkvref_cuda.so, compiled from its sources for
+    sm_100a) on this step's inputs, host-timed per call as the reference runs them (each call
+    synchronises its stream and copies its scores to the host):
+      per_token: llama_kvmem_attention_cuda::score per layer, one decode row, zero mask
+                 (src/adapter/llama-kvmem-attention-cuda.cu:146-193), summed over the layers;
+      meank:     PageSoftmaxCuda::score over the pages' mean keys of the same K, all layers in one
+                 call (kvmem/src/cuda/page_softmax.cu:202-280)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    if O.ref_cuda() is None:
+        return {"unavailable": "oracle/_ref/libkvref_cuda.so was not built (reference sources absent at build)"}
+    L, P, T = w.layers, w.pages, w.pages * w.page_tokens
+    rb = h["rbk"]
+    mask = torch.zeros((1, T), dtype=torch.float32, device=dev)
+    qf = q.contiguous()
+    esz = 4
+
+    def per_token_step():
+        total = 0.0
+        for l in range(L):
+            _, ms = O.ref_attention_score(
+                qf[l].data_ptr(), O.F32, dim=w.head_dim, q_rows=w.rows, heads=w.q_heads,
+                q_row_stride=w.q_heads * w.head_dim * esz, q_head_stride=w.head_dim * esz,
+                k_ptr=h["k_dev"].data_ptr() + l * h["layer_k"], k_type=w.k_type, tokens=w.tokens,
+                kv_heads=w.kv_heads, k_token_stride=w.kv_heads * rb, k_head_stride=rb, mask_ptr=mask.data_ptr(),
+                mask_type=O.F32, mask_row_stride=T * 4, scale=float(1 / np.sqrt(w.head_dim)), softcap=0.0,
+                block=w.page_tokens, rows=list(range(w.rows)))
+            total += ms
+        return total
+
+    per_token_step()
+    pt = [per_token_step() for _ in range(2)]
+    kbytes = L * P * w.page_tokens * w.kv_heads * rb
+    out = {"per_token_ms": min(pt), "per_token_GBps_of_K": kbytes / (min(pt) * 1e-3) / 1e9}
+    if w.k_type == 1:
+        kv = h["k_dev"].view(torch.float16).view(L, P, w.page_tokens, w.kv_heads * w.head_dim)
+        sums = torch.stack([kv[l].float().sum(dim=1) for l in range(L)]).cpu().numpy()
+        counts = np.full(P, w.page_tokens, np.uint32)
+        qn = qf.view(L, w.rows, -1).cpu().numpy()
+        kw = dict(heads=w.q_heads, kv_heads=w.kv_heads, dim=w.head_dim, block=w.page_tokens, accepted=w.tokens,
+                  budget=w.budget, sink=1, recent=1, fixed=w.keep)
+        lr = np.full(L, w.rows, np.uint32)
+        O.ref_page_softmax_cuda(dev.index or 0, sums, counts, qn, lr, **kw)
+        mk = [O.ref_page_softmax_cuda(dev.index or 0, sums, counts, qn, lr, **kw)[1] for _ in range(3)]
+        out["meank_ms"] = min(mk)
+    O.ref_cuda().kvref_cuda_release()
+    out["note"] = ("the reference's kernels compiled from its sources for sm_100a; per-token re-reads K once per "
+                   "query head (no GQA reuse) and synchronises after each layer's call")
+    return out
 
 def run_kernel_only(args, w, local):
     """The page scorer alone over the workload (device-resident K), for profiling."""
@@ -337,88 +899,6 @@ def run_kernel_only(args, w, local):
                       "frac": kbytes / ms / 1e6 / peak, "peak_source": src, "launches": ctx.launches}), flush=True)
     ctx.close()
 
-
-def run_sharded(args, w, world, rank, local):
-    """Config 5: one history partitioned by page range over the ranks (strong scaling).
-    A step = sharded selection (local page LSE, all-gather of softmax statistics,
-    local masses, local candidates, all-gather, global top-k) on every rank."""
-    import torch
-    import kvmem_b200 as K
-    from kvmem_b200 import row_bytes, synth
-    from kvmem_b200.shard import ShardCompute, ShardedSelector, ShardGeometry, page_ranges
-    dev = torch.device("cuda", local)
-    P, L, B = w.pages, w.layers, w.page_tokens
-    p0, p1 = page_ranges(P, world)[rank]
-    lp = p1 - p0
-    rb = row_bytes(w.k_type, w.head_dim)
-    page_bytes = B * w.kv_heads * rb
-    q_base, drift = synth.make_queries(w, args.seed, dev, drift_steps=8)
-    k_local = torch.empty(L * lp * page_bytes, dtype=torch.uint8, device=dev)
-    for l in range(L):
-        kl = (synth.q8_0_layer(w, args.seed, l, q_base, dev) if w.k_type == 3
-              else synth.fp16_layer(w, args.seed, l, q_base, dev).view(torch.uint8)).reshape(-1)
-        k_local[l * lp * page_bytes:(l + 1) * lp * page_bytes].copy_(kl[p0 * page_bytes:p1 * page_bytes])
-        del kl
-    torch.cuda.synchronize()
-    ctx = K.RecallContext(local)
-    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     tokens=w.tokens, page_tokens=B, groups=w.groups)
-    kc = K.RecallContext.make_kcache(k_local, w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     capacity_tokens=lp * B)
-    qds = [K.RecallContext.make_query(q, w.rows) for q in [q_base] + drift]
-    geo = ShardGeometry(layers=L, rows=w.rows, q_heads=w.q_heads, kv_heads=w.kv_heads, groups=w.groups,
-                        total_pages=P, page0=p0, local_pages=lp)
-    sel = ShardedSelector(ShardCompute(ctx))
-    for i in range(args.warmup):
-        ids, n = sel.select(desc, qds[i % len(qds)], kc, geo, w.keep, w.budget)
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0 = ctx.launches
-    with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("timed")
-        ev0.record()
-        for i in range(args.steps):
-            ids, n = sel.select(desc, qds[(args.warmup + i) % len(qds)], kc, geo, w.keep, w.budget)
-        ev1.record()
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-    launches = ctx.launches - a0
-    ctx.check_status("sharded steps")
-    # The local scorer alone (this rank's pages), for the roofline.
-    ctx.score_pages(K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads,
-                                              head_dim=w.head_dim, tokens=lp * B, page_tokens=B),
-                    qds[0], kc, want_rows=False)
-    torch.cuda.synchronize()
-    ev0.record()
-    for _ in range(5):
-        ctx.score_pages(K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads,
-                                                  head_dim=w.head_dim, tokens=lp * B, page_tokens=B),
-                        qds[0], kc, want_rows=False)
-    ev1.record()
-    torch.cuda.synchronize()
-    kernel_ms = max_over_ranks(ev0.elapsed_time(ev1) / 5, world)
-    kbytes_local = L * lp * page_bytes
-    hbm_peak, src = peaks()
-    ctx.close()
-    if rank != 0:
-        return
-    total_bytes = L * P * page_bytes
-    print(json.dumps({
-        "metric": METRIC, "value": L * w.tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "q8_0" if w.k_type == 3 else "f16",
-        "data": "synthetic: seeded on-device q8_0 K (codes round(N(0,1)*40), scales U(0.005,0.03)), needle pages",
-        "config": {"workload": w.name, "layers": L, "tokens": w.tokens, "pages": P, "top_k": w.top_k,
-                   "parallelism": f"page-range shards x{world}", "pages_per_rank": lp,
-                   "step": "sharded selection (two NCCL all-gathers); stage-in not included",
-                   "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)"},
-        "clocks": clk.summary(), "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "page_lse_q_kernel (local pages)", "kernel_ms": kernel_ms,
-                     "achieved": kbytes_local / (kernel_ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": kbytes_local / (kernel_ms * 1e-3) / 1e9 / hbm_peak, "peak_source": src,
-                     "algorithmic_bytes": kbytes_local, "step_GBps_all_ranks": total_bytes / (ms * 1e-3) / 1e9},
-    }), flush=True)
 
 
 def tensor_peak():
@@ -554,295 +1034,6 @@ def run_replay(args, w, world, rank, local):
     }), flush=True)
 
 
-def run_ours(args, world, rank, local):
-    import torch
-    import kvmem_b200 as K
-    w = workload(args)
-    if args.kernel_only:
-        return run_kernel_only(args, w, local)
-    if args.config == "c5":
-        return run_sharded(args, w, world, rank, local)
-    if args.config == "c4":
-        return run_replay(args, w, world, rank, local)
-    dev = torch.device("cuda", local)
-    seed = args.seed  # replicas run the same history (the node shares its host page records)
-    h = build_history(w, seed, dev, world=world, local=local)
-    ctx = K.RecallContext(local)
-    P, L = w.pages, w.layers
-    srows = L * w.groups
-    page_k = w.page_tokens * w.kv_heads * h["rbk"]
-    page_v = w.page_tokens * w.kv_heads * h["rbv"]
-    slots = w.budget
-    cache_k = torch.zeros(srows * slots * page_k // w.groups, dtype=torch.uint8, device=dev)
-    cache_v = torch.zeros(srows * slots * page_v // w.groups, dtype=torch.uint8, device=dev)
-    assert w.groups == 1, "stage-in geometry of this bench is per-layer selection"
-    layout = K.stage_layout([
-        dict(host_base=h["host_k"].data_ptr(), host_row_stride=h["layer_k"], host_page_stride=page_k,
-             dev_base=cache_k.data_ptr(), dev_row_stride=slots * page_k, dev_slot_stride=page_k, bytes=page_k),
-        dict(host_base=h["host_v"].data_ptr(), host_row_stride=h["layer_v"], host_page_stride=page_v,
-             dev_base=cache_v.data_ptr(), dev_row_stride=slots * page_v, dev_slot_stride=page_v, bytes=page_v)])
-    pool = K.ResidencyPool(ctx, srows, P, slots)
-    desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
-    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     capacity_tokens=P * w.page_tokens)
-    qs = [h["q_base"]] + h["drift"]
-    qdescs = [K.RecallContext.make_query(q, w.rows) for q in qs]
-    mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
-    sel_ids = torch.empty((srows, w.budget), dtype=torch.int32, device=dev)
-    sel_n = torch.empty((srows,), dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream()
-
-    def step(i, force=False, with_layout=True, qd=None):
-        ctx.recall_step(desc, qd or qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
-                        sel_n=sel_n, pool=pool, layout=layout if with_layout else None, chunks=args.chunks,
-                        stage_ctas=args.stage_ctas, force_reload=force)
-
-    # Warm-up, then the timed steady state.
-    for i in range(args.warmup):
-        step(i)
-    ctx.wait(120.0)
-    a0 = ctx.launches
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    with ClockSampler(local) as clk:
-        torch.cuda.nvtx.range_push("timed")
-        ev0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    launches = ctx.launches - a0
-    ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-    ctx.check_status("timed steps")
-
-    # End to end through the C ABI with host buffers: H2D of the step's queries,
-    # the step, D2H of the selection; measured right after the device-resident loop,
-    # in the same steady state.
-    q_host = [q.cpu().pin_memory() for q in qs]
-    q_dev = torch.empty_like(qs[0])
-    qd_e2e = K.RecallContext.make_query(q_dev, w.rows)
-    ids_host = torch.empty(sel_ids.shape, dtype=torch.int32, pin_memory=True)
-    n_host = torch.empty(sel_n.shape, dtype=torch.int32, pin_memory=True)
-    h2d = q_host[0].numel() * 4
-    d2h = ids_host.numel() * 4 + n_host.numel() * 4
-    for i in range(2):
-        q_dev.copy_(q_host[i % len(q_host)], non_blocking=True)
-        step(i, qd=qd_e2e)
-        ids_host.copy_(sel_ids, non_blocking=True)
-        n_host.copy_(sel_n, non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    ev0.record(stream)
-    for i in range(args.steps):
-        q_dev.copy_(q_host[i % len(q_host)], non_blocking=True)
-        step(args.warmup + i, qd=qd_e2e)
-        ids_host.copy_(sel_ids, non_blocking=True)
-        n_host.copy_(sel_n, non_blocking=True)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-
-    # Pages restored per steady step (replayed untimed, selection only).
-    restored = []
-    prev = None
-    for i in range(args.warmup, args.warmup + min(args.steps, 8)):
-        ctx.recall_step(desc, qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
-                        sel_n=sel_n, chunks=args.chunks)
-        ids, n = sel_ids.cpu().numpy(), sel_n.cpu().numpy()
-        cur = [set(ids[r, : n[r]].tolist()) for r in range(srows)]
-        if prev is not None:
-            restored.append(sum(len(c - p) for c, p in zip(cur, prev)))
-        prev = cur
-    restored_per_step = float(np.mean(restored)) if restored else 0.0
-
-    # Cold worst case: every selected page staged every step.
-    n_cold = max(3, min(10, args.steps))
-    step(0, force=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    ev0.record(stream)
-    for i in range(n_cold):
-        step(i, force=True)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    ms_cold = max_over_ranks(ev0.elapsed_time(ev1) / n_cold, world)
-    cold_bytes = srows * w.budget * (page_k + page_v)
-
-    # Stage-in alone (the gather of a full cold plan) -> link GB/s.
-    pool.plan(sel_ids, sel_n, force_reload=True)
-    pool.stage_in(layout, ctas=args.stage_ctas)
-    torch.cuda.synchronize()
-    g_ms = []
-    for _ in range(3):
-        pool.plan(sel_ids, sel_n, force_reload=True)
-        ev0.record(stream)
-        pool.stage_in(layout, ctas=args.stage_ctas)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        g_ms.append(ev0.elapsed_time(ev1))
-    gather_ms = statistics.median(g_ms)
-
-    # The reference's stage-in route for the same cold set, restated: each page record is
-    # copied out of the store into a host vector (src/adapter/llama-memory-kvmem.cpp:4501-4502),
-    # then into a 32 MiB pinned slab; a full slab goes to a device staging buffer with one
-    # H2D copy and an event wait, then one D2D copy per item into its cache slot
-    # (src/adapter/llama-kvmem-stagein.cu:673-794). Python drives the item loop.
-    slot_of, _ = pool.read()
-    slab_bytes = 32 << 20
-    slab = torch.empty(slab_bytes, dtype=torch.uint8, pin_memory=True)
-    slab_np = slab.numpy()
-    dev_q = torch.empty(slab_bytes, dtype=torch.uint8, device=dev)
-    items = []
-    hk, hv = h["host_k"].numpy(), h["host_v"].numpy()
-    for r in range(srows):
-        for p in np.nonzero(slot_of[r] >= 0)[0]:
-            s_ = int(slot_of[r, p])
-            items.append((hk, r * h["layer_k"] + int(p) * page_k, cache_k, (r * slots + s_) * page_k, page_k))
-            items.append((hv, r * h["layer_v"] + int(p) * page_v, cache_v, (r * slots + s_) * page_v, page_v))
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    used, pending = 0, []
-
-    def flush():
-        dev_q[:used].copy_(slab[:used], non_blocking=True)
-        torch.cuda.synchronize()  # the slab is reused by the next batch
-        for dst, doff, off, n in pending:
-            dst[doff:doff + n].copy_(dev_q[off:off + n], non_blocking=True)
-
-    for src, soff, dst, doff, n in items:
-        if used + n > slab_bytes:
-            flush()
-            used, pending = 0, []
-        slab_np[used:used + n] = src[soff:soff + n].copy()
-        pending.append((dst, doff, used, n))
-        used += n
-    if pending:
-        flush()
-    torch.cuda.synchronize()
-    ref_route_ms = (time.perf_counter() - t0) * 1e3
-    del slab, dev_q
-
-    # Stage-out (harvest) of one filled block per layer: its K and V bytes from the
-    # device cache into the two 32 MiB pinned slots in turn -> D2H link GB/s.
-    so = K.StageOut(local)
-    out_bytes = L * (page_k + page_v)
-
-    def harvest():
-        pending = -1
-        for l in range(L):
-            for cache, pb in ((cache_k, page_k), (cache_v, page_v)):
-                src = cache.data_ptr() + l * slots * pb
-                if so.enqueue(src, pb) is None:
-                    slot = so.submit(ctas=args.stage_ctas)
-                    so.wait(pending)
-                    pending = slot
-                    so.enqueue(src, pb)
-        slot = so.submit(ctas=args.stage_ctas)
-        so.wait(pending)
-        so.wait(slot)
-
-    harvest()
-    o_ms = []
-    for _ in range(3):
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        harvest()
-        o_ms.append((time.perf_counter() - t0) * 1e3)
-    so.close()
-    stageout_ms = statistics.median(o_ms)
-
-    # Dominant kernel alone: the page log-sum-exp pass over all layers (+ its tiny normaliser).
-    kbytes = L * P * w.page_tokens * w.kv_heads * h["rbk"]
-    for _ in range(2):
-        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
-    torch.cuda.synchronize()
-    n_k = 10
-    ev0.record(stream)
-    for _ in range(n_k):
-        ctx.score_pages(desc, qdescs[0], kc, want_rows=False, out_mean=mass.view(L, w.groups, P))
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    kernel_ms = ev0.elapsed_time(ev1) / n_k
-    hbm_peak, peak_src = peaks()
-    achieved = kbytes / (kernel_ms * 1e-3) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        try:
-            traffic = json.load(open(tp)).get(f"page_lse_{args.config}")
-        except Exception:
-            traffic = None
-
-    token_layers = L * w.tokens
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_port(w, h)
-
-    pool.close()
-    ctx.close()
-    for st in h["stores"]:
-        st.close(world)
-    if rank != 0:
-        return
-    line = {
-        "metric": METRIC, "value": world * token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16" if w.k_type == 1 else "q8_0",
-        "data": "synthetic: seeded on-device N(0,1) K/V with per-channel scale U(0.5,2) and planted needle pages",
-        "config": {"workload": w.name, "layers": L, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
-                   "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": w.page_tokens, "pages": P,
-                   "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
-                   "step": "score all pages -> top-k -> residency plan -> stage-in of non-resident pages "
-                           "(seeded query drift)"},
-        "restored_pages_per_step": restored_per_step,
-        "clocks": clk.summary(),
-        "e2e": {"value": world * token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches,
-        "roofline": {"bound": "hbm",
-                     "kernel": ("page_lse_mma_kernel" if w.k_type == 1 else "page_lse_q_kernel")
-                               + " (+page_mass_normalize_kernel)",
-                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "peak_source": peak_src, "traffic": traffic, "kernel_ms": kernel_ms,
-                     "algorithmic_bytes": kbytes},
-        "cold": {"ms_per_step": ms_cold, "stage_bytes_per_step": cold_bytes,
-                 "note": "every selected page staged every step (force_reload)"},
-        "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
-                    "ctas": args.stage_ctas, "link": "PCIe Gen5 x16 (mapped pinned host reads)"},
-        "stagein_reference_route": {"ms": ref_route_ms, "bytes": cold_bytes,
-                                    "GB/s": cold_bytes / (ref_route_ms * 1e-3) / 1e9,
-                                    "route": "two host memcpys per record (store -> vector -> 32 MiB pinned slab), "
-                                             "one H2D per slab, one D2D per item (the reference's slab "
-                                             "route, restated; host clock)"},
-        "stageout": {"ms": stageout_ms, "bytes": out_bytes, "GB/s": out_bytes / (stageout_ms * 1e-3) / 1e9,
-                     "what": "K+V of one block per layer into two 32 MiB pinned slots in turn (host clock, "
-                             "submit to last slot observed)", "ctas": args.stage_ctas},
-        "cpu_baseline": cpu,
-    }
-    print(json.dumps(line), flush=True)
-
-
-def cpu_baseline_port(w, h):
-    """FP64 per-token page mass of the oracle port (single thread) on a bounded sample."""
-    from oracle import oracle as O
-    tokens = 32768 if w.tokens >= 32768 else w.tokens
-    rb = h["rbk"]
-    k0 = h["host_k"][: tokens * w.kv_heads * rb].numpy()
-    q0 = h["q_base"][0:1].cpu().numpy().astype(np.float32)
-    t0 = time.perf_counter()
-    O.page_mass(q0, O.F32, k0, w.k_type, layers=1, rows=w.rows, heads=w.q_heads, kv_heads=w.kv_heads,
-                dim=w.head_dim, tokens=tokens, page_tokens=w.page_tokens, scale=1 / np.sqrt(w.head_dim),
-                k_strides=(tokens * w.kv_heads * rb, w.kv_heads * rb, rb))
-    dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": f"1 layer x {tokens} tokens x {w.q_heads} heads, FP64 oracle restatement "
-                      f"(AttentionSampler::qualify), {dt:.1f} s"}
-
-
 def cpu_baseline_replay(w, h):
     """FP64 per-token page mass of the oracle port (single thread), config 4 sample."""
     from oracle import oracle as O
@@ -886,7 +1077,7 @@ def run_reference(args, world, rank, local):
             kl = (raw[..., 2:].contiguous().view(torch.int8).float() * d).view(T, w.kv_heads, w.head_dim)
         sums[l] = kl.view(P, w.page_tokens, -1).sum(dim=1).cpu().numpy()
     counts = np.full(P, w.page_tokens, np.uint32)
-    queries = [q.view(L, w.rows, -1).cpu().numpy() for q in [q_base] + drift]
+    queries = [q.view(L, w.rows, -1).cpu().numpy() for q in drift]
     use_ref = O.ref() is not None
     threads = os.cpu_count() or 1
 

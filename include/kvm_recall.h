@@ -488,6 +488,36 @@ int kvm_meank_score(kvm_ctx* ctx, const float* sums, const uint32_t* counts, con
                     uint32_t kv_heads, uint32_t head_dim, uint32_t pages, const uint8_t* score_mask,
                     int aggregation, float scale, float* out, void* stream);
 
+/* -------------------------------------------------- layerwise tile accumulation */
+
+/* The layerwise (current-layer Query) recall scores a prefill's query rows in
+ * tiles against one frozen page frame and sums the tiles' page masses (no mean
+ * over rows): kvmem/src/host/layerwise_selection.cpp (layerwise_tile_scores
+ * :32-75, LayerwiseQuerySelection::accumulate :283-296 and finish :298-309).
+ * The accumulator is device FP64 [pages * (keep_halves ? 2 : 1)], zeroed by the
+ * caller before the first tile.
+ *
+ * kvm_layerwise_accumulate adds one tile: tile is device f32 [pages * halves],
+ * the scorer's masses over the frame (halves = 1) or over its half-page frame
+ * (halves = 2: Mean-K records of half a page; elements 2i, 2i+1 are page i's
+ * halves), e.g. the output of kvm_meank_score for the tile's rows of one layer.
+ * With halves = 2 the halves are summed (left + right, in FP64) unless
+ * keep_halves, which keeps both until kvm_layerwise_finish (keep_halves needs
+ * halves = 2, else KVM_ERR_INVALID_ARGUMENT). score_mask: device u8 [pages].
+ * Checks, all made before anything is added (a failure sets the context status
+ * and leaves accum as it was): halves >= 0 with a finite sum and 0 on pages
+ * outside the score mask (KVM_ERR_INVALID_ARGUMENT, the reference's
+ * std::invalid_argument); every value finite, >= 0, keeping the sum finite and 0
+ * outside the mask (KVM_ERR_INVALID_PLAN, the reference's MemoryError InvalidPlan).
+ *
+ * kvm_layerwise_finish writes scores[i] (device f32 [pages]) = accum[i], or with
+ * keep_halves the larger of page i's halves (layerwise_max_page_scores :24-30),
+ * ready for kvm_select_topk. */
+int kvm_layerwise_accumulate(kvm_ctx* ctx, const float* tile, uint32_t pages, uint32_t halves, int keep_halves,
+                             const uint8_t* score_mask, double* accum, void* stream);
+int kvm_layerwise_finish(kvm_ctx* ctx, const double* accum, uint32_t pages, int keep_halves, float* scores,
+                         void* stream);
+
 /* ------------------------------------------------------------ fused step */
 
 /* One decode-step recall: score -> per-row top-k -> residency plan -> stage-in,
@@ -507,7 +537,7 @@ typedef struct kvm_step_desc {
     uint32_t nkeep;
     uint32_t budget;
     uint32_t chunks;     /* layer chunks (0 = 4) */
-    uint32_t stage_ctas; /* CTAs of each gather launch (0 = 32) */
+    uint32_t stage_ctas; /* CTAs (128 threads each) of each gather launch (0 = 64) */
     int force_reload;    /* stage every selected page (cold worst case) */
     int reserved;
 } kvm_step_desc;
@@ -550,6 +580,33 @@ int kvm_shard_candidates(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint
 int kvm_shard_merge(kvm_ctx* ctx, const float* cand_scores, const uint32_t* cand_ids, uint32_t ranks, uint32_t nrows,
                     uint32_t k, const uint32_t* keep, uint32_t nkeep, uint32_t budget, uint32_t* out_ids,
                     uint32_t* out_n, uint32_t out_stride, void* stream);
+
+/* Stage-in of one rank's page range, to the owning decode GPU. The ranks of
+ * a page-range partition keep identical residency tables (each plans the same
+ * merged selection with kvm_plan_residency: the plan is deterministic), and
+ * each rank gathers only the planned restores whose page lies in
+ * [page0, page0 + page_count), from its own range's records over its own PCIe
+ * link: page p of row i is at host_base[j] + i*host_row_stride[j] +
+ * (p - page0)*host_page_stride[j]. dev_base[j] is the decode GPU's cache: on
+ * the decode GPU its own memory, on the other ranks a peer mapping of it
+ * (kvm_ipc_open), written over NVLink. Every writer fences its stores at system
+ * scope before the gather completes, so a collective enqueued after it on
+ * `stream` (on every rank) tells the decode GPU that its cache is complete.
+ * No counterpart in the reference (its stage-in has one GPU,
+ * src/adapter/llama-kvmem-stagein.cu:673-881). Asynchronous on `stream`. */
+int kvm_shard_stagein(kvm_ctx* ctx, kvm_pool* pool, const kvm_stage_layout* layout, uint32_t page0,
+                      uint32_t page_count, uint32_t ctas, void* stream);
+
+/* Device memory shared between the processes of one node (one per GPU):
+ * kvm_ipc_export writes an opaque handle (KVM_IPC_HANDLE_BYTES) naming dev_ptr
+ * (any address inside a device allocation: the handle carries the offset);
+ * kvm_ipc_open maps it in another process for `device`, with peer access
+ * enabled, and returns the same address's mapping; kvm_ipc_close(device, that
+ * pointer) unmaps it. Plain CUDA IPC (no multicast). */
+#define KVM_IPC_HANDLE_BYTES 72
+int kvm_ipc_export(const void* dev_ptr, void* handle);
+int kvm_ipc_open(int device, const void* handle, void** dev_ptr);
+int kvm_ipc_close(int device, void* dev_ptr);
 
 /* Bytes of one D-element row of `type` (0 for an unknown type). */
 uint64_t kvm_row_bytes(int type, uint32_t dim);

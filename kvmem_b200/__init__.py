@@ -10,7 +10,8 @@ host-side binding.
 from . import _abi
 from ._abi import KvmError, F32, F16, BF16, Q8_0, Q4_0, Q5_0
 from .recall import (AttentionCuda, PageSoftmaxCuda, RecallContext, ResidencyPool, StageOut, TensorView, Transfer,
-                     pick_scored_blocks, row_bytes, stage_layout)
+                     ipc_close, ipc_export, ipc_open, pick_scored_blocks, row_bytes, stage_layout)
 
 __all__ = ["KvmError", "F32", "F16", "BF16", "Q8_0", "Q4_0", "Q5_0", "AttentionCuda", "PageSoftmaxCuda",
-           "RecallContext", "ResidencyPool", "StageOut", "TensorView", "Transfer", "pick_scored_blocks", "row_bytes", "stage_layout"]
+           "RecallContext", "ResidencyPool", "StageOut", "TensorView", "Transfer", "ipc_close", "ipc_export",
+           "ipc_open", "pick_scored_blocks", "row_bytes", "stage_layout"]

@@ -38,6 +38,8 @@ STATUS_NAMES = {
 # kvm_type
 F32, F16, BF16, Q8_0, Q4_0, Q5_0 = 0, 1, 2, 3, 4, 5
 
+IPC_HANDLE_BYTES = 72  # KVM_IPC_HANDLE_BYTES
+
 
 class KvmError(RuntimeError):
     """A non-zero kvm_status. ``code`` is the status value."""
@@ -153,6 +155,8 @@ SIGNATURES = {
     "kvm_meank_add": ([_vp, C.POINTER(KCache), _u32, _u32, _u32, _u64, _u32, _u32, _vp, _u32, _vp, _vp], _i),
     "kvm_meank_score": ([_vp, _vp, _vp, _vp, C.POINTER(C.c_uint32), _u32, _u32, _u32, _u32, _u32, _u32,
                          C.POINTER(C.c_uint8), _i, C.c_float, _vp, _vp], _i),
+    "kvm_layerwise_accumulate": ([_vp, _vp, _u32, _u32, _i, _vp, _vp, _vp], _i),
+    "kvm_layerwise_finish": ([_vp, _vp, _u32, _i, _vp, _vp], _i),
     "kvm_recall_step": ([_vp, C.POINTER(StepDesc), _vp, C.POINTER(StageLayout), _vp, _vp, _vp, _vp], _i),
     "kvm_shard_score_partial": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _u32, _u32, _vp,
                                  _vp], _i),
@@ -162,6 +166,10 @@ SIGNATURES = {
                              _i),
     "kvm_shard_merge": ([_vp, _vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _vp, _vp, _u32, _vp],
                         _i),
+    "kvm_shard_stagein": ([_vp, _vp, C.POINTER(StageLayout), _u32, _u32, _u32, _vp], _i),
+    "kvm_ipc_export": ([_vp, _vp], _i),
+    "kvm_ipc_open": ([_i, _vp, C.POINTER(C.c_void_p)], _i),
+    "kvm_ipc_close": ([_i, _vp], _i),
     "kvm_row_bytes": ([_i, _u32], _u64),
     "kvm_ctx_launches": ([_vp], _u64),
 }

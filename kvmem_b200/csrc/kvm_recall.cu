@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "layerwise.cuh"
 #include "lse_launch.cuh"
 #include "page_mass_tc.cuh"
 #include "meank.cuh"
@@ -44,6 +45,9 @@ struct kvm_transfer {
     bool restore_started = false;
     bool drained = true;  // false when an abort could not drain the device work
     cudaEvent_t planned = nullptr, spill_done = nullptr, restore_done = nullptr;
+    // The transfer's own device status word (inside `mem`): its plan reports
+    // there, so unrelated work on the context neither fails nor is hidden by it.
+    kvmb::DeviceStatus* status = nullptr;
 };
 
 namespace {
@@ -75,6 +79,17 @@ struct DeviceGuard {
     } while (0)
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+// Defined with the transfer entry points below (inside their extern "C" block).
+extern "C" {
+namespace {
+int transfer_drain(kvm_transfer* t, uint64_t timeout_us);
+}
+}
+
+namespace {
 
 int ensure_ws(kvm_ctx* c, size_t bytes) {
     if (bytes <= c->ws_bytes) return KVM_OK;
@@ -253,6 +268,8 @@ void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
     const uint32_t kvh = d->kv_heads;
     if (kvh == 0 || 8 % kvh) return;
     const uint64_t rb = row_bytes_of(k->type, d->head_dim);
+    const char* want_hpg = std::getenv("KVM_Q_HPG");  // tuning experiment
+    const char* want_tpc = std::getenv("KVM_Q_TPC");
     uint32_t hpg = 0, pad = 0;
     for (uint32_t h = 1; h <= kvh; h <<= 1) {
         const uint64_t gb = h * rb;
@@ -261,11 +278,12 @@ void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
         if ((gb + pd) / 8 > 255) break;
         hpg = h;
         pad = pd;
-        break;
+        if (!want_hpg || h >= uint32_t(std::atoi(want_hpg))) break;
     }
     if (!hpg) return;
     const uint32_t slot = uint32_t(hpg * rb + pad), groups = kvh / hpg;
-    const uint32_t tpc = 8 * (kLseConsumerWarps / kvh);
+    uint32_t tpc = 8 * (kLseConsumerWarps / kvh);
+    if (want_tpc && std::atoi(want_tpc) > 0 && uint32_t(std::atoi(want_tpc)) % tpc == 0) tpc = uint32_t(std::atoi(want_tpc));
     if (d->page_tokens % tpc || tpc > 256 || groups > uint32_t(kQMaxGroups)) return;
     const uint64_t stage = uint64_t(tpc) * slot;
     const uint32_t stride = uint32_t((stage + 127) / 128 * 128);
@@ -369,6 +387,35 @@ TensorMapEncodeFn tensor_map_encoder() {
             cudaGetLastError();
     });
     return fn;
+}
+
+// cuMemGetAddressRange from the driver: the allocation that holds a device
+// pointer (CUDA IPC handles name whole allocations).
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range_fn() {
+    static AddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddressRangeFn>(ptr);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// Peer mappings opened by kvm_ipc_open: returned pointer -> mapped allocation base.
+std::mutex& ipc_mutex() {
+    static std::mutex m;
+    return m;
+}
+std::unordered_map<void*, void*>& ipc_bases() {
+    static std::unordered_map<void*, void*> m;
+    return m;
 }
 
 // 4-D tensor map of fp16 K of layers [0, nl) from `base`: dims (head_dim,
@@ -634,10 +681,11 @@ int select_rows(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages,
 
 int plan_rows(kvm_ctx* c, kvm_pool* pool, uint32_t row0, uint32_t nrows, const uint32_t* sel_ids,
               const uint32_t* sel_n, uint32_t sel_stride, int force, uint32_t* n_restore, uint32_t* n_evict,
-              cudaStream_t s) {
+              cudaStream_t s, DeviceStatus* status = nullptr) {
     KVM_CUDA(smem_attr(reinterpret_cast<const void*>(plan_residency_kernel), 200 * 1024));
     plan_residency_kernel<<<nrows, kPlanThreads, pool->view.pages, s>>>(pool->view, row0, sel_ids, sel_n, sel_stride,
-                                                                         force, n_restore, n_evict, c->status);
+                                                                         force, n_restore, n_evict,
+                                                                         status ? status : c->status);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
     return KVM_OK;
@@ -664,9 +712,9 @@ int gather_layout(const kvm_stage_layout* L, GatherLayout* g) {
 }
 
 int gather_rows(kvm_ctx* c, kvm_pool* pool, uint32_t row0, uint32_t nrows, const GatherLayout& g, uint32_t ctas,
-                cudaStream_t s) {
-    const uint32_t grid = ctas ? ctas : 32;
-    stagein_gather_kernel<<<grid, kGatherThreads, 0, s>>>(pool->view, row0, nrows, g);
+                cudaStream_t s, uint32_t page0 = 0, uint32_t page_end = 0xffffffffu, int fence_sys = 0) {
+    const uint32_t grid = ctas ? ctas : kGatherDefaultCtas;
+    stagein_gather_kernel<<<grid, kGatherThreads, 0, s>>>(pool->view, row0, nrows, g, page0, page_end, fence_sys);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
     return KVM_OK;
@@ -840,6 +888,11 @@ int kvm_pool_destroy(kvm_pool* p) {
 int kvm_pool_reset(kvm_pool* p, void* stream) {
     if (!p) return KVM_ERR_INVALID_ARGUMENT;
     DeviceGuard guard(p->ctx->device);
+    if (p->pending) {
+        // An aborted transfer that could not drain: wait for its copies first.
+        if (p->pending->phase != kvm_transfer::Aborted) return KVM_ERR_PENDING;
+        KVM_TRY(transfer_drain(p->pending, 30ull * 1000 * 1000));
+    }
     auto s = static_cast<cudaStream_t>(stream);
     const auto& v = p->view;
     KVM_CUDA(cudaMemsetAsync(v.slot_of, 0xff, size_t(v.rows) * v.pages * 4, s));
@@ -882,6 +935,18 @@ void transfer_free(kvm_transfer* t) {
     delete t;
 }
 
+// Waits (bounded) for every step of an aborted transfer that had not drained;
+// once it has, the transfer releases its pool.
+int transfer_drain(kvm_transfer* t, uint64_t timeout_us) {
+    for (cudaEvent_t e : {t->planned, t->spill_done, t->restore_done}) {
+        const int w = event_wait(e, timeout_us);
+        if (w != KVM_OK) return w;
+    }
+    t->drained = true;
+    if (t->pool && t->pool->pending == t) t->pool->pending = nullptr;
+    return KVM_OK;
+}
+
 }  // namespace
 
 int kvm_transfer_prepare(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, const uint32_t* sel_n,
@@ -901,7 +966,7 @@ int kvm_transfer_prepare(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, co
     const size_t a = align256(size_t(v.rows) * v.pages * 4), b = align256(size_t(v.rows) * v.slots * 4),
                  n = align256(size_t(v.rows) * 4);
     // Everything the transfer needs is reserved here; the pool's tables are only read.
-    if (cudaMalloc(&t->mem, a + 3 * b + n) != cudaSuccess ||
+    if (cudaMalloc(&t->mem, a + 3 * b + n + 256) != cudaSuccess ||
         cudaEventCreateWithFlags(&t->planned, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&t->spill_done, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&t->restore_done, cudaEventDisableTiming) != cudaSuccess) {
@@ -916,8 +981,10 @@ int kvm_transfer_prepare(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, co
     t->shadow.restore = reinterpret_cast<uint32_t*>(base + a + b);
     t->shadow.restore_slot = reinterpret_cast<uint32_t*>(base + a + 2 * b);
     t->shadow.n_restore = reinterpret_cast<uint32_t*>(base + a + 3 * b);
+    t->status = reinterpret_cast<DeviceStatus*>(base + a + 3 * b + n);
     int rc = KVM_OK;
-    if (cudaMemcpyAsync(t->shadow.slot_of, v.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToDevice, s) !=
+    if (cudaMemsetAsync(t->status, 0, sizeof(DeviceStatus), s) != cudaSuccess ||
+        cudaMemcpyAsync(t->shadow.slot_of, v.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToDevice, s) !=
             cudaSuccess ||
         cudaMemcpyAsync(t->shadow.page_of, v.page_of, size_t(v.rows) * v.slots * 4, cudaMemcpyDeviceToDevice, s) !=
             cudaSuccess) {
@@ -928,7 +995,8 @@ int kvm_transfer_prepare(kvm_ctx* c, kvm_pool* pool, const uint32_t* sel_ids, co
         kvm_pool shadow_pool;
         shadow_pool.ctx = c;
         shadow_pool.view = t->shadow;
-        rc = plan_rows(c, &shadow_pool, 0, v.rows, sel_ids, sel_n, sel_stride, force_reload, nullptr, nullptr, s);
+        rc = plan_rows(c, &shadow_pool, 0, v.rows, sel_ids, sel_n, sel_stride, force_reload, nullptr, nullptr, s,
+                       t->status);
     }
     if (rc == KVM_OK && cudaEventRecord(t->planned, s) != cudaSuccess) {
         cudaGetLastError();
@@ -956,7 +1024,7 @@ int kvm_transfer_start_spill(kvm_transfer* t, const kvm_stage_layout* layout, co
         GatherLayout g{};
         KVM_TRY(gather_layout(layout, &g));
         const auto& v = t->pool->view;
-        spill_gather_kernel<<<ctas ? ctas : 32, kGatherThreads, 0, s>>>(v.page_of, t->shadow.slot_of, stale, v.rows,
+        spill_gather_kernel<<<ctas ? ctas : kGatherDefaultCtas, kGatherThreads, 0, s>>>(v.page_of, t->shadow.slot_of, stale, v.rows,
                                                                         v.pages, v.slots, t->force, g);
         ++t->ctx->launches;
         KVM_CUDA(cudaGetLastError());
@@ -1004,10 +1072,13 @@ int kvm_transfer_publish(kvm_transfer* t, void* stream) {
     const int ready = event_ready(t->restore_done);
     if (ready != KVM_OK) return ready;
     auto s = static_cast<cudaStream_t>(stream);
-    // A device-side failure of the plan or the copies fails the transfer; its
-    // restore has already reused slots, so the previous view is not preserved.
-    const int st = kvm_ctx_status(t->ctx, stream);
-    if (st != KVM_OK) return st == KVM_ERR_BUDGET_EXCEEDED ? st : KVM_ERR_TRANSFER_FAILED;
+    // A device-side failure of the plan fails the transfer; its restore has
+    // already reused slots, so the previous view is not preserved. Only the
+    // transfer's own status word is read: the context's is left to its owner.
+    DeviceStatus st{};
+    KVM_CUDA(cudaMemcpyAsync(&st, t->status, sizeof(st), cudaMemcpyDeviceToHost, s));
+    KVM_CUDA(cudaStreamSynchronize(s));
+    if (st.code != KVM_OK) return st.code == KVM_ERR_BUDGET_EXCEEDED ? st.code : KVM_ERR_TRANSFER_FAILED;
     const auto& v = t->pool->view;
     const auto& w = t->shadow;
     KVM_CUDA(cudaMemcpyAsync(v.slot_of, w.slot_of, size_t(v.rows) * v.pages * 4, cudaMemcpyDeviceToDevice, s));
@@ -1039,7 +1110,10 @@ int kvm_transfer_abort(kvm_transfer* t, uint64_t timeout_us, int* previous_view_
     t->drained = rc == KVM_OK;
     if (previous_view_preserved) *previous_view_preserved = (!t->restore_started && t->drained) ? 1 : 0;
     t->phase = kvm_transfer::Aborted;
-    if (t->pool->pending == t) t->pool->pending = nullptr;
+    // A transfer whose copies may still write the pool's slots keeps the pool
+    // blocked (prepare returns KVM_ERR_PENDING) until a later drain succeeds:
+    // kvm_transfer_destroy or kvm_pool_reset.
+    if (t->drained && t->pool->pending == t) t->pool->pending = nullptr;
     return rc;
 }
 
@@ -1050,6 +1124,7 @@ int kvm_transfer_destroy(kvm_transfer* t) {
         int preserved = 0;
         kvm_transfer_abort(t, 30ull * 1000 * 1000, &preserved);
     }
+    if (!t->drained) KVM_TRY(transfer_drain(t, 30ull * 1000 * 1000));
     if (!t->drained) return KVM_ERR_TIMEOUT;  // device work may still use the buffers: keep them
     transfer_free(t);
     return KVM_OK;
@@ -1082,6 +1157,66 @@ int kvm_stagein_pool(kvm_ctx* c, kvm_pool* pool, const kvm_stage_layout* layout,
     KVM_TRY(gather_layout(layout, &g));
     DeviceGuard guard(c->device);
     return gather_rows(c, pool, 0, pool->view.rows, g, ctas, static_cast<cudaStream_t>(stream));
+}
+
+int kvm_shard_stagein(kvm_ctx* c, kvm_pool* pool, const kvm_stage_layout* layout, uint32_t page0,
+                      uint32_t page_count, uint32_t ctas, void* stream) {
+    if (!c || !pool || pool->ctx != c || !page_count) return KVM_ERR_INVALID_ARGUMENT;
+    if (uint64_t(page0) + page_count > pool->view.pages) return KVM_ERR_INVALID_ARGUMENT;
+    GatherLayout g{};
+    KVM_TRY(gather_layout(layout, &g));
+    DeviceGuard guard(c->device);
+    return gather_rows(c, pool, 0, pool->view.rows, g, ctas, static_cast<cudaStream_t>(stream), page0,
+                       page0 + page_count, 1);
+}
+
+int kvm_ipc_export(const void* dev_ptr, void* handle) {
+    if (!dev_ptr || !handle) return KVM_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(uint64_t) <= KVM_IPC_HANDLE_BYTES, "IPC handle size");
+    AddressRangeFn range = address_range_fn();
+    if (!range) return KVM_ERR_CUDA;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return KVM_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h{};
+    KVM_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    const uint64_t offset = reinterpret_cast<uintptr_t>(dev_ptr) - base;
+    std::memset(handle, 0, KVM_IPC_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    std::memcpy(static_cast<uint8_t*>(handle) + sizeof(h), &offset, sizeof(offset));
+    return KVM_OK;
+}
+
+int kvm_ipc_open(int device, const void* handle, void** dev_ptr) {
+    if (!handle || !dev_ptr) return KVM_ERR_INVALID_ARGUMENT;
+    *dev_ptr = nullptr;
+    DeviceGuard guard(device);
+    if (!guard.ok) return KVM_ERR_CUDA;
+    cudaIpcMemHandle_t h{};
+    uint64_t offset = 0;
+    std::memcpy(&h, handle, sizeof(h));
+    std::memcpy(&offset, static_cast<const uint8_t*>(handle) + sizeof(h), sizeof(offset));
+    void* base = nullptr;
+    KVM_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr = static_cast<uint8_t*>(base) + offset;
+    std::lock_guard<std::mutex> lock(ipc_mutex());
+    ipc_bases()[*dev_ptr] = base;
+    return KVM_OK;
+}
+
+int kvm_ipc_close(int device, void* dev_ptr) {
+    if (!dev_ptr) return KVM_OK;
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(ipc_mutex());
+        auto it = ipc_bases().find(dev_ptr);
+        if (it == ipc_bases().end()) return KVM_ERR_INVALID_ARGUMENT;
+        base = it->second;
+        ipc_bases().erase(it);
+    }
+    DeviceGuard guard(device);
+    KVM_CUDA(cudaIpcCloseMemHandle(base));
+    return KVM_OK;
 }
 
 int kvm_stagein_copies(kvm_ctx* c, const kvm_copy* ops, uint32_t n, uint32_t ctas, void* stream) {
@@ -1121,7 +1256,7 @@ int kvm_stagein_copies(kvm_ctx* c, const kvm_copy* ops, uint32_t n, uint32_t cta
     std::memcpy(L.host, ops, size_t(n) * sizeof(CopyOp));
     CopyOp* dev_ops = nullptr;
     KVM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_ops), L.host, 0));
-    const uint32_t grid = std::min<uint32_t>(n, ctas ? ctas : 64);
+    const uint32_t grid = std::min<uint32_t>(n, ctas ? ctas : kGatherDefaultCtas);
     copy_ops_kernel<<<grid, kGatherThreads, 0, s>>>(dev_ops, n);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
@@ -1454,6 +1589,30 @@ int kvm_meank_score(kvm_ctx* c, const float* sums, const uint32_t* counts, const
     const float weight = aggregation == 0 ? 1.f / (float(nact) * q_heads) : 1.f / (float(nact) * kv_heads);
     meank_accumulate_kernel<<<(n + 255) / 256, 256, 0, s>>>(logits, norms, ginv, d_enabled, n, uint32_t(dists), group,
                                                             aggregation, weight, out);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_layerwise_accumulate(kvm_ctx* c, const float* tile, uint32_t pages, uint32_t halves, int keep_halves,
+                             const uint8_t* score_mask, double* accum, void* stream) {
+    if (!c || !tile || !score_mask || !accum || !pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (halves != 1 && halves != 2) return KVM_ERR_INVALID_ARGUMENT;
+    if (keep_halves && halves != 2) return KVM_ERR_INVALID_ARGUMENT;  // needs two Mean-K records per page
+    DeviceGuard guard(c->device);
+    layerwise_accumulate_kernel<<<1, kLayerwiseThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        tile, pages, halves, keep_halves, score_mask, accum, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
+}
+
+int kvm_layerwise_finish(kvm_ctx* c, const double* accum, uint32_t pages, int keep_halves, float* scores,
+                         void* stream) {
+    if (!c || !accum || !scores || !pages) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    const uint32_t grid = std::min<uint32_t>((pages + 255) / 256, uint32_t(c->num_sms));
+    layerwise_finish_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(accum, pages, keep_halves, scores);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
     return KVM_OK;

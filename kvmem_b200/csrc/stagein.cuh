@@ -19,7 +19,12 @@
 namespace kvmb {
 
 constexpr int kPlanThreads = 512;
-constexpr int kGatherThreads = 256;
+// 128 threads and no shared memory per gather CTA: small enough to sit on an SM
+// beside the two CTAs of the page scorer (2 x 288 threads x 96 registers, ~220 KB
+// of shared memory), so a stage-in on a side stream runs during scoring instead
+// of waiting for the scorer's persistent CTAs to exit.
+constexpr int kGatherThreads = 128;
+constexpr int kGatherDefaultCtas = 64;
 constexpr int kGatherUnroll = 8;
 
 struct PoolView {
@@ -138,23 +143,34 @@ __device__ __forceinline__ void copy_item(const uint8_t* __restrict__ src, uint8
     }
 }
 
-__global__ void __launch_bounds__(kGatherThreads) stagein_gather_kernel(PoolView pool, uint32_t row0, uint32_t nrows,
-                                                                        GatherLayout lay) {
+// Restores of rows [row0, row0 + nrows) whose page lies in [page0, page_end)
+// (the whole row: 0 and pages). The host records start at page page0: page p of
+// row r is at host_base + r*host_row_stride + (p - page0)*host_page_stride, so a
+// rank of a page-range partition passes only its own range's records. With
+// `fence_sys`, every thread fences its writes at system scope before it exits:
+// the destination may be another GPU's memory (a peer mapping), and the
+// collective that follows the gather on the stream must find them in place.
+__global__ void __launch_bounds__(kGatherThreads, 8) stagein_gather_kernel(PoolView pool, uint32_t row0, uint32_t nrows,
+                                                                        GatherLayout lay, uint32_t page0,
+                                                                        uint32_t page_end, int fence_sys) {
     uint64_t item = 0;
     for (uint32_t r = row0; r < row0 + nrows; ++r) {
         const uint32_t n = pool.n_restore[r];
         const uint32_t* rest = pool.restore + uint64_t(r) * pool.slots;
         const uint32_t* rest_slot = pool.restore_slot + uint64_t(r) * pool.slots;
-        for (uint32_t i = 0; i < n; ++i)
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t p = rest[i], s = rest_slot[i];
+            if (p < page0 || p >= page_end) continue;
             for (uint32_t j = 0; j < lay.planes; ++j, ++item) {
                 if (item % gridDim.x != blockIdx.x) continue;
-                const uint32_t p = rest[i], s = rest_slot[i];
                 const uint8_t* src = lay.host_base[j] + uint64_t(r) * lay.host_row_stride[j] +
-                                     uint64_t(p) * lay.host_page_stride[j];
+                                     uint64_t(p - page0) * lay.host_page_stride[j];
                 uint8_t* dst = lay.dev_base[j] + uint64_t(r) * lay.dev_row_stride[j] + uint64_t(s) * lay.dev_slot_stride[j];
                 copy_item(src, dst, lay.bytes[j]);
             }
+        }
     }
+    if (fence_sys) __threadfence_system();
 }
 
 // Write-back before a restore may reuse slots (the spill of a working-set
@@ -162,7 +178,7 @@ __global__ void __launch_bounds__(kGatherThreads) stagein_gather_kernel(PoolView
 // the new plan (not at that slot in new_slot_of, or force_reload) and whose host
 // copy is stale (stale[row][p] != 0), the device slot's bytes are copied to the
 // page's host record (mapped pinned memory). Items are spread over the CTAs.
-__global__ void __launch_bounds__(kGatherThreads) spill_gather_kernel(const int32_t* old_page_of,
+__global__ void __launch_bounds__(kGatherThreads, 8) spill_gather_kernel(const int32_t* old_page_of,
                                                                        const int32_t* new_slot_of,
                                                                        const uint8_t* stale, uint32_t rows,
                                                                        uint32_t pages, uint32_t slots, int force,
@@ -189,7 +205,7 @@ struct CopyOp {
     uint64_t bytes;
 };
 
-__global__ void __launch_bounds__(kGatherThreads) copy_ops_kernel(const CopyOp* ops, uint32_t n) {
+__global__ void __launch_bounds__(kGatherThreads, 8) copy_ops_kernel(const CopyOp* ops, uint32_t n) {
     for (uint32_t i = blockIdx.x; i < n; i += gridDim.x) {
         const CopyOp op = ops[i];
         if (op.src && op.dst && op.bytes) copy_item(op.src, op.dst, op.bytes);

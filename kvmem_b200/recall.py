@@ -247,6 +247,24 @@ class RecallContext:
         A.check(rc, "kvm_meank_score")
         return out
 
+    def layerwise_accumulate(self, tile: torch.Tensor, score_mask: torch.Tensor, accum: torch.Tensor, *,
+                             halves: int = 1, keep_halves: bool = False, stream=None) -> None:
+        """kvm_layerwise_accumulate: tile f32 [pages * halves], score_mask u8 [pages],
+        accum f64 [pages * (2 if keep_halves else 1)] (all device)."""
+        pages = score_mask.numel()
+        A.check(self.lib.kvm_layerwise_accumulate(self.h, tile.data_ptr(), pages, halves, int(keep_halves),
+                                                  score_mask.data_ptr(), accum.data_ptr(), _stream_ptr(stream)),
+                "kvm_layerwise_accumulate")
+
+    def layerwise_finish(self, accum: torch.Tensor, pages: int, *, keep_halves: bool = False,
+                         out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        """kvm_layerwise_finish -> scores f32 [pages] (device)."""
+        if out is None:
+            out = torch.empty((pages,), dtype=torch.float32, device=accum.device)
+        A.check(self.lib.kvm_layerwise_finish(self.h, accum.data_ptr(), pages, int(keep_halves), out.data_ptr(),
+                                              _stream_ptr(stream)), "kvm_layerwise_finish")
+        return out
+
     def stagein_copies(self, ops: Sequence[tuple], ctas: int = 0, stream=None) -> None:
         arr = (A.Copy * max(1, len(ops)))()
         for i, (src, dst, nbytes) in enumerate(ops):
@@ -309,6 +327,14 @@ class ResidencyPool:
     def stage_in(self, layout: A.StageLayout, ctas: int = 0, stream=None) -> None:
         A.check(self.ctx.lib.kvm_stagein_pool(self.ctx.h, self.h, C.byref(layout), ctas, _stream_ptr(stream)),
                 "kvm_stagein_pool")
+
+    def stage_in_range(self, layout: A.StageLayout, page0: int, page_count: int, ctas: int = 0,
+                       stream=None) -> None:
+        """kvm_shard_stagein: the planned restores of pages [page0, page0 + page_count) from
+        this rank's records (layout.host_base starts at page0) into layout.dev_base, which
+        may be a peer mapping of the decode GPU's cache (ipc_open)."""
+        A.check(self.ctx.lib.kvm_shard_stagein(self.ctx.h, self.h, C.byref(layout), page0, page_count, ctas,
+                                               _stream_ptr(stream)), "kvm_shard_stagein")
 
     def read(self, stream=None):
         import numpy as np
@@ -441,6 +467,25 @@ class StageOut:
 
     def clear(self) -> None:
         A.check(self.lib.kvm_stageout_clear(self.h), "kvm_stageout_clear")
+
+
+def ipc_export(t: torch.Tensor) -> bytes:
+    """Opaque handle (kvm_ipc_export) naming a device tensor's memory for another process."""
+    buf = (C.c_uint8 * A.IPC_HANDLE_BYTES)()
+    A.check(A.load().kvm_ipc_export(t.data_ptr(), buf), "kvm_ipc_export")
+    return bytes(buf)
+
+
+def ipc_open(device: int, handle: bytes) -> int:
+    """Maps another process's device memory on `device` (peer access enabled); returns the address."""
+    buf = (C.c_uint8 * A.IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    ptr = C.c_void_p()
+    A.check(A.load().kvm_ipc_open(device, buf, C.byref(ptr)), "kvm_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(device: int, ptr: int) -> None:
+    A.check(A.load().kvm_ipc_close(device, ptr), "kvm_ipc_close")
 
 
 def stage_layout(planes: Sequence[dict]) -> A.StageLayout:

@@ -141,3 +141,68 @@ class ShardedSelector:
         cs, ci = self.compute.candidates(mass, geo, keep, kcand)
         gs, gi = self._all_gather(cs), self._all_gather(ci)
         return self.compute.merge(gs, gi, self.world, geo, keep, kcand, budget)
+
+
+class ShardedRecall:
+    """A whole decode-step recall over a page-range partition: selection and stage-in.
+
+    The step is cut into layer chunks, pipelined as in kvm_recall_step. Per chunk, on
+    every rank: the sharded selection of the chunk's layers (ShardedSelector: two
+    all-gathers), the residency plan of those rows on this rank's copy of the pool
+    (every rank plans the same merged selection with the same deterministic kernel, so
+    the copies stay identical without a collective), then, on a side stream, the
+    gather of the planned restores that lie in this rank's page range, from this rank's
+    pinned records over its own PCIe link into the decode rank's paged cache (through a
+    peer mapping of it on the other ranks: NVLink). The gather of chunk i overlaps the
+    scoring of chunk i + 1. The step ends with a one-element all-reduce enqueued after
+    the gathers on every rank: when it completes on the decode rank, every rank's pages
+    are in its cache.
+
+    pools[i] / layouts[i]: chunk i's residency table (rows = its layers x groups, all
+    pages of the history) and stage-in layout (host records of this rank's range,
+    destination = the decode rank's cache rows of the chunk)."""
+
+    def __init__(self, selector: ShardedSelector, pools, layouts, chunk_layers, geo: ShardGeometry,
+                 stage_ctas: int = 64):
+        self.sel = selector
+        self.pools, self.layouts = pools, layouts
+        self.chunk_layers = chunk_layers  # [(l0, nl)]
+        self.geo = geo
+        self.stage_ctas = stage_ctas
+        dev = torch.device("cuda", selector.compute.ctx.device)
+        self.side = torch.cuda.Stream(device=dev)
+        self.events = [torch.cuda.Event() for _ in chunk_layers]
+        self.flag = torch.ones(1, dtype=torch.int32, device=dev)
+        self.ids = torch.zeros((geo.sel_rows, 1), dtype=torch.int32, device=dev)
+        self.n = torch.zeros((geo.sel_rows,), dtype=torch.int32, device=dev)
+
+    def step(self, desc, q: torch.Tensor, k, keep: Sequence[int], budget: int, *, force_reload: bool = False):
+        """desc: the whole step's kvm_score_desc (global token count); q: [L][R][Hq][D] device
+        queries; k: kvm_kcache of this rank's pages for all layers. Returns (ids, n) of all
+        selection rows ([L*groups][budget], [L*groups]), identical on every rank."""
+        from .recall import RecallContext
+        g = self.geo
+        if self.ids.shape[1] != budget:
+            self.ids = torch.zeros((g.sel_rows, budget), dtype=torch.int32, device=self.ids.device)
+        main = torch.cuda.current_stream()
+        for ci, (l0, nl) in enumerate(self.chunk_layers):
+            d = type(desc).from_buffer_copy(desc)
+            d.layers = nl
+            kc = type(k).from_buffer_copy(k)
+            kc.data = k.data + l0 * k.layer_stride
+            qd = RecallContext.make_query(q[l0:l0 + nl], q.shape[1])
+            geo = ShardGeometry(layers=nl, rows=g.rows, q_heads=g.q_heads, kv_heads=g.kv_heads, groups=g.groups,
+                                total_pages=g.total_pages, page0=g.page0, local_pages=g.local_pages)
+            ids, n = self.sel.select(d, qd, kc, geo, keep, budget)
+            r0, nr = l0 * g.groups, nl * g.groups
+            self.ids[r0:r0 + nr].copy_(ids)
+            self.n[r0:r0 + nr].copy_(n)
+            self.pools[ci].plan(ids, n, force_reload=force_reload)
+            self.events[ci].record(main)
+            self.side.wait_event(self.events[ci])
+            self.pools[ci].stage_in_range(self.layouts[ci], g.page0, g.local_pages, ctas=self.stage_ctas,
+                                          stream=self.side)
+        main.wait_stream(self.side)
+        if self.sel.world > 1:
+            dist.all_reduce(self.flag, op=dist.ReduceOp.MAX, group=self.sel.group)  # the decode cache is complete
+        return self.ids, self.n

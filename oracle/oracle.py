@@ -118,6 +118,10 @@ def ref():
         L.kvref_plan_residency.argtypes = lib().kvo_plan_residency.argtypes
         L.kvref_propagate_scores.argtypes = _PROPAGATE_ARGS
         L.kvref_lrfu_preview.argtypes = _LRFU_ARGS
+        L.kvref_layerwise_tile_scores.argtypes = [_u64p, _u32p, _u8p, _u8p, C.c_uint64, C.c_uint64, C.c_uint32,
+                                                  C.c_uint32, C.c_int, _f64p, C.c_uint64, _f64p,
+                                                  C.POINTER(C.c_uint64)]
+        L.kvref_layerwise_max_page_scores.argtypes = [_f64p, C.c_uint64, _f64p]
         _ref = L
     return _ref
 
@@ -324,6 +328,33 @@ def ref_page_softmax_scores(sums, counts, q, layer_rows, *, heads, kv_heads, dim
     if rc:
         raise ValueError(f"reference page_softmax_scores rejected (rc={rc})")
     return out[:P]
+
+
+def ref_layerwise_tile_scores(frame: dict, page_tokens: int, mean_tokens: int, keep_halves: bool, masses):
+    """The reference's layerwise_tile_scores of one tile whose scorer returned `masses`
+    (over the half-page frame when mean_tokens = page_tokens / 2). Raises on a rejection."""
+    n = len(frame["starts"])
+    masses = np.ascontiguousarray(masses, np.float64)
+    out = np.zeros(2 * n + 1, np.float64)
+    k = C.c_uint64()
+    rc = ref().kvref_layerwise_tile_scores(np.ascontiguousarray(frame["starts"], np.uint64),
+                                           np.ascontiguousarray(frame["counts"], np.uint32),
+                                           np.ascontiguousarray(frame["score_mask"], np.uint8),
+                                           np.ascontiguousarray(frame["transport_mask"], np.uint8), n,
+                                           frame["accepted_through"], page_tokens, mean_tokens, int(keep_halves),
+                                           masses, len(masses), out, C.byref(k))
+    if rc:
+        raise ValueError(f"reference layerwise_tile_scores rejected (rc={rc})")
+    return out[:k.value].copy()
+
+
+def ref_layerwise_max_page_scores(halves):
+    halves = np.ascontiguousarray(halves, np.float64)
+    out = np.zeros(max(1, len(halves) // 2), np.float64)
+    rc = ref().kvref_layerwise_max_page_scores(halves, len(halves), out)
+    if rc:
+        raise ValueError(f"reference layerwise_max_page_scores rejected (rc={rc})")
+    return out[: len(halves) // 2]
 
 
 def _graph_arrays(graph):

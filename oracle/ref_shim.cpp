@@ -7,6 +7,7 @@
 // product never links it. Exceptions are mapped to status codes:
 //   0 ok, 1 std::invalid_argument / MemoryError(InvalidPlan), 2 other exception.
 #include "kvmem/graph_recall.hpp"
+#include "kvmem/layerwise_selection.hpp"
 #include "kvmem/kvmem_store.hpp"
 #include "kvmem/memory_contract.hpp"
 #include "kvmem/raw_kv_store.hpp"
@@ -182,6 +183,40 @@ int kvref_lrfu_preview(const double* scores, uint32_t n, const double* prev, uin
         history.begin_round();
         history.preview(std::vector<double>(scores, scores + n));
         for (uint32_t i = 0; i < n; ++i) out[i] = history.score(i);
+    });
+}
+
+// layerwise_tile_scores (kvmem/src/host/layerwise_selection.cpp:32-75) over the
+// frame of n pages (starts / counts / masks) with a scorer that returns the given
+// masses (n_masses of them: n, or 2n for the half-page frame); out receives the
+// tile's slot scores (*out_n of them).
+int kvref_layerwise_tile_scores(const uint64_t* starts, const uint32_t* counts, const uint8_t* score_mask,
+                                const uint8_t* transport_mask, uint64_t n, uint64_t accepted, uint32_t page_tokens,
+                                uint32_t mean_tokens, int keep_halves, const double* masses, uint64_t n_masses,
+                                double* out, uint64_t* out_n) {
+    return guarded([&] {
+        kvmem::QueryScoreFrame f;
+        f.accepted_through = accepted;
+        f.starts.assign(starts, starts + n);
+        f.counts.assign(counts, counts + n);
+        f.score_mask.assign(score_mask, score_mask + n);
+        f.transport_mask.assign(transport_mask, transport_mask + n);
+        const auto r = kvmem::layerwise_tile_scores(f, page_tokens, mean_tokens, keep_halves != 0,
+                                                    [&](const kvmem::QueryScoreFrame& g) {
+                                                        if (g.starts.size() != n_masses)
+                                                            throw std::invalid_argument("mass count");
+                                                        return std::vector<double>(masses, masses + n_masses);
+                                                    });
+        std::memcpy(out, r.data(), r.size() * sizeof(double));
+        *out_n = r.size();
+    });
+}
+
+// layerwise_max_page_scores (kvmem/src/host/layerwise_selection.cpp:24-30).
+int kvref_layerwise_max_page_scores(const double* halves, uint64_t n, double* out) {
+    return guarded([&] {
+        const auto r = kvmem::layerwise_max_page_scores(std::vector<double>(halves, halves + n));
+        std::memcpy(out, r.data(), r.size() * sizeof(double));
     });
 }
 

@@ -1,6 +1,7 @@
-"""CPU: the C++ memory-backend adapter (kvmem_b200/adapter) and its session test compile
-against the reference's `kvmem/memory_contract.hpp` and link against libkvm_b200.so and the
-reference build (runs where the reference headers and both libraries are present)."""
+"""CPU: the C++ adapters (kvmem_b200/adapter: the memory backend, llama_kvmem_attention_cuda,
+kvmem::PageSoftmaxCuda) and their tests compile against the reference's own headers and link
+against libkvm_b200.so and the reference build (runs where the reference headers and the
+libraries are present)."""
 import os
 import subprocess
 
@@ -21,3 +22,4 @@ def test_adapter_compiles_against_the_reference_contract(tmp_path):
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert os.path.exists(os.path.join(tmp_path, "memory_session_test"))
+    assert os.path.exists(os.path.join(tmp_path, "adapters_test"))

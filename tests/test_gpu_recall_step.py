@@ -17,8 +17,9 @@ Configs: 1 at full size (4 layers x 16,384 tokens, 32/8 heads, D 128, per-KV-hea
 selection, top-16 + first/last), 2 with 2 of its 64 layers at the full 131,072
 fp16 tokens (top-32 + first/last), 3 with 1 layer at the full 262,144 q8_0 tokens
 (q4_0 V, top-64 + first/last; and once more at top-32). The queries change between
-steps (the workload's query, then one of another seed, then the first again) so
-later steps restore and evict pages, not only the cold first step.
+steps so that later steps restore and evict pages, not only the cold first step:
+the workload's step-0 query, a query of another seed, then the workload's step-1
+query (whose rotating needle group differs from step 0's).
 
 Which rows the gap rule leaves to check: with the workload's own queries the needle
 pages stand far above the rest, so where the selection width does not exceed the
@@ -45,8 +46,8 @@ def _build(cfg, layers, seed=0):
     w = dataclasses.replace(synth.CONFIGS[cfg], layers=layers)
     T = w.pages * w.page_tokens
     rbk, rbv = row_bytes(w.k_type, w.head_dim), row_bytes(w.v_type, w.head_dim)
-    q0, _ = synth.make_queries(w, seed, dev)
-    q1, _ = synth.make_queries(w, seed + 101, dev)
+    q0, (d0, d1) = synth.make_queries(w, seed, dev, drift_steps=2)
+    q_other, _ = synth.make_queries(w, seed + 101, dev)
     k_dev = torch.empty((layers, T, w.kv_heads, rbk), dtype=torch.uint8, device=dev)
     v_dev = torch.empty((layers, T, w.kv_heads, rbv), dtype=torch.uint8, device=dev)
     for l in range(layers):
@@ -56,7 +57,7 @@ def _build(cfg, layers, seed=0):
         vl = synth.fp16_v_layer(w, seed, l, dev).view(torch.uint8) if w.v_type == 1 \
             else synth.q4_0_v_layer(w, seed, l, dev)
         v_dev[l] = vl.reshape(T, w.kv_heads, rbv)
-    return w, k_dev, v_dev, [q0, q1, q0], rbk, rbv
+    return w, k_dev, v_dev, [d0, q_other, d1], rbk, rbv
 
 
 def _records(x, groups):

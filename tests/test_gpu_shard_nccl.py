@@ -1,8 +1,11 @@
-"""Sharded selection across 2 GPUs with NCCL all-gathers (skipped with fewer GPUs).
+"""Sharded selection and recall across 2 GPUs with NCCL all-gathers (skipped with fewer GPUs).
 
 Runs tests/shard_nccl_worker.py under torchrun (one rank per GPU, 127.0.0.1
 rendezvous, bounded by a timeout) and checks that every rank ends with the same
-selection as the unsharded top-k of the whole history.
+selection as the unsharded top-k of the whole history, and that the sharded
+recall step (kvmem_b200.shard.ShardedRecall) leaves rank 0's paged cache holding
+exactly the host records of the selected pages, each rank having written the
+pages of its own range (rank 1 through a CUDA-IPC peer mapping).
 """
 import json
 import os
@@ -29,3 +32,7 @@ def test_two_rank_nccl_sharded_selection(tmp_path):
     res = [json.load(open(tmp_path / f"rank{i}.json")) for i in range(2)]
     assert res[0]["status"] == 0 and res[1]["status"] == 0
     assert res[0]["ids"] == res[1]["ids"] == res[0]["unsharded"]
+    # sharded recall: each rank's restored pages written into rank 0's cache over NVLink
+    for r in res:
+        assert r["recall"]["steps"] == 3 and r["recall"]["status"] == 0
+    assert res[0]["recall"]["bad"] == [], res[0]["recall"]["bad"][:10]

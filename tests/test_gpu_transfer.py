@@ -171,3 +171,52 @@ def test_abort_before_restore_preserves_previous_view(ctx):
         t.close()
     finally:
         pool.close()
+
+
+def test_abort_that_cannot_drain_keeps_the_pool_blocked(ctx):
+    """An abort whose bounded host wait runs out (1 us, while a ~1 GiB restore streams over
+    PCIe) reports KVM_ERR_TIMEOUT and keeps the pool blocked: a new prepare is refused
+    with KVM_ERR_PENDING until the transfer is destroyed (which drains it), and the
+    transfer's own status word, not the context's, decides its publish."""
+    rows, pages, slots, pbytes = 8, 64, 32, 4 << 20  # 8 rows x 32 pages x 4 MiB = 1 GiB restored
+    host = torch.empty(rows * pages * pbytes, dtype=torch.uint8).pin_memory()
+    host.view(-1)[::4096] = 7
+    cache = torch.zeros(rows * slots * pbytes, dtype=torch.uint8, device="cuda")
+    layout = K.stage_layout([dict(host_base=host.data_ptr(), host_row_stride=pages * pbytes,
+                                  host_page_stride=pbytes, dev_base=cache.data_ptr(),
+                                  dev_row_stride=slots * pbytes, dev_slot_stride=pbytes, bytes=pbytes)])
+    pool = K.ResidencyPool(ctx, rows, pages, slots)
+    lib = ctx.lib
+    import ctypes as C
+    try:
+        scores = torch.rand((rows, pages), device="cuda")
+        ids, n = ctx.select_topk(scores, [], slots)
+        t = K.Transfer(pool, ids, n)
+        t.start_spill(layout)
+        t.wait()
+        t.start_restore(layout, ctas=8)
+        kept = C.c_int(1)
+        rc = lib.kvm_transfer_abort(t.h, 1, C.byref(kept))
+        assert rc == K._abi.ERR_TIMEOUT and kept.value == 0
+        with pytest.raises(K.KvmError) as e:
+            K.Transfer(pool, ids, n)
+        assert e.value.code == K._abi.ERR_PENDING
+        assert lib.kvm_transfer_destroy(t.h) == K._abi.OK  # drains, then frees
+        t.h = None
+        t2 = K.Transfer(pool, ids, n)  # the pool is free again
+        t2.abort()
+        t2.close()
+        # a non-finite score on the context fails that selection's status, not a transfer
+        bad = torch.full((1, pages), float("nan"), device="cuda")
+        ctx.select_topk(bad, [], 4)
+        t3 = K.Transfer(pool, ids, n, force_reload=True)
+        t3.start_spill(layout)
+        t3.wait()
+        t3.start_restore(layout)
+        t3.wait()
+        t3.publish()
+        t3.close()
+        assert ctx.status() == K._abi.ERR_NONFINITE  # still there for its owner
+    finally:
+        torch.cuda.synchronize()
+        pool.close()
