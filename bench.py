@@ -55,8 +55,12 @@ def parse():
     ap.add_argument("--config", default="c2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--chunks", type=int, default=4)
-    ap.add_argument("--stage-ctas", type=int, default=64)
+    ap.add_argument("--chunks", type=int, default=8)
+    ap.add_argument("--first-layers", type=int, default=2,
+                    help="layers of the step's first chunk (starts the stage-in early)")
+    ap.add_argument("--kmirror", default="head", choices=["head", "token"],
+                    help="config 4: layout of the resident K score mirror (head-major or the engine's token-major)")
+    ap.add_argument("--stage-ctas", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline and the reference GPU timings")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sharded-selection key")
@@ -213,6 +217,22 @@ def build_history(w, seed, device, need_host=True, page_range=None):
                 layer_v=layer_v, rbk=rbk, rbv=rbv, page_k=page_k, page_v=page_v, page0=p0, local_pages=p1 - p0)
 
 
+def head_major_mirror(w, k_dev):
+    """K of every layer re-laid head-major ([layer][kv_head][token][row]): each KV head's
+    rows contiguous, so a 128-token tile is one contiguous 32 KiB run in HBM. Returns the
+    mirror and its kvm_kcache."""
+    import kvmem_b200 as K
+    from kvmem_b200 import _abi as A
+    rb = K.row_bytes(w.k_type, w.head_dim)
+    T = w.pages * w.page_tokens
+    mirror = k_dev.view(w.layers, T, w.kv_heads, rb).permute(0, 2, 1, 3).contiguous()
+    kc = A.KCache()
+    kc.data, kc.type = mirror.data_ptr(), w.k_type
+    kc.token_stride, kc.head_stride, kc.layer_stride = rb, T * rb, w.kv_heads * T * rb
+    kc.capacity_tokens = T
+    return mirror, kc
+
+
 def workload(args):
     import dataclasses
     from kvmem_b200 import synth
@@ -309,7 +329,8 @@ def run_ours(args, world, rank, local):
     def step(i, force=False, with_pool=True, qd=None):
         ctx.recall_step(desc, qd or qdescs[i % len(qdescs)], kc, w.keep, w.budget, mass_mean=mass, sel_ids=sel_ids,
                         sel_n=sel_n, pool=pool if with_pool else None, layout=layout if with_pool else None,
-                        chunks=args.chunks, stage_ctas=args.stage_ctas, force_reload=force)
+                        chunks=args.chunks, stage_ctas=args.stage_ctas, force_reload=force,
+                        first_layers=args.first_layers)
 
     def timed(n, fn):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -414,7 +435,7 @@ def run_ours(args, world, rank, local):
         "config": {"workload": w.name, "layers": L, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
                    "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": w.page_tokens, "pages": P,
                    "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
-                   "parallelism": "single GPU", "chunks": args.chunks,
+                   "parallelism": "single GPU", "chunks": args.chunks, "first_chunk_layers": args.first_layers,
                    "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
                    "step": "score all pages -> top-k -> residency plan -> stage-in of non-resident pages (K+V) "
                            f"from pinned host; the query of each step favours the next rotating needle group, "
@@ -876,8 +897,11 @@ def run_kernel_only(args, w, local):
     L, P = w.layers, w.pages
     desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
                                      tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
-    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     capacity_tokens=P * w.page_tokens)
+    if args.config == "c4" and args.kmirror == "head":
+        h["k_dev"], kc = head_major_mirror(w, h["k_dev"])
+    else:
+        kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                         capacity_tokens=P * w.page_tokens)
     qd = K.RecallContext.make_query(h["q_base"], w.rows)
     mass = torch.empty((L, w.groups, P), dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
@@ -925,8 +949,11 @@ def run_replay(args, w, world, rank, local):
     srows = L * w.groups
     desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
                                      tokens=w.tokens, page_tokens=w.page_tokens, groups=w.groups)
-    kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
-                                     capacity_tokens=P * w.page_tokens)
+    if args.kmirror == "head":
+        h["k_dev"], kc = head_major_mirror(w, h["k_dev"])
+    else:
+        kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
+                                         capacity_tokens=P * w.page_tokens)
     qs = [h["q_base"]] + h["drift"]
     qdescs = [K.RecallContext.make_query(q, w.rows) for q in qs]
     mass = torch.empty((srows, P), dtype=torch.float32, device=dev)
@@ -1016,6 +1043,7 @@ def run_replay(args, w, world, rank, local):
                    "kv_heads": w.kv_heads, "head_dim": w.head_dim, "tokens_per_lane": w.tokens,
                    "page_tokens": w.page_tokens, "pages": P, "replay_rows": w.rows,
                    "vectors_per_kv_head": vectors, "top_k": w.top_k, "selection": "per (lane, layer, KV head)",
+                   "k_mirror": args.kmirror + "-major",
                    "parallelism": f"lane replicas x{world}" if world > 1 else "single GPU",
                    "l2": f"inputs larger than L2 ({kbytes / 1e9:.1f} GB of K read per step)",
                    "step": "score all pages (tcgen05) -> mean over replayed rows -> top-24; no stage-in"},

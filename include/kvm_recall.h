@@ -166,6 +166,9 @@ int kvm_score_pages(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q
  * plugin host that forbids new device allocations after start-up.
  *  - Runs on the current device. The first call on a device looks up the
  *    array's device address; make that first call before any stream capture.
+ *    The address is kept for the life of the process: after cudaDeviceReset
+ *    (or anything else that tears down the device's primary context) it is
+ *    stale, so do not call this entry point on that device again.
  *  - Needs layers * rows * q_heads * pages * 4 bytes (rounded up to 256) of
  *    scratch, plus the packed rows of a row list (see kvm_query), at most
  *    8 MiB - 256 B in all; larger problems return KVM_ERR_LENGTH before any
@@ -523,7 +526,10 @@ int kvm_layerwise_finish(kvm_ctx* ctx, const double* accum, uint32_t pages, int 
 /* One decode-step recall: score -> per-row top-k -> residency plan -> stage-in,
  * pipelined over layer chunks so the stage-in of chunk i (side stream, PCIe)
  * overlaps the scoring of chunk i+1 (HBM). Selection rows are (layer, group)
- * pairs; the keep list applies to every row.
+ * pairs; the keep list applies to every row. When the stage-in of a step takes
+ * longer than its scoring, the step ends about one first chunk's scoring after
+ * the stage-in alone would: first_layers (< layers) makes the first chunk that
+ * small and splits the other layers into chunks - 1 chunks.
  *   mass_mean: device f32 [layers*groups][pages]
  *   sel_ids: device u32 [layers*groups][budget], sel_n: device u32 [layers*groups]
  *   pool: residency table with rows = layers*groups (NULL: select only)
@@ -539,7 +545,7 @@ typedef struct kvm_step_desc {
     uint32_t chunks;     /* layer chunks (0 = 4) */
     uint32_t stage_ctas; /* CTAs (128 threads each) of each gather launch (0 = 64) */
     int force_reload;    /* stage every selected page (cold worst case) */
-    int reserved;
+    uint32_t first_layers; /* layers of the first chunk (0: all chunks equal) */
 } kvm_step_desc;
 int kvm_recall_step(kvm_ctx* ctx, const kvm_step_desc* step, kvm_pool* pool, const kvm_stage_layout* layout,
                     float* mass_mean, uint32_t* sel_ids, uint32_t* sel_n, void* stream);

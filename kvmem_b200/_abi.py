@@ -84,7 +84,7 @@ class StepDesc(C.Structure):
     _fields_ = [("score", C.POINTER(ScoreDesc)), ("q", C.POINTER(Query)), ("k", C.POINTER(KCache)),
                 ("keep", C.POINTER(C.c_uint32)), ("nkeep", C.c_uint32), ("budget", C.c_uint32),
                 ("chunks", C.c_uint32), ("stage_ctas", C.c_uint32), ("force_reload", C.c_int),
-                ("reserved", C.c_int)]
+                ("first_layers", C.c_uint32)]
 
 
 _vp, _u32, _u64, _i = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int

@@ -179,6 +179,7 @@ struct LseConfig {
     size_t q_smem = 0;
     // tcgen05 scorer (fp16 keys, 16..160 query vectors per KV head), when usable.
     bool tc = false;
+    bool head_major = false;  // K is a head-major mirror (only the tcgen05 scorer reads it)
     int tc_ka = 0, tc_lm = 0;
     uint32_t tc_stages = 0;
     size_t tc_smem = 0;
@@ -255,21 +256,24 @@ void plan_mma(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
                     2 * 2 * kLseConsumerWarps * 8 * sizeof(float) + 16;
 }
 
-// Quantised-key scorer: the K heads of a token are split into the smallest
+// Quantised-key scorer: the K heads of a token are split into the largest
 // groups of hpg heads whose row bytes are a multiple of 16 and fit one TMA box
-// row (<= 255 u64 elements with the pad); each group has its own ring, its rows
-// land in shared memory at a stride of an odd number of 16-byte units (pad = 0
-// or 16 zero-filled bytes). A chunk is 8 tokens per warp of a KV head; the
-// rings and the kernel's other shared memory fill ~112 KiB so two CTAs share
-// an SM.
+// row (<= 255 u64 elements with the pad) -- normally all heads of a token, one
+// ring, so each chunk is one contiguous run of token rows in HBM; each group
+// has its own ring, its rows land in shared memory at a stride of an odd
+// number of 16-byte units (pad = 0 or 16 zero-filled bytes). A chunk is the
+// largest of 32, 16 or 8 tokens per warp of a KV head whose stage stays within
+// 40 KiB with two stages fitting; the rings and the kernel's other shared
+// memory fill ~112 KiB so two CTAs share an SM. (Config 3, q8_0 D 256 x 4 KV
+// heads: one ring of two 32-token, 35 KiB stages reads K at 0.99 of the
+// measured copy bandwidth, where four per-head rings of 16-token stages read it
+// at 0.74 and one ring of five 16-token stages at 0.78.)
 void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
     if (force_simt() || scorer_is("mma_generic")) return;
     if (k->type != KVM_Q8_0 && k->type != KVM_Q4_0) return;
     const uint32_t kvh = d->kv_heads;
     if (kvh == 0 || 8 % kvh) return;
     const uint64_t rb = row_bytes_of(k->type, d->head_dim);
-    const char* want_hpg = std::getenv("KVM_Q_HPG");  // tuning experiment
-    const char* want_tpc = std::getenv("KVM_Q_TPC");
     uint32_t hpg = 0, pad = 0;
     for (uint32_t h = 1; h <= kvh; h <<= 1) {
         const uint64_t gb = h * rb;
@@ -278,17 +282,30 @@ void plan_q(const kvm_score_desc* d, const kvm_kcache* k, LseConfig* cfg) {
         if ((gb + pd) / 8 > 255) break;
         hpg = h;
         pad = pd;
-        if (!want_hpg || h >= uint32_t(std::atoi(want_hpg))) break;
     }
     if (!hpg) return;
     const uint32_t slot = uint32_t(hpg * rb + pad), groups = kvh / hpg;
-    uint32_t tpc = 8 * (kLseConsumerWarps / kvh);
-    if (want_tpc && std::atoi(want_tpc) > 0 && uint32_t(std::atoi(want_tpc)) % tpc == 0) tpc = uint32_t(std::atoi(want_tpc));
+    const uint64_t budget = 112 * 1024 - q_smem_extra();
+    auto stages_for = [&](uint32_t tpc) {
+        const uint32_t stride = uint32_t((uint64_t(tpc) * slot + 127) / 128 * 128);
+        return uint32_t(std::min<uint64_t>(kMmaMaxStages, budget / (uint64_t(groups) * stride)));
+    };
+    // Chunks of 4, 2 or 1 octets per warp: the largest whose stages stay within
+    // 40 KiB and of which two fit (fewer, larger chunks mean fewer barrier
+    // round trips and refills per byte).
+    const uint32_t base = 8 * (kLseConsumerWarps / kvh);
+    uint32_t tpc = base;
+    for (uint32_t mult = 4; mult >= 2; mult /= 2) {
+        const uint32_t t = mult * base;
+        if (d->page_tokens % t == 0 && t <= 256 && uint64_t(t) * slot <= 40 * 1024 && stages_for(t) >= 2) {
+            tpc = t;
+            break;
+        }
+    }
     if (d->page_tokens % tpc || tpc > 256 || groups > uint32_t(kQMaxGroups)) return;
     const uint64_t stage = uint64_t(tpc) * slot;
     const uint32_t stride = uint32_t((stage + 127) / 128 * 128);
-    const uint64_t budget = 112 * 1024 - q_smem_extra();
-    const uint32_t stages = uint32_t(std::min<uint64_t>(kMmaMaxStages, budget / (uint64_t(groups) * stride)));
+    const uint32_t stages = stages_for(tpc);
     if (stages < 2) return;
     cfg->q = true;
     cfg->q_tpc = tpc;
@@ -319,14 +336,21 @@ int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache
     const uint32_t ng = kLseConsumerWarps * 32 / lpr;
     if (ng % d->kv_heads) return KVM_ERR_UNSUPPORTED;
     const uint64_t rb = row_bytes_of(k->type, D);
-    if (k->head_stride != rb || k->token_stride != rb * d->kv_heads) return KVM_ERR_UNSUPPORTED;
     const uint64_t pages = (d->tokens + d->page_tokens - 1) / d->page_tokens;
     if (!pages) return KVM_ERR_INVALID_ARGUMENT;
     if (k->capacity_tokens < pages * d->page_tokens) return KVM_ERR_UNSUPPORTED;
+    // Token-major (the engine's cache view) for every scorer; head-major (each KV
+    // head's rows contiguous, a score mirror) for the tcgen05 scorer.
+    const bool token_major = k->head_stride == rb && k->token_stride == rb * d->kv_heads;
+    const bool head_major = !token_major && d->kv_heads > 1 && k->token_stride == rb && !(k->head_stride & 15) &&
+                            k->head_stride >= k->capacity_tokens * rb;
+    if (!token_major && !head_major) return KVM_ERR_UNSUPPORTED;
     const uint64_t page_bytes = uint64_t(d->page_tokens) * k->token_stride;
     if ((reinterpret_cast<uintptr_t>(k->data) & 15) || (k->layer_stride & 15) || (page_bytes & 15))
         return KVM_ERR_UNSUPPORTED;
-    if (d->layers > 1 && k->layer_stride < pages * page_bytes) return KVM_ERR_INVALID_ARGUMENT;
+    const uint64_t layer_span = head_major ? d->kv_heads * k->head_stride : pages * page_bytes;
+    if (d->layers > 1 && k->layer_stride < layer_span) return KVM_ERR_INVALID_ARGUMENT;
+    cfg->head_major = head_major;
     if (pages > 0x7fffffffull || uint64_t(d->layers) * pages > 0x7fffffffull) return KVM_ERR_LENGTH;
     if (q->rows * uint64_t(d->q_heads / d->kv_heads) > 0x7fffffffull) return KVM_ERR_LENGTH;
     // Tokens per ring chunk: the largest power of two dividing page_tokens whose
@@ -348,10 +372,13 @@ int validate_score(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache
     cfg->stage_stride = uint32_t((cfg->chunk_bytes + 16 + 127) / 128 * 128);
     cfg->smem = size_t(kLseStages) * cfg->stage_stride + 2 * kLseStages * sizeof(uint64_t) +
                 2 * 2 * size_t(ng) * 8 * sizeof(float) + 16;
-    plan_mma(d, k, cfg);
-    plan_q(d, k, cfg);
+    if (!head_major) {
+        plan_mma(d, k, cfg);
+        plan_q(d, k, cfg);
+    }
     plan_tc(d, q, k, cfg);
     if (scorer_is("tc") && !cfg->tc) return KVM_ERR_UNSUPPORTED;  // strict: the tcgen05 kernel or nothing
+    if (head_major && !cfg->tc) return KVM_ERR_UNSUPPORTED;       // only the tcgen05 scorer reads head-major K
     return KVM_OK;
 }
 
@@ -419,17 +446,27 @@ std::unordered_map<void*, void*>& ipc_bases() {
 }
 
 // 4-D tensor map of fp16 K of layers [0, nl) from `base`: dims (head_dim,
-// kv_heads, tokens, layers), box 64 dims x 1 head x 128 tokens x 1 layer,
-// 128-byte swizzle; reads past the allocated tokens fill zeros.
-int encode_k_map(const kvm_score_desc* d, const kvm_kcache* k, const void* base, uint32_t nl, CUtensorMap* map) {
+// kv_heads, tokens, layers), box 64 dims x 1 head x 128 tokens x 1 layer, or
+// for a head-major mirror (head_dim, tokens, kv_heads, layers), box 64 dims x
+// 128 tokens x 1 head x 1 layer (strides increase in both); 128-byte swizzle;
+// reads past the allocated tokens fill zeros.
+int encode_k_map(const kvm_score_desc* d, const kvm_kcache* k, const void* base, uint32_t nl, bool head_major,
+                 CUtensorMap* map) {
     TensorMapEncodeFn enc = tensor_map_encoder();
     if (!enc) return KVM_ERR_CUDA;
     uint64_t cap = std::min<uint64_t>(k->capacity_tokens, 0x7fffffffull);
-    if (nl > 1) cap = std::min<uint64_t>(cap, k->layer_stride / k->token_stride);  // layers never overlap
-    const cuuint64_t dims[4] = {d->head_dim, d->kv_heads, cap, nl};
-    const uint64_t lstride = nl > 1 ? k->layer_stride : cap * k->token_stride;
-    const cuuint64_t strides[3] = {k->head_stride, k->token_stride, lstride};
-    const cuuint32_t box[4] = {64, 1, uint32_t(kTcTile), 1};
+    if (head_major) cap = std::min<uint64_t>(cap, k->head_stride / k->token_stride);  // heads never overlap
+    else if (nl > 1) cap = std::min<uint64_t>(cap, k->layer_stride / k->token_stride);  // layers never overlap
+    const uint64_t span = head_major ? uint64_t(d->kv_heads) * k->head_stride : cap * k->token_stride;
+    const uint64_t lstride = nl > 1 ? k->layer_stride : span;
+    cuuint64_t dims[4] = {d->head_dim, d->kv_heads, cap, nl};
+    cuuint64_t strides[3] = {k->head_stride, k->token_stride, lstride};
+    cuuint32_t box[4] = {64, 1, uint32_t(kTcTile), 1};
+    if (head_major) {
+        dims[1] = cap, dims[2] = d->kv_heads;
+        strides[0] = k->token_stride, strides[1] = k->head_stride;
+        box[1] = uint32_t(kTcTile), box[2] = 1;
+    }
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -520,7 +557,8 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
     if (cfg.tc) {
         // All query vectors of a KV head in one pass (one or two M tiles).
         CUtensorMap map;
-        KVM_TRY(encode_k_map(d, k, p.k, nl, &map));
+        KVM_TRY(encode_k_map(d, k, p.k, nl, cfg.head_major, &map));
+        p.head_major = cfg.head_major;
         p.stages = cfg.tc_stages;
         p.v0 = 0;
         p.nv = nvt;
@@ -1635,9 +1673,21 @@ int kvm_recall_step(kvm_ctx* c, const kvm_step_desc* st, kvm_pool* pool, const k
     }
     DeviceGuard guard(c->device);
     auto s = static_cast<cudaStream_t>(stream);
-    const uint32_t chunks = std::max<uint32_t>(1, std::min(st->chunks ? st->chunks : 4u, d->layers));
-    const uint32_t per = (d->layers + chunks - 1) / chunks;
-    KVM_TRY(ensure_ws(c, lse_bytes(d, per, st->q->rows)));
+    // Layer chunks: [l0, l0 + nl) each; a small first chunk when asked for.
+    const uint32_t nch = std::max<uint32_t>(1, std::min(st->chunks ? st->chunks : 4u, d->layers));
+    std::vector<std::pair<uint32_t, uint32_t>> parts;
+    uint32_t l0 = 0;
+    if (st->first_layers && st->first_layers < d->layers && nch > 1) {
+        parts.push_back({0, st->first_layers});
+        l0 = st->first_layers;
+    }
+    const uint32_t rest_chunks = parts.empty() ? nch : nch - 1;
+    const uint32_t per = (d->layers - l0 + rest_chunks - 1) / rest_chunks;
+    for (; l0 < d->layers; l0 += per) parts.push_back({l0, std::min(per, d->layers - l0)});
+    const uint32_t chunks = uint32_t(parts.size());
+    uint32_t widest = 0;
+    for (const auto& pc : parts) widest = std::max(widest, pc.second);
+    KVM_TRY(ensure_ws(c, lse_bytes(d, widest, st->q->rows)));
     while (c->events.size() < chunks) {
         cudaEvent_t e;
         KVM_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -1646,9 +1696,7 @@ int kvm_recall_step(kvm_ctx* c, const kvm_step_desc* st, kvm_pool* pool, const k
     const uint32_t out_stride = st->budget;
     bool staged = false;
     for (uint32_t ci = 0; ci < chunks; ++ci) {
-        const uint32_t l0 = ci * per;
-        if (l0 >= d->layers) break;
-        const uint32_t nl = std::min(per, d->layers - l0);
+        const uint32_t l0 = parts[ci].first, nl = parts[ci].second;
         KVM_TRY(score_layers(c, d, st->q, st->k, cfg, l0, nl, static_cast<float*>(c->ws), nullptr, mass_mean, s));
         const uint32_t r0 = l0 * d->groups, nr = nl * d->groups;
         KVM_TRY(select_rows(c, mass_mean + size_t(r0) * pages, nr, pages, pages, st->keep, st->nkeep, st->budget, 0,

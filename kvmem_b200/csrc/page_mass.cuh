@@ -59,6 +59,7 @@ struct LseParams {
     uint32_t slot_stride;   // tensor-core kernel, quantised keys: padded shared-memory stride per token
     uint32_t hpg;           // quantised-key kernel: KV heads per TMA head group
     uint32_t groups_tma;    // quantised-key kernel: head groups (one tiled TMA box each per chunk)
+    uint32_t head_major;    // tcgen05 kernel: K rows of one KV head are contiguous (head-major mirror)
 };
 
 // Decode the lane's 8 consecutive elements of one K row held in shared

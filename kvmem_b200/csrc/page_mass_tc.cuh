@@ -476,9 +476,10 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     mbar_arrive_expect_tx(&kfull[s], kStageBytes);
                     const int tok = int((uint64_t(un.j) * ut + t) * kTcTile);
 #pragma unroll
-                    for (int a = 0; a < KA; ++a)
-                        tma_load_4d(ksm + s * kStageBytes + a * kTcAtomBytes, &kmap, a * 64, int(un.h), tok,
-                                    int(un.l), &kfull[s], policy);
+                    for (int a = 0; a < KA; ++a)  // map dims: (D, heads, tokens) or, head-major, (D, tokens, heads)
+                        tma_load_4d(ksm + s * kStageBytes + a * kTcAtomBytes, &kmap, a * 64,
+                                    P.head_major ? tok : int(un.h), P.head_major ? int(un.h) : tok, int(un.l),
+                                    &kfull[s], policy);
                     issued = it + 1;
                     if (++s == S) {
                         s = 0;

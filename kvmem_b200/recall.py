@@ -277,7 +277,8 @@ class RecallContext:
     def recall_step(self, desc: A.ScoreDesc, q: A.Query, k: A.KCache, keep: Sequence[int], budget: int, *,
                     mass_mean: torch.Tensor, sel_ids: torch.Tensor, sel_n: torch.Tensor,
                     pool: Optional["ResidencyPool"] = None, layout: Optional[A.StageLayout] = None,
-                    chunks: int = 0, stage_ctas: int = 0, force_reload: bool = False, stream=None) -> None:
+                    chunks: int = 0, stage_ctas: int = 0, force_reload: bool = False, first_layers: int = 0,
+                    stream=None) -> None:
         st = A.StepDesc()
         st.score = C.pointer(desc)
         st.q = C.pointer(q)
@@ -286,6 +287,7 @@ class RecallContext:
         st.keep = C.cast(kp, C.POINTER(C.c_uint32))
         st.nkeep, st.budget, st.chunks, st.stage_ctas = len(keep), budget, chunks, stage_ctas
         st.force_reload = int(force_reload)
+        st.first_layers = first_layers
         rc = self.lib.kvm_recall_step(self.h, C.byref(st), pool.h if pool is not None else None,
                                       C.byref(layout) if layout is not None else None, mass_mean.data_ptr(),
                                       sel_ids.data_ptr(), sel_n.data_ptr(), _stream_ptr(stream))

@@ -142,6 +142,10 @@ def ref_cuda():
         L.kvref_page_softmax_cuda.argtypes = [C.c_int] + ref().kvref_page_softmax_scores.argtypes + [
             C.POINTER(C.c_double)]
         L.kvref_cuda_release.argtypes = []
+        _pp = C.POINTER(C.c_void_p)
+        L.kvref_stagein.argtypes = [C.c_int, C.c_uint32, _pp, _u64p, _pp, np.ctypeslib.ndpointer(np.int64),
+                                    np.ctypeslib.ndpointer(np.int32), C.c_int64, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, _f32p, C.c_int, C.c_uint32, _pp, _u64p, _pp]
         _refcuda = L
     return _refcuda
 
@@ -185,6 +189,33 @@ def ref_page_softmax_cuda(device, sums, counts, q, layer_rows, *, heads, kv_head
     if rc:
         raise ValueError(f"reference PageSoftmaxCuda::score failed (rc={rc})")
     return out[:P], ms.value
+
+
+def ref_stagein(ktype: int, k_items, *, n_head: int, dim: int, n_rot: int = 0, theta=None, nrot: int = 0,
+                v_items=()):
+    """The reference's stage-in route (kvmem_stagein_enqueue_k / _v + kvmem_stagein_flush,
+    src/adapter/llama-kvmem-stagein.cu) for K items (host bytes, device dst pointer, tokens, pos0)
+    with the raw-K restore transform, and V items (host bytes, device dst pointer)."""
+    nk, nv = len(k_items), len(v_items)
+    keep = [np.ascontiguousarray(x[0], np.uint8) for x in k_items] + [np.ascontiguousarray(x[0], np.uint8)
+                                                                       for x in v_items]
+    vp = C.c_void_p * max(1, nk)
+    ks = vp(*[a.ctypes.data for a in keep[:nk]])
+    kd = vp(*[x[1] for x in k_items])
+    kb = np.array([a.size for a in keep[:nk]] or [0], np.uint64)
+    kt = np.array([x[2] for x in k_items] or [0], np.int64)
+    kp = np.array([x[3] for x in k_items] or [0], np.int32)
+    wp = C.c_void_p * max(1, nv)
+    vs = wp(*[a.ctypes.data for a in keep[nk:]])
+    vd = wp(*[x[1] for x in v_items])
+    vb = np.array([a.size for a in keep[nk:]] or [0], np.uint64)
+    th = np.ascontiguousarray(list(theta) if theta is not None and len(theta) else [0.0], np.float32)
+    rc = ref_cuda().kvref_stagein(ktype, nk, C.cast(ks, C.POINTER(C.c_void_p)), kb, C.cast(kd, C.POINTER(C.c_void_p)),
+                                  kt, kp, n_head * dim, nrot, n_head, dim, n_rot, th,
+                                  n_rot // 2 if theta is not None else 0, nv, C.cast(vs, C.POINTER(C.c_void_p)), vb,
+                                  C.cast(vd, C.POINTER(C.c_void_p)))
+    if rc:
+        raise ValueError(f"reference stage-in refused (rc={rc})")
 
 
 def row_bytes(ktype: int, dim: int) -> int:

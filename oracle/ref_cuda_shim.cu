@@ -11,7 +11,10 @@
 //    normalize / average at :59-121), built against oracle/ggml_stub;
 //  * kvmem::PageSoftmaxCuda::score — the Mean-K page softmax
 //    (kvmem/src/cuda/page_softmax.cu:202-280) over a RawKvStore of per-page
-//    K sums.
+//    K sums;
+//  * kvmem_stagein_enqueue_k / _v + kvmem_stagein_flush — the stage-in route
+//    with the raw-K restore transform (src/adapter/llama-kvmem-stagein.cu:
+//    104-234, 673-881), run on this thread's own execution state.
 //
 // The product never links this file. Exceptions become status codes:
 // 0 ok, 1 std::invalid_argument, 2 any other exception, 3 score() returned
@@ -19,6 +22,8 @@
 #include "ggml-backend.h"
 #include "ggml.h"
 #include "llama-kvmem-attention-cuda.h"
+#include "llama-kvmem-execution.h"
+#include "llama-kvmem-stagein.h"
 
 #include "kvmem/graph_recall.hpp"
 #include "kvmem/page_softmax_cuda.hpp"
@@ -174,4 +179,52 @@ void kvref_cuda_release(void) {
     meank_scorers().clear();
 }
 
+int64_t ggml_time_us(void) {
+    return std::chrono::duration_cast<std::chrono::microseconds>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+void ggml_backend_tensor_set(struct ggml_tensor* tensor, const void* data, size_t offset, size_t size) {
+    std::memcpy(static_cast<uint8_t*>(tensor->data) + offset, data, size);
+}
+
+bool ggml_backend_buffer_is_host(ggml_backend_buffer_t) { return true; }
+
+// The reference's stage-in route for one batch of K items (raw-K restore:
+// dequant -> NeoX RoPE -> Walsh-Hadamard -> requant into dst) and V items
+// (byte copies): enqueue each, flush, synchronise. k_src / v_src are host bytes
+// (the reference copies them into its pinned slab), dst device memory. type:
+// 3 = q8_0, 4 = q4_0 (this repository's kvm_type). Returns 0, or 3 when the
+// reference refused an item or a step failed.
+int kvref_stagein(int type, uint32_t n_k, const uint8_t* const* k_src, const uint64_t* k_bytes,
+                  uint8_t* const* k_dst, const int64_t* k_tokens, const int32_t* k_pos0, int64_t n_embd, int nrot,
+                  int n_head, int n_embd_head, int n_rot_rope, const float* theta, int n_theta, uint32_t n_v,
+                  const uint8_t* const* v_src, const uint64_t* v_bytes, uint8_t* const* v_dst) {
+    return guarded([&] {
+        const ggml_type ty = type == 3 ? GGML_TYPE_Q8_0 : GGML_TYPE_Q4_0;
+        for (uint32_t i = 0; i < n_k; ++i)
+            if (!kvmem_stagein_enqueue_k(ty, k_src[i], k_bytes[i], k_dst[i], k_tokens[i], n_embd, nrot, n_head,
+                                         n_embd_head, n_rot_rope, k_pos0[i], theta, n_theta, nullptr, nullptr,
+                                         nullptr, nullptr))
+                return 3;
+        for (uint32_t i = 0; i < n_v; ++i)
+            if (!kvmem_stagein_enqueue_v(v_src[i], v_bytes[i], v_dst[i], nullptr)) return 3;
+        if (!kvmem_stagein_flush(nullptr, nullptr, nullptr, nullptr)) return 3;
+        return kvmem_stagein_sync_checked() ? 0 : 3;
+    });
+}
+
 }  // extern "C"
+
+// The engine's side of the execution state, as the stage-in code reaches it:
+// one state per host thread here, with its GPU staging created on first use.
+struct kvmem_conv_pool {};
+llama_kvmem_execution_state::llama_kvmem_execution_state() = default;
+llama_kvmem_execution_state::~llama_kvmem_execution_state() = default;
+llama_kvmem_execution_state& kvmem_current_execution() {
+    static thread_local llama_kvmem_execution_state state;
+    if (!state.gpu) state.gpu = kvmem_gpu_state_create();
+    return state;
+}
+void kvmem_record_transfer(int, uint64_t) {}

@@ -132,3 +132,42 @@ def test_beyond_tc_range_uses_mma_kernel(ctx, monkeypatch):
     """256 vectors per KV head: the default scorer falls back to the mma.sync kernel, still exact."""
     monkeypatch.setenv("KVM_SCORER", "auto")
     run_case(ctx, ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320)
+
+
+@pytest.mark.parametrize("case", [dict(D=128, Hq=40, Hkv=8, R=32, page=128, T=1024, L=2),
+                                  dict(D=128, Hq=40, Hkv=8, R=4, page=128, T=700, L=1),
+                                  dict(D=64, Hq=16, Hkv=4, R=8, page=64, T=1000, L=3, cap=1088),
+                                  dict(D=128, Hq=24, Hkv=4, R=4, page=256, T=2048, L=2)],
+                         ids=["160v", "20v_partial", "d64_3layers", "page256"])
+def test_head_major_mirror_matches_oracle(ctx, case):
+    """A head-major K score mirror ([layer][kv_head][token][D]: each head's rows contiguous)
+    scored by the tcgen05 kernel equals the FP64 oracle on the token-major bytes; the other
+    scorers reject that layout (KVM_ERR_UNSUPPORTED)."""
+    import kvmem_b200 as K
+    from kvmem_b200 import _abi as A
+    D, Hq, Hkv, R, page, T, L = (case[k] for k in ("D", "Hq", "Hkv", "R", "page", "T", "L"))
+    cap = case.get("cap", -(-T // page) * page)
+    rng = np.random.default_rng(D + R + L)
+    kb = U.make_k(rng, U.F16, L, cap, Hkv, D)  # token-major bytes [L][cap][Hkv][row]
+    qb = U.make_q(rng, U.F32, L, R, Hq, D)
+    dev = torch.device("cuda", 0)
+    rb = U.row_bytes(U.F16, D)
+    mirror = torch.from_numpy(np.ascontiguousarray(kb.transpose(0, 2, 1, 3)).reshape(-1)).to(dev)
+    kc = A.KCache()
+    kc.data, kc.type = mirror.data_ptr(), U.F16
+    kc.token_stride, kc.head_stride, kc.layer_stride = rb, cap * rb, Hkv * cap * rb
+    kc.capacity_tokens = cap
+    q_d = torch.from_numpy(qb.reshape(-1).copy()).to(dev).view(torch.float32).view(L, R, Hq, D)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=page)
+    rows, _ = ctx.score_pages(desc, K.RecallContext.make_query(q_d, R), kc, want_mean=False)
+    torch.cuda.synchronize()
+    ctx.check_status("head-major")
+    scale = float(np.float32(1) / np.sqrt(np.float32(D)))
+    exp = O.page_mass(qb, U.F32, kb, U.F16, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                      page_tokens=page, scale=scale, k_strides=(cap * Hkv * rb, Hkv * rb, rb))
+    ok, worst, nbad = U.close(rows.cpu().numpy(), exp, REL, ABS)
+    assert ok, f"{nbad} pages off, worst {worst:.3g}"
+    one = K.RecallContext.make_query(q_d, 1, strides=(R * Hq * D * 4, Hq * D * 4, D * 4))  # too few vectors
+    with pytest.raises(K.KvmError) as e:
+        ctx.score_pages(desc, one, kc, want_mean=False)
+    assert e.value.code == A.ERR_UNSUPPORTED
