@@ -31,6 +31,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstdint>
 #include <cstring>
@@ -203,6 +204,18 @@ int kvref_stagein(int type, uint32_t n_k, const uint8_t* const* k_src, const uin
                   const uint8_t* const* v_src, const uint64_t* v_bytes, uint8_t* const* v_dst) {
     return guarded([&] {
         const ggml_type ty = type == 3 ? GGML_TYPE_Q8_0 : GGML_TYPE_Q4_0;
+        // The engine sizes the route's scratch before it enqueues a block
+        // (src/adapter/llama-memory-kvmem.cpp:4470-4473): f32 rows of the
+        // largest item, packed bytes of the largest record (at least one
+        // 32 MiB slab, which also pins the two host slabs).
+        int64_t max_tokens = 1;
+        uint64_t max_bytes = 1;
+        for (uint32_t i = 0; i < n_k; ++i) {
+            max_tokens = std::max(max_tokens, k_tokens[i]);
+            max_bytes = std::max(max_bytes, k_bytes[i]);
+        }
+        for (uint32_t i = 0; i < n_v; ++i) max_bytes = std::max(max_bytes, v_bytes[i]);
+        if (!kvmem_stagein_gpu_ready(size_t(max_tokens) * size_t(n_embd), size_t(max_bytes))) return 3;
         for (uint32_t i = 0; i < n_k; ++i)
             if (!kvmem_stagein_enqueue_k(ty, k_src[i], k_bytes[i], k_dst[i], k_tokens[i], n_embd, nrot, n_head,
                                          n_embd_head, n_rot_rope, k_pos0[i], theta, n_theta, nullptr, nullptr,
