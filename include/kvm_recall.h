@@ -198,6 +198,25 @@ int kvm_select_topk(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint32_t 
                     const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
                     uint32_t* out_ids, uint32_t* out_n, uint32_t out_stride, void* stream);
 
+/* kvm_select_topk with the store's media groups. Replaces
+ * KvMemStore::pick_scored_blocks (kvmem/src/host/kvmem_store.cpp:418-451)
+ * with its media-group closure scored_media_group (:18-32), candidates = all
+ * pages of the row: a page is admitted only together with its whole group (the
+ * pages covered by a chain of overlapping media ranges, or the page alone).
+ *   ranges: host u32 [nranges][2], token ranges [begin, end) of the media
+ *   items; block_tokens: tokens per page.
+ *   Keep pages first, each with its group, in the given order (an
+ *   out-of-range keep is KVM_ERR_INVALID_ARGUMENT, groups that overflow
+ *   `budget` KVM_ERR_BUDGET_EXCEEDED, both before any launch); then groups in
+ *   the order of their best page by (score desc, page id desc), each kept if
+ *   it still fits the budget and skipped otherwise; output ascending.
+ * pages <= 16384 (else KVM_ERR_LENGTH). Other arguments, outputs and the
+ * non-finite rule as kvm_select_topk. */
+int kvm_select_topk_media(kvm_ctx* ctx, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
+                          const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
+                          uint32_t block_tokens, const uint32_t* ranges, uint32_t nranges, uint32_t* out_ids,
+                          uint32_t* out_n, uint32_t out_stride, void* stream);
+
 /* ------------------------------------------------ post-scoring fusion */
 
 /* Attention-feedback graph (kvmem::GraphSnapshot, kvmem/include/kvmem/graph_recall.hpp:47-99)

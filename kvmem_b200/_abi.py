@@ -124,6 +124,8 @@ SIGNATURES = {
     "kvm_score_pages_noalloc": ([C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _vp, _vp, _vp], _i),
     "kvm_select_topk": ([_vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _i, _vp, _vp, _u32, _vp],
                         _i),
+    "kvm_select_topk_media": ([_vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _i, _u32,
+                               C.POINTER(C.c_uint32), _u32, _vp, _vp, _u32, _vp], _i),
     "kvm_pool_create": ([_vp, _u32, _u32, _u32, C.POINTER(C.c_void_p)], _i),
     "kvm_pool_destroy": ([_vp], _i),
     "kvm_pool_reset": ([_vp, _vp], _i),

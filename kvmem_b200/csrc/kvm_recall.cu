@@ -181,7 +181,7 @@ struct LseConfig {
     bool tc = false;
     bool head_major = false;  // K is a head-major mirror (only the tcgen05 scorer reads it)
     int tc_ka = 0, tc_lm = 0;
-    uint32_t tc_stages = 0;
+    uint32_t tc_stages = 0, tc_pass_nv = 0;  // tc_pass_nv: vectors per launch (the last may have fewer)
     size_t tc_smem = 0;
 };
 
@@ -198,20 +198,28 @@ bool scorer_is(const char* name) {
 }
 bool force_simt() { return scorer_is("simt"); }
 
-// tcgen05 scorer: fp16 K, head_dim 64 / 128, 16..160 query vectors per KV
-// head (rows x group), pages of 32 / 64 / 128 tokens or multiples of 128, a
-// token range addressable by 32-bit TMA coordinates, and room for at least
-// two K stages next to the query tiles.
+// tcgen05 scorer: fp16 K, head_dim 64 / 128 / 256, 16 or more query vectors
+// per KV head (rows x group), pages of 32 / 64 / 128 tokens or multiples of
+// 128, a token range addressable by 32-bit TMA coordinates, and room for at
+// least two K stages next to the query tiles. One launch scores up to 160
+// vectors (128 at head_dim 256, whose query operand leaves no shared memory
+// for a packed second tile); more are split into equal passes, each reading K
+// once, so a batch of sampled rows costs ceil(vectors / 160) reads of K rather
+// than the mma.sync kernel's ceil(vectors / 8).
 void plan_tc(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, LseConfig* cfg) {
     if (force_simt() || scorer_is("mma")) return;
-    if (k->type != KVM_F16 || (d->head_dim != 64 && d->head_dim != 128)) return;
+    if (k->type != KVM_F16 || (d->head_dim != 64 && d->head_dim != 128 && d->head_dim != 256)) return;
     const uint64_t nv = uint64_t(q->rows) * (d->q_heads / d->kv_heads);
-    if (nv < 16 || nv > kTcMaxVectors) return;
+    if (nv < 16) return;
     const uint32_t pt = d->page_tokens;
     if (pt % 32 || (pt < 128 && 128 % pt) || (pt > 128 && pt % 128)) return;
     const uint64_t pages = (d->tokens + pt - 1) / pt;
     if (pages * pt + 128 > 0x7fffffffull) return;
-    const int ka = int(d->head_dim / 64), lm = tc_layout_for(uint32_t(nv));
+    const int ka = int(d->head_dim / 64);
+    const uint64_t per_launch = ka == 4 ? uint64_t(kTcTile) : uint64_t(kTcMaxVectors);
+    const uint64_t passes = (nv + per_launch - 1) / per_launch;
+    const uint32_t pass_nv = uint32_t((nv + passes - 1) / passes);
+    const int lm = tc_layout_for(pass_nv);
     const size_t fixed = tc_smem_bytes(ka, lm, 0);
     const size_t stage = size_t(ka) * kTcAtomBytes;
     if (fixed + 2 * stage > kTcSmemMax) return;
@@ -219,6 +227,7 @@ void plan_tc(const kvm_score_desc* d, const kvm_query* q, const kvm_kcache* k, L
     cfg->tc = true;
     cfg->tc_ka = ka;
     cfg->tc_lm = lm;
+    cfg->tc_pass_nv = pass_nv;
     cfg->tc_stages = stages;
     cfg->tc_smem = tc_smem_bytes(ka, lm, stages);
 }
@@ -555,14 +564,19 @@ int lse_layers(kvm_ctx* c, const kvm_score_desc* d, const kvm_query* q, const kv
     p.status = c->status;
     p.stage_stride = cfg.stage_stride;
     if (cfg.tc) {
-        // All query vectors of a KV head in one pass (one or two M tiles).
+        // The query vectors of a KV head in passes of tc_pass_nv (one or two M
+        // tiles each); a smaller last pass may use the one-tile layout.
         CUtensorMap map;
         KVM_TRY(encode_k_map(d, k, p.k, nl, cfg.head_major, &map));
         p.head_major = cfg.head_major;
         p.stages = cfg.tc_stages;
-        p.v0 = 0;
-        p.nv = nvt;
-        return launch_lse_tc(c, map, p, cfg.tc_ka, cfg.tc_lm, cfg.tc_smem, s);
+        for (uint32_t v0 = 0; v0 < nvt; v0 += cfg.tc_pass_nv) {
+            p.v0 = v0;
+            p.nv = std::min<uint32_t>(cfg.tc_pass_nv, nvt - v0);
+            const int lm = tc_layout_for(p.nv);
+            KVM_TRY(launch_lse_tc(c, map, p, cfg.tc_ka, lm, tc_smem_bytes(cfg.tc_ka, lm, cfg.tc_stages), s));
+        }
+        return KVM_OK;
     }
     if (cfg.q) {
         // Passes of up to 8 query vectors, as the mma.sync kernel below.
@@ -878,6 +892,60 @@ int kvm_select_topk(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pa
     DeviceGuard guard(c->device);
     return select_rows(c, scores, nrows, pages, score_stride, keep, nkeep, budget, signed_scores, out_ids, out_n,
                        out_stride, static_cast<cudaStream_t>(stream));
+}
+
+int kvm_select_topk_media(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
+                          const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
+                          uint32_t block_tokens, const uint32_t* ranges, uint32_t nranges, uint32_t* out_ids,
+                          uint32_t* out_n, uint32_t out_stride, void* stream) {
+    if (!c || !scores || !out_ids || !out_n || !nrows || !pages || !budget || !block_tokens)
+        return KVM_ERR_INVALID_ARGUMENT;
+    if ((nkeep && !keep) || (nranges && !ranges)) return KVM_ERR_INVALID_ARGUMENT;
+    if (pages > kMediaMaxPages) return KVM_ERR_LENGTH;
+    if (score_stride < pages || out_stride < std::min(budget, pages)) return KVM_ERR_INVALID_ARGUMENT;
+    // Media groups: each range covers pages [first / block, ceil(second / block)) (clipped
+    // to the row); chains of strictly overlapping spans merge into one group, which is
+    // what scored_media_group's fixed point reaches from any page inside them.
+    std::vector<std::pair<uint32_t, uint32_t>> spans;
+    for (uint32_t i = 0; i < nranges; ++i) {
+        const uint32_t lo = ranges[2 * i] / block_tokens;
+        const uint32_t hi = uint32_t(std::min<uint64_t>(pages, (uint64_t(ranges[2 * i + 1]) + block_tokens - 1) /
+                                                                   block_tokens));
+        if (lo < hi) spans.emplace_back(lo, hi);
+    }
+    std::sort(spans.begin(), spans.end());
+    std::vector<uint32_t> group(pages);
+    for (uint32_t p = 0; p < pages; ++p) group[p] = p | ((p + 1) << 15);
+    for (size_t i = 0; i < spans.size();) {
+        uint32_t b = spans[i].first, e = spans[i].second;
+        size_t j = i + 1;
+        for (; j < spans.size() && spans[j].first < e; ++j) e = std::max(e, spans[j].second);
+        for (uint32_t p = b; p < e; ++p) group[p] = b | (e << 15);
+        i = j;
+    }
+    // Keep pages first, each with its whole group, in the caller's order.
+    uint32_t count = 0;
+    for (uint32_t i = 0; i < nkeep; ++i) {
+        if (keep[i] >= pages) return KVM_ERR_INVALID_ARGUMENT;
+        const uint32_t b = group[keep[i]] & 0x7fffu, e = (group[keep[i]] >> 15) & 0x7fffu;
+        uint32_t need = 0;
+        for (uint32_t p = b; p < e; ++p) need += !(group[p] >> 30);
+        if (count + need > budget) return KVM_ERR_BUDGET_EXCEEDED;
+        for (uint32_t p = b; p < e; ++p) group[p] |= 1u << 30;
+        count += need;
+    }
+    DeviceGuard guard(c->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    KVM_TRY(ensure_aux(c, size_t(pages) * 4));
+    KVM_CUDA(cudaMemcpyAsync(c->aux, group.data(), size_t(pages) * 4, cudaMemcpyHostToDevice, s));
+    const size_t smem = media_smem_bytes(pages);
+    KVM_CUDA(smem_attr(reinterpret_cast<const void*>(select_topk_media_kernel), int(media_smem_bytes(kMediaMaxPages))));
+    select_topk_media_kernel<<<nrows, kMediaThreads, smem, s>>>(scores, pages, score_stride,
+                                                                static_cast<const uint32_t*>(c->aux), count, budget,
+                                                                signed_scores, out_ids, out_n, out_stride, c->status);
+    ++c->launches;
+    KVM_CUDA(cudaGetLastError());
+    return KVM_OK;
 }
 
 int kvm_pool_create(kvm_ctx* c, uint32_t rows, uint32_t pages, uint32_t slots, kvm_pool** out) {

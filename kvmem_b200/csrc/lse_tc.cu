@@ -1,7 +1,7 @@
 // Launcher of the tcgen05 page log-sum-exp kernel (page_mass_tc.cuh):
-// head_dim 64 / 128 (one or two 64-dim swizzle atoms), query-tile layout 1 / 2
-// (one M tile, plus a packed second tile), with or without an additive
-// attention mask.
+// head_dim 64 / 128 / 256 (one, two or four 64-dim swizzle atoms), query-tile
+// layout 1 / 2 (one M tile, plus a packed second tile; head_dim 256 has layout
+// 1 only), with or without an additive attention mask.
 #include "lse_launch.cuh"
 #include "page_mass_tc.cuh"
 
@@ -43,6 +43,7 @@ int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka
                   cudaStream_t s) {
     if (ka == 1) return launch_tc_l<1>(c, map, p, lm, smem, s);
     if (ka == 2) return launch_tc_l<2>(c, map, p, lm, smem, s);
+    if (ka == 4 && lm == 1) return launch_tc_m<4, 1>(c, map, p, smem, s);  // head_dim 256: one M tile only
     return KVM_ERR_UNSUPPORTED;
 }
 

@@ -1,7 +1,7 @@
 // Per-token page mass, first pass, on the 5th-generation tensor cores
 // (tcgen05): page log-sum-exp of 16..256 query vectors per KV head (query
 // replay / multi-lane batching turn the scoring into a real Q.K^T contraction),
-// fp16 keys, head_dim 64 or 128.
+// fp16 keys, head_dim 64, 128 or 256 (256: up to 128 vectors per launch).
 //
 // Same result as page_lse_kernel (page_mass.cuh) and page_lse_mma_kernel
 // (page_mass_mma.cuh). One CTA per SM walks a contiguous range of units
@@ -138,12 +138,16 @@ __host__ __device__ constexpr int tc_layout_for(uint32_t nv) { return nv <= 128 
 constexpr uint32_t kTcMaxVectors = 160;
 
 // Tensor-memory columns (512 allocated). Layout 1: tile-0 accumulators triple
-// buffered at [0, 384), the tile-0 query operand (fp16 hi at [384, 384 + D/2),
-// lo after it) at the top. Layout 2: tile-0 accumulators double buffered at
-// [0, 256), the packed tile's accumulators double buffered at [256, 384) and
-// [384, 512); the tile-0 query operand lives in shared memory.
+// buffered at [0, 384) and the tile-0 query operand (fp16 hi at [384, 384 + D/2),
+// lo after it) at the top; at head_dim 256 the operand takes 256 columns, so the
+// accumulators are double buffered at [0, 256) and the operand sits at
+// [256, 512). Layout 2: tile-0 accumulators double buffered at [0, 256), the
+// packed tile's accumulators double buffered at [256, 384) and [384, 512); the
+// tile-0 query operand lives in shared memory.
 constexpr uint32_t kTcColPacked = 256;
-constexpr uint32_t kTcColQ = 384;
+__host__ __device__ constexpr uint32_t tc_col_q(int KA) { return KA <= 2 ? 384u : 256u; }
+// Tile-0 accumulator buffers.
+__host__ __device__ constexpr uint32_t tc_acc_buffers(int KA, int LM) { return LM == 1 && KA <= 2 ? 3u : 2u; }
 
 // Shared memory of the query operands of layout 2: the packed tile (KA atoms),
 // then the tile-0 hi parts (KA atoms) and lo parts (KA atoms).
@@ -388,8 +392,9 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
     constexpr uint32_t kQBytes = tc_q_bytes(KA, LM);
     constexpr uint32_t kStageBytes = KA * kTcAtomBytes;
     constexpr uint32_t kCols = 512;
-    // Tile-0 accumulator buffers: three when no packed tile needs columns.
-    constexpr uint32_t NB = LM == 1 ? 3 : 2;
+    // Tile-0 accumulator buffers: three when neither a packed tile nor a
+    // head_dim-256 query operand needs their columns.
+    constexpr uint32_t NB = tc_acc_buffers(KA, LM);
     extern __shared__ uint8_t smem_raw[];
     const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint8_t* qsm = smem_raw + pad;                 // packed query tile (layout 2)
@@ -412,7 +417,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
     volatile uint32_t* lo_any = reinterpret_cast<volatile uint32_t*>(tmem_slot + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t V = P.nv;  // query vectors per KV head (rows * group)
+    const uint32_t V = P.nv;  // query vectors per KV head in this pass (vectors P.v0 .. P.v0 + V - 1)
     const uint32_t warps0 = (min(V, 128u) + 31) / 32;                  // active tile-0 epilogue warps
     const uint32_t warps1 = LM == 2 ? (V - 128 + 7) / 8 : 0;          // active packed epilogue warps
     if (tid == 0) {
@@ -567,7 +572,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
                     const uint32_t kbase = smem_u32(ksm + s * kStageBytes);
                     const uint32_t d0 = tmem + b * kTcTile;
                     if constexpr (LM == 1) {
-                        const uint32_t qhi = tmem + kTcColQ, qlo = tmem + kTcColQ + D / 2;
+                        const uint32_t qhi = tmem + tc_col_q(KA), qlo = tmem + tc_col_q(KA) + D / 2;
 #pragma unroll
                         for (int a = 0; a < KA; ++a)
 #pragma unroll
@@ -638,7 +643,8 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
         const bool warp_active = packed ? kTcTile + 8 * q < V : 32u * q < V;
         if (warp_active) {
             const bool vvalid = v < V;
-            const uint32_t r = vvalid ? v / G : 0, gsub = vvalid ? v % G : 0;
+            // This pass's vector v is vector P.v0 + v = (row r, head gsub of the group).
+            const uint32_t r = vvalid ? (P.v0 + v) / G : 0, gsub = vvalid ? (P.v0 + v) % G : 0;
             const TcSlowArgs sa{P.tokens, P.scale, P.softcap, P.mask, P.mask_type, P.mask_row};
             // Page ends: pages of <= 128 tokens end every cpp = page_tokens / 32
             // chunks (a power of two) inside a tile; larger pages at the last
@@ -646,7 +652,7 @@ __global__ void __launch_bounds__(tc_threads(LM), 1) page_lse_tc_kernel(const __
             const bool small_pages = P.page_tokens <= uint32_t(kTcTile);
             const uint32_t cpp_log = small_pages ? (P.page_tokens == 32 ? 0 : P.page_tokens == 64 ? 1 : 2) : 2;
             const uint32_t ppt = small_pages ? kTcTile / P.page_tokens : 1;
-            const uint32_t qbase = tmem + (uint32_t(32 * q) << 16) + kTcColQ;
+            const uint32_t qbase = tmem + (uint32_t(32 * q) << 16) + tc_col_q(KA);
             uint32_t it = 0, nq = 0, tb = 0, tround = 0;
             float cvt = 0.f, qinv = 1.f;
             TcLse st;

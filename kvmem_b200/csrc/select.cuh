@@ -125,4 +125,112 @@ __global__ void __launch_bounds__(kSelectThreads) select_topk_kernel(
     if (tid == 0) out_n[row] = written;
 }
 
+// ---------------------------------------------------------------- media groups
+//
+// Same result as KvMemStore::pick_scored_blocks (kvmem_store.cpp:418-451)
+// with candidates = every page of the row and the store's media ranges: a page
+// is admitted only together with its whole media group (the closure
+// scored_media_group, kvmem_store.cpp:18-32, computes it: the pages covered by
+// a chain of overlapping media ranges, or the page alone). Groups are disjoint
+// intervals, so a group is decided once, at its best-ranked page: kept when it
+// still fits the budget, skipped for good otherwise (its later pages find the
+// same need and a count that only grew).
+//
+// group[p] (host-built): bits 0-14 first page of p's group, bits 15-29 one past
+// its last page, bit 30 set when a keep page's group covers p (the host admits
+// those groups first, in keep order, and rejects a list that overflows the
+// budget before any launch). One CTA per row: a bitonic sort of the 64-bit
+// keys (order_key(score) << 32 | page id, descending = score desc then id
+// desc; kept pages get key 0, which no finite score produces) in shared memory,
+// then one thread walks the ranked pages until the budget is full, and the
+// block writes the kept pages in ascending order.
+constexpr uint32_t kMediaMaxPages = 16384;
+constexpr int kMediaThreads = 512;
+
+__host__ __device__ inline size_t media_smem_bytes(uint32_t pages) {
+    uint32_t n = 1;
+    while (n < pages) n <<= 1;
+    return size_t(n) * 8 + pages;
+}
+
+__global__ void __launch_bounds__(kMediaThreads) select_topk_media_kernel(
+    const float* scores, uint32_t pages, uint32_t score_stride, const uint32_t* group, uint32_t kept0,
+    uint32_t budget, int signed_scores, uint32_t* out_ids, uint32_t* out_n, uint32_t out_stride,
+    DeviceStatus* status) {
+    extern __shared__ uint64_t keys[];  // [npow2], then kept flags [pages]
+    __shared__ uint32_t warp_sums[32];
+    __shared__ uint32_t sh_bad;
+    uint32_t npow2 = 1;
+    while (npow2 < pages) npow2 <<= 1;
+    uint8_t* kept = reinterpret_cast<uint8_t*>(keys + npow2);  // 0 no, 1 kept, 2 group skipped (at its first page)
+    const uint32_t row = blockIdx.x;
+    const float* sc = scores + uint64_t(row) * score_stride;
+    const int tid = threadIdx.x;
+    if (tid == 0) sh_bad = 0;
+    __syncthreads();
+    for (uint32_t p = tid; p < npow2; p += blockDim.x) {
+        uint64_t key = 0;
+        if (p < pages) {
+            const float s = sc[p];
+            if (!isfinite(s) || (!signed_scores && s < 0.f)) sh_bad = 1;
+            const bool k = (group[p] >> 30) & 1u;
+            kept[p] = k ? 1 : 0;
+            if (!k) key = (uint64_t(order_key(s)) << 32) | p;
+        }
+        keys[p] = key;
+    }
+    __syncthreads();
+    if (sh_bad) {
+        if (tid == 0) {
+            record_error(status, KVM_ERR_NONFINITE, 11);
+            out_n[row] = 0;
+        }
+        return;
+    }
+    // Bitonic sort, descending.
+    for (uint32_t k = 2; k <= npow2; k <<= 1)
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = tid; i < npow2; i += blockDim.x) {
+                const uint32_t ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t a = keys[i], b = keys[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? a < b : a > b) {
+                        keys[i] = b;
+                        keys[ixj] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    if (tid == 0) {
+        uint32_t count = kept0;
+        for (uint32_t i = 0; i < pages && count < budget; ++i) {
+            const uint64_t key = keys[i];
+            if (key == 0) break;  // only kept pages (and padding) remain
+            const uint32_t p = uint32_t(key & 0xffffffffu), g = group[p];
+            const uint32_t b = g & 0x7fffu, e = (g >> 15) & 0x7fffu;
+            if (kept[b] != 0) continue;  // the group was decided at a better-ranked page
+            const uint32_t need = e - b;
+            if (count + need <= budget) {
+                for (uint32_t q = b; q < e; ++q) kept[q] = 1;
+                count += need;
+            } else {
+                kept[b] = 2;
+            }
+        }
+    }
+    __syncthreads();
+    uint32_t written = 0;
+    for (uint32_t base = 0; base < pages; base += blockDim.x) {
+        const uint32_t p = base + tid;
+        const uint32_t f = (p < pages && kept[p] == 1) ? 1u : 0u;
+        uint32_t pre;
+        const uint32_t tot = block_exclusive_scan(f, warp_sums, &pre);
+        if (f) out_ids[uint64_t(row) * out_stride + written + pre] = p;
+        written += tot;
+    }
+    if (tid == 0) out_n[row] = written;
+}
+
 }  // namespace kvmb

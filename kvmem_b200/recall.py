@@ -157,6 +157,25 @@ class RecallContext:
         A.check(rc, "kvm_select_topk")
         return out_ids, out_n
 
+    def select_topk_media(self, scores: torch.Tensor, keep: Sequence[int], budget: int, *, block_tokens: int,
+                          media_ranges: Sequence[tuple], signed: bool = False, stream=None):
+        """select_topk with media groups (KvMemStore::pick_scored_blocks with the store's
+        media ranges, token [begin, end) pairs; pages of block_tokens tokens)."""
+        assert scores.dtype == torch.float32 and scores.dim() == 2
+        nrows, pages = scores.shape
+        width = min(budget, pages)
+        out_ids = torch.zeros((nrows, width), dtype=torch.int32, device=scores.device)
+        out_n = torch.zeros((nrows,), dtype=torch.int32, device=scores.device)
+        kp = (C.c_uint32 * max(1, len(keep)))(*keep)
+        flat = [int(x) for r in media_ranges for x in r]
+        rg = (C.c_uint32 * max(1, len(flat)))(*flat)
+        rc = self.lib.kvm_select_topk_media(self.h, scores.data_ptr(), nrows, pages, scores.stride(0), kp, len(keep),
+                                            budget, int(signed), block_tokens, rg, len(media_ranges),
+                                            out_ids.data_ptr(), out_n.data_ptr(), out_ids.stride(0),
+                                            _stream_ptr(stream))
+        A.check(rc, "kvm_select_topk_media")
+        return out_ids, out_n
+
     def restore_k(self, ktype: int, items: Sequence[tuple], *, n_head: int, head_dim: int, n_rot: int = 0,
                   theta: Optional[Sequence[float]] = None, nrot: int = 0, stream=None) -> None:
         """items: (src_ptr, dst_ptr, tokens, pos0) -> kvm_restore_k (raw-K restore transform)."""

@@ -10,8 +10,9 @@ decode step on every rank (include/kvm_recall.h, "page-range sharding"):
   4. local top-B candidates (B = budget - keep pages)     kvm_shard_candidates
   5. all-gather of the candidates, global top-k           kvm_shard_merge
 
-The collectives are plain all-gathers of small tensors (NCCL over NVLink on
-GPUs); every rank ends with the same selection, equal to a top-k over the
+The collectives are two plain all-gathers of small tensors per step (the
+statistics; the candidates' scores and ids side by side), NCCL over NVLink on
+GPUs; every rank ends with the same selection, equal to a top-k over the
 whole row. The compute steps are injected (`ShardCompute`), so the exchange
 logic can run with CPU stand-ins on gloo ranks.
 """
@@ -129,6 +130,18 @@ class ShardedSelector:
         dist.all_gather(parts, t, group=self.group)
         return torch.stack(parts)
 
+    def _all_gather_pair(self, a: torch.Tensor, b: torch.Tensor):
+        """All-gathers two tensors in one collective (their bytes side by side)."""
+        if self.world == 1:
+            return a.unsqueeze(0).contiguous(), b.unsqueeze(0).contiguous()
+        a, b = a.contiguous(), b.contiguous()
+        na = a.numel() * a.element_size()
+        packed = torch.cat([a.reshape(-1).view(torch.uint8), b.reshape(-1).view(torch.uint8)])
+        g = self._all_gather(packed)  # [world][bytes]
+        ga = g[:, :na].contiguous().view(a.dtype).view((self.world,) + tuple(a.shape))
+        gb = g[:, na:].contiguous().view(b.dtype).view((self.world,) + tuple(b.shape))
+        return ga, gb
+
     def select(self, desc, q, k, geo: ShardGeometry, keep: Sequence[int], budget: int):
         """Returns (ids [sel_rows][budget] int32, n [sel_rows] int32), identical on every rank."""
         keep = sorted(set(int(x) for x in keep))
@@ -139,7 +152,7 @@ class ShardedSelector:
         global_stats = self.compute.merge_stats(self._all_gather(stats), self.world, geo)
         mass = self.compute.finish(desc, geo, global_stats)
         cs, ci = self.compute.candidates(mass, geo, keep, kcand)
-        gs, gi = self._all_gather(cs), self._all_gather(ci)
+        gs, gi = self._all_gather_pair(cs, ci)
         return self.compute.merge(gs, gi, self.world, geo, keep, kcand, budget)
 
 
@@ -176,10 +189,12 @@ class ShardedRecall:
         self.ids = torch.zeros((geo.sel_rows, 1), dtype=torch.int32, device=dev)
         self.n = torch.zeros((geo.sel_rows,), dtype=torch.int32, device=dev)
 
-    def step(self, desc, q: torch.Tensor, k, keep: Sequence[int], budget: int, *, force_reload: bool = False):
+    def step(self, desc, q: torch.Tensor, k, keep: Sequence[int], budget: int, *, force_reload: bool = False,
+             stage: bool = True):
         """desc: the whole step's kvm_score_desc (global token count); q: [L][R][Hq][D] device
         queries; k: kvm_kcache of this rank's pages for all layers. Returns (ids, n) of all
-        selection rows ([L*groups][budget], [L*groups]), identical on every rank."""
+        selection rows ([L*groups][budget], [L*groups]), identical on every rank. stage=False
+        runs the selection alone (same collectives; no residency plan, no stage-in)."""
         from .recall import RecallContext
         g = self.geo
         if self.ids.shape[1] != budget:
@@ -197,6 +212,8 @@ class ShardedRecall:
             r0, nr = l0 * g.groups, nl * g.groups
             self.ids[r0:r0 + nr].copy_(ids)
             self.n[r0:r0 + nr].copy_(n)
+            if not stage:
+                continue
             self.pools[ci].plan(ids, n, force_reload=force_reload)
             self.events[ci].record(main)
             self.side.wait_event(self.events[ci])

@@ -209,10 +209,13 @@ def ref_stagein(ktype: int, k_items, *, n_head: int, dim: int, n_rot: int = 0, t
     vs = wp(*[a.ctypes.data for a in keep[nk:]])
     vd = wp(*[x[1] for x in v_items])
     vb = np.array([a.size for a in keep[nk:]] or [0], np.uint64)
-    th = np.ascontiguousarray(list(theta) if theta is not None and len(theta) else [0.0], np.float32)
+    # The route rotates every K item and refuses to run without a device theta table
+    # (rope_from_dev, llama-kvmem-stagein.cu:557-569); with n_rot = 0 the table is never read,
+    # so a one-element placeholder stands in for the engine's frequencies.
+    th = np.ascontiguousarray(list(theta)[: n_rot // 2] if theta is not None and n_rot else [1.0], np.float32)
     rc = ref_cuda().kvref_stagein(ktype, nk, C.cast(ks, C.POINTER(C.c_void_p)), kb, C.cast(kd, C.POINTER(C.c_void_p)),
                                   kt, kp, n_head * dim, nrot, n_head, dim, n_rot, th,
-                                  n_rot // 2 if theta is not None else 0, nv, C.cast(vs, C.POINTER(C.c_void_p)), vb,
+                                  len(th), nv, C.cast(vs, C.POINTER(C.c_void_p)), vb,
                                   C.cast(vd, C.POINTER(C.c_void_p)))
     if rc:
         raise ValueError(f"reference stage-in refused (rc={rc})")
@@ -435,6 +438,9 @@ def restore_k(ktype: int, src: np.ndarray, *, tokens: int, n_head: int, dim: int
     """Raw-K restore transform of `tokens` packed rows -> (rc, packed output bytes)."""
     src = np.ascontiguousarray(src, np.uint8).reshape(-1)
     dst = np.zeros_like(src)
-    th = np.ascontiguousarray(list(theta) if theta is not None and len(theta) else [0.0], np.float32)
+    # The route rotates every K item and refuses to run without a device theta table
+    # (rope_from_dev, llama-kvmem-stagein.cu:557-569); with n_rot = 0 the table is never read,
+    # so a one-element placeholder stands in for the engine's frequencies.
+    th = np.ascontiguousarray(list(theta)[: n_rot // 2] if theta is not None and n_rot else [1.0], np.float32)
     rc = lib().kvo_restore_k(ktype, src, dst, tokens, n_head, dim, n_rot, pos0, th, nrot)
     return int(rc), dst

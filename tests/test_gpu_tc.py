@@ -1,7 +1,8 @@
 """GPU parity of the tcgen05 page scorer (query replay / multi-lane batching).
 
-The tcgen05 kernel scores 16..160 query vectors per KV head (rows x group)
-against fp16 keys with head_dim 64 or 128. Every case runs twice: with
+The tcgen05 kernel scores 16 or more query vectors per KV head (rows x group)
+against fp16 keys with head_dim 64, 128 or 256: up to 160 vectors per launch
+(128 at head_dim 256), more in equal passes. Every case runs twice: with
 KVM_SCORER=tc, which makes kvm_score_pages fail unless that kernel runs, and
 with KVM_SCORER=mma (the mma.sync kernel) on the same inputs; both are compared
 with the FP64 oracle at the north-star tolerance of 1e-3 relative.
@@ -46,6 +47,17 @@ CASES = [
     # f16 queries on the 129..160-vector layout (the tile-0 lo MMAs are skipped: every lo part is 0)
     dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=32, page=128, T=512, L=2, qtype=U.F16),
     dict(ktype=U.F16, D=64, Hq=40, Hkv=8, R=30, page=64, T=384, qtype=U.BF16),
+    # head_dim 256 (config-2 / 3 / 5 heads, sampled rows): 24 and 126 vectors in one launch
+    dict(ktype=U.F16, D=256, Hq=24, Hkv=4, R=4, page=256, T=2048),
+    dict(ktype=U.F16, D=256, Hq=24, Hkv=4, R=21, page=256, T=1100, L=2),
+    # several passes: 160 vectors at head_dim 256 (2 x 80), 384 (3 x 128), 200 at head_dim 128
+    # (2 x 100) and 256 at head_dim 64 (2 x 128)
+    dict(ktype=U.F16, D=256, Hq=16, Hkv=2, R=20, page=128, T=700, L=2),
+    dict(ktype=U.F16, D=256, Hq=24, Hkv=4, R=64, page=256, T=1024),
+    dict(ktype=U.F16, D=128, Hq=40, Hkv=8, R=40, page=128, T=640),
+    dict(ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320),
+    # head_dim 256 with f16 queries and a softcap
+    dict(ktype=U.F16, D=256, Hq=24, Hkv=4, R=8, page=256, T=1024, qtype=U.F16, softcap=20.0, scale=0.1),
 ]
 
 
@@ -81,12 +93,13 @@ def test_tc_query_magnitudes(ctx, scorer, mag):
     assert ok, f"worst {worst:.3g}, {nbad} pages"
 
 
-def test_tc_mask_and_empty_rows(ctx, scorer):
+@pytest.mark.parametrize("D", [128, 256])
+def test_tc_mask_and_empty_rows(ctx, scorer, D):
     """Additive mask rows on the tcgen05 path: hidden tokens, a causal tail, a
     bias row, and a fully hidden row whose masses are NaN as the reference's."""
     import kvmem_b200 as K
     rng = np.random.default_rng(5)
-    L, R, Hq, Hkv, D, T, page = 1, 8, 16, 4, 128, 640, 128
+    L, R, Hq, Hkv, T, page = 1, 8, 16, 4, 640, 128
     mask = np.zeros((R, T), np.float32)
     mask[0, 100:300] = -np.inf
     mask[1, :] = rng.standard_normal(T).astype(np.float32)
@@ -113,32 +126,37 @@ def test_tc_mask_and_empty_rows(ctx, scorer):
     assert ok, worst
 
 
-@pytest.mark.parametrize("rows", [1, 32])
-def test_tc_strict_mode_rejects_other_shapes(ctx, monkeypatch, rows):
-    """KVM_SCORER=tc refuses shapes outside the tcgen05 kernel: 4 and 256 vectors per KV head."""
+@pytest.mark.parametrize("rows,page", [(1, 64), (32, 96)])
+def test_tc_strict_mode_rejects_other_shapes(ctx, monkeypatch, rows, page):
+    """KVM_SCORER=tc refuses shapes outside the tcgen05 kernel: 8 vectors per KV head
+    (fewer than 16), and pages of 96 tokens (neither a divisor nor a multiple of 128)."""
     import kvmem_b200 as K
     monkeypatch.setenv("KVM_SCORER", "tc")
     dev = torch.device("cuda", 0)
-    k_d = torch.zeros(256 * 2 * 128 * 2, dtype=torch.uint8, device=dev)
+    k_d = torch.zeros(288 * 2 * 128 * 2, dtype=torch.uint8, device=dev)
     q_d = torch.zeros((1, rows, 16, 128), dtype=torch.float32, device=dev)
-    desc = K.RecallContext.make_desc(layers=1, q_heads=16, kv_heads=2, head_dim=128, tokens=256, page_tokens=64)
+    desc = K.RecallContext.make_desc(layers=1, q_heads=16, kv_heads=2, head_dim=128, tokens=288, page_tokens=page)
     with pytest.raises(K.KvmError) as e:
         ctx.score_pages(desc, K.RecallContext.make_query(q_d, rows),
-                        K.RecallContext.make_kcache(k_d, U.F16, kv_heads=2, head_dim=128, capacity_tokens=256))
+                        K.RecallContext.make_kcache(k_d, U.F16, kv_heads=2, head_dim=128, capacity_tokens=288))
     assert e.value.code == K._abi.ERR_UNSUPPORTED
 
 
-def test_beyond_tc_range_uses_mma_kernel(ctx, monkeypatch):
-    """256 vectors per KV head: the default scorer falls back to the mma.sync kernel, still exact."""
+def test_default_scorer_takes_tc_passes_for_large_batches(ctx, monkeypatch):
+    """384 vectors per KV head at head_dim 256 under the default scorer choice: three
+    tcgen05 passes (3 launches of the LSE kernel + the normaliser), still exact."""
     monkeypatch.setenv("KVM_SCORER", "auto")
-    run_case(ctx, ktype=U.F16, D=64, Hq=16, Hkv=2, R=32, page=32, T=320)
+    before = ctx.launches
+    run_case(ctx, ktype=U.F16, D=256, Hq=24, Hkv=4, R=64, page=256, T=768)
+    assert ctx.launches - before == 4
 
 
 @pytest.mark.parametrize("case", [dict(D=128, Hq=40, Hkv=8, R=32, page=128, T=1024, L=2),
                                   dict(D=128, Hq=40, Hkv=8, R=4, page=128, T=700, L=1),
                                   dict(D=64, Hq=16, Hkv=4, R=8, page=64, T=1000, L=3, cap=1088),
-                                  dict(D=128, Hq=24, Hkv=4, R=4, page=256, T=2048, L=2)],
-                         ids=["160v", "20v_partial", "d64_3layers", "page256"])
+                                  dict(D=128, Hq=24, Hkv=4, R=4, page=256, T=2048, L=2),
+                                  dict(D=256, Hq=24, Hkv=4, R=8, page=256, T=2048, L=2)],
+                         ids=["160v", "20v_partial", "d64_3layers", "page256", "d256"])
 def test_head_major_mirror_matches_oracle(ctx, case):
     """A head-major K score mirror ([layer][kv_head][token][D]: each head's rows contiguous)
     scored by the tcgen05 kernel equals the FP64 oracle on the token-major bytes; the other
