@@ -45,6 +45,7 @@ METRIC = "select+stage-in ms/decode step @128K; KV tokens scored/s; % HBM roofli
 UNIT = "KV token-layers/s"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_TFLOPS = 1590.0
+PCIE_PEAK_GBS = 63.0  # pcie__read_bytes at 55.7 GB/s read 88.4% of ncu's pcie__throughput peak
 
 
 def parse():
@@ -56,6 +57,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--chunks", type=int, default=8)
+    ap.add_argument("--chunks-sharded", type=int, default=4,
+                    help="layer chunks of the page-range sharded step (N > 1)")
+    ap.add_argument("--shard-exchange", default="lse", choices=["lse", "candidates"],
+                    help="N > 1: one all-gather of the page LSE per chunk (lse) or statistics + candidates")
     ap.add_argument("--first-layers", type=int, default=2,
                     help="layers of the step's first chunk (starts the stage-in early)")
     ap.add_argument("--kmirror", default="head", choices=["head", "token"],
@@ -158,6 +163,44 @@ def dist_setup(args):
     return world, rank, local
 
 
+class NumaLocal:
+    """Runs the enclosed host work on the CPU cores nearest to GPU `local` (NVML's affinity
+    mask for its PCI address), so pinned host memory first touched there sits on that GPU's
+    NUMA node and its PCIe reads do not cross the socket interconnect. Restores the previous
+    affinity on exit (the pages stay where they were touched). A no-op where NVML or the
+    affinity call is unavailable."""
+
+    def __init__(self, local: int):
+        self.local = local
+        self.saved = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            import torch
+            p = torch.cuda.get_device_properties(self.local)
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+            n = os.cpu_count() or 1
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+            cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+            allowed = os.sched_getaffinity(0)
+            near = cpus & allowed
+            if near and near != allowed:
+                self.saved = allowed
+                os.sched_setaffinity(0, near)
+        except Exception:
+            self.saved = None
+        return self
+
+    def __exit__(self, *a):
+        if self.saved:
+            try:
+                os.sched_setaffinity(0, self.saved)
+            except OSError:
+                pass
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -196,9 +239,11 @@ def build_history(w, seed, device, need_host=True, page_range=None):
     q_base, drift = synth.make_queries(w, seed, device, drift_steps=max(8, 2 * w.rot_groups))
     k_dev = torch.empty(w.layers * layer_k, dtype=torch.uint8, device=device)
     host_k = host_v = None
+    numa = NumaLocal(device.index or 0)
     if need_host:
-        host_k = torch.empty(w.layers * layer_k, dtype=torch.uint8, pin_memory=True)
-        host_v = torch.empty(w.layers * layer_v, dtype=torch.uint8, pin_memory=True)
+        with numa:
+            host_k = torch.empty(w.layers * layer_k, dtype=torch.uint8, pin_memory=True)
+            host_v = torch.empty(w.layers * layer_v, dtype=torch.uint8, pin_memory=True)
     for l in range(w.layers):
         if w.k_type == 1:
             kl = synth.fp16_layer(w, seed, l, q_base, device).view(torch.uint8).reshape(-1)
@@ -453,6 +498,12 @@ def run_ours(args, world, rank, local):
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": peak_src, "traffic": traffic, "traffic_source": traffic_src,
                      "kernel_ms": kernel_ms, "algorithmic_bytes": kbytes},
+        "roofline_stagein": {"bound": "pcie", "kernel": "stagein_gather_kernel (steady plan, alone)",
+                             "achieved": restored * (page_k + page_v) / (gather_steady_ms * 1e-3) / 1e9,
+                             "peak": PCIE_PEAK_GBS, "unit": "GB/s",
+                             "frac": restored * (page_k + page_v) / (gather_steady_ms * 1e-3) / 1e9 / PCIE_PEAK_GBS,
+                             "peak_source": "ncu pcie__throughput peak of PCIe Gen5 x16 on this pool "
+                                            "(profiles/stagein_stageout_pcie_c2.md)"},
         "cold": {"ms_per_step": ms_cold, "stage_bytes_per_step": cold_bytes,
                  "note": "every selected page staged every step (force_reload)"},
         "stagein": {"gather_ms": gather_ms, "bytes": cold_bytes, "GB/s": cold_bytes / (gather_ms * 1e-3) / 1e9,
@@ -561,7 +612,7 @@ def sharded_selection(args, w, world, rank, local):
     host records would be 111 GB of pinned K and V). Returns the line as a dict (rank 0)."""
     import torch
     import kvmem_b200 as K
-    from kvmem_b200.shard import ShardCompute, ShardedSelector, ShardGeometry, page_ranges
+    from kvmem_b200.shard import LseGatherSelector, ShardCompute, ShardedSelector, ShardGeometry, page_ranges
     dev = torch.device("cuda", local)
     P, L, B = w.pages, w.layers, w.page_tokens
     p0, p1 = page_ranges(P, world)[rank]
@@ -576,7 +627,7 @@ def sharded_selection(args, w, world, rank, local):
     qds = [K.RecallContext.make_query(q, w.rows) for q in h["drift"]]
     geo = ShardGeometry(layers=L, rows=w.rows, q_heads=w.q_heads, kv_heads=w.kv_heads, groups=w.groups,
                         total_pages=P, page0=p0, local_pages=lp)
-    sel = ShardedSelector(ShardCompute(ctx))
+    sel = (LseGatherSelector if args.shard_exchange == "lse" else ShardedSelector)(ShardCompute(ctx))
     warm = max(3, min(args.warmup, 5))
     steps = max(5, min(args.steps, 10))
     for i in range(warm):
@@ -617,7 +668,9 @@ def sharded_selection(args, w, world, rank, local):
                 "fixed and rotating needle pages",
         "config": {"workload": w.name, "layers": L, "tokens": w.tokens, "pages": P, "top_k": w.top_k,
                    "parallelism": f"page-range shards x{world}", "pages_per_rank": lp,
-                   "step": "sharded selection (two NCCL all-gathers); stage-in not included",
+                   "exchange": args.shard_exchange,
+                   "step": ("sharded selection (one NCCL all-gather of the page LSE)" if args.shard_exchange == "lse"
+                            else "sharded selection (two NCCL all-gathers)") + "; stage-in not included",
                    "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)"},
         "clocks": clk.summary(), "gpu_launches": launches,
         "roofline": {"bound": "hbm", "kernel": "page_lse_q_kernel (local pages)", "kernel_ms": kernel_ms,
@@ -626,6 +679,22 @@ def sharded_selection(args, w, world, rank, local):
                      "algorithmic_bytes": kbytes_local,
                      "step_GBps_all_ranks": L * P * page_bytes / (ms * 1e-3) / 1e9},
     }
+
+
+def chunk_schedule(layers, chunks, first):
+    """Layer chunks [(l0, n)] as kvm_recall_step cuts them: a first chunk of `first` layers
+    (when 0 < first < layers and chunks > 1), the rest in equal parts."""
+    chunks = max(1, min(chunks, layers))
+    parts, l0 = [], 0
+    if 0 < first < layers and chunks > 1:
+        parts.append((0, first))
+        l0 = first
+    rest = chunks - len(parts)
+    per = -(-(layers - l0) // rest)
+    while l0 < layers:
+        parts.append((l0, min(per, layers - l0)))
+        l0 += per
+    return parts
 
 
 def run_sharded_recall(args, w, world, rank, local):
@@ -638,7 +707,8 @@ def run_sharded_recall(args, w, world, rank, local):
     import torch
     import torch.distributed as dist
     import kvmem_b200 as K
-    from kvmem_b200.shard import ShardCompute, ShardedRecall, ShardedSelector, ShardGeometry, page_ranges
+    from kvmem_b200.shard import (LseGatherSelector, ShardCompute, ShardedRecall, ShardedSelector, ShardGeometry,
+                                  page_ranges)
     assert w.groups == 1, "stage-in geometry of this bench is per-layer selection"
     dev = torch.device("cuda", local)
     P, L, B = w.pages, w.layers, w.page_tokens
@@ -661,9 +731,7 @@ def run_sharded_recall(args, w, world, rank, local):
     else:
         ck, cv = K.ipc_open(local, box[0][0]), K.ipc_open(local, box[0][1])
     ctx = K.RecallContext(local)
-    chunks = max(1, min(args.chunks, L))
-    per = -(-L // chunks)
-    chunk_layers = [(l0, min(per, L - l0)) for l0 in range(0, L, per)]
+    chunk_layers = chunk_schedule(L, args.chunks_sharded, args.first_layers)
     pools, layouts = [], []
     for l0, nl in chunk_layers:
         pools.append(K.ResidencyPool(ctx, nl, P, slots))
@@ -676,8 +744,8 @@ def run_sharded_recall(args, w, world, rank, local):
                  dev_slot_stride=page_v, bytes=page_v)]))
     geo = ShardGeometry(layers=L, rows=w.rows, q_heads=w.q_heads, kv_heads=w.kv_heads, groups=w.groups,
                         total_pages=P, page0=p0, local_pages=lp)
-    rec = ShardedRecall(ShardedSelector(ShardCompute(ctx)), pools, layouts, chunk_layers, geo,
-                        stage_ctas=args.stage_ctas)
+    selector = (LseGatherSelector if args.shard_exchange == "lse" else ShardedSelector)(ShardCompute(ctx))
+    rec = ShardedRecall(selector, pools, layouts, chunk_layers, geo, stage_ctas=args.stage_ctas)
     desc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
                                      tokens=w.tokens, page_tokens=B, groups=w.groups)
     kc = K.RecallContext.make_kcache(h["k_dev"], w.k_type, kv_heads=w.kv_heads, head_dim=w.head_dim,
@@ -742,6 +810,49 @@ def run_sharded_recall(args, w, world, rank, local):
     h2d = world * q_host[0].numel() * 4
     d2h = ids_host.numel() * 4 + n_host.numel() * 4
 
+    # Breakdown: the selection alone (same chunks and collectives, no plan or stage-in), and the
+    # step's collectives alone (per chunk one all-gather of the softmax statistics and one of the
+    # candidates, then the step's all-reduce; same sizes), each max over ranks.
+    def timed_steps(fn, n):
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record(stream)
+        for i in range(n):
+            fn(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(ev0.elapsed_time(ev1) / n, world)
+
+    select_ms = timed_steps(lambda i: rec.step(desc, qs[i % len(qs)], kc, w.keep, w.budget, stage=False),
+                            args.steps)
+    kcand = w.budget - len(w.keep)
+    widest = max(e - b for b, e in page_ranges(P, world))
+    if args.shard_exchange == "lse":  # per chunk: the page LSE of the rank's range
+        bufs = [[torch.zeros(nl * w.rows * w.q_heads * widest, dtype=torch.float32, device=dev)]
+                for _, nl in chunk_layers]
+    else:  # per chunk: softmax statistics, then candidate scores and ids side by side
+        bufs = [[torch.zeros(nl * w.rows * w.q_heads * 2, dtype=torch.float32, device=dev),
+                 torch.zeros(nl * w.groups * kcand * 2, dtype=torch.int32, device=dev)] for _, nl in chunk_layers]
+    outs = [[torch.empty((world,) + a.shape, dtype=a.dtype, device=dev) for a in bl] for bl in bufs]
+    flag = torch.ones(1, dtype=torch.int32, device=dev)
+
+    def collectives(_):
+        for bl, ol in zip(bufs, outs):
+            for a, ga in zip(bl, ol):
+                dist.all_gather_into_tensor(ga, a)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+
+    collectives(0)
+    coll_ms = timed_steps(collectives, args.steps)
+
+    # This rank's stage-in alone: the last step's restores of every chunk gathered again.
+    def gather_again(_):
+        for ci in range(len(chunk_layers)):
+            pools[ci].stage_in_range(layouts[ci], p0, lp, ctas=args.stage_ctas)
+
+    gather_again(0)
+    gather_ms = timed_steps(gather_again, 5)
+
     # The local scorer alone (this rank's pages), for the roofline.
     ldesc = K.RecallContext.make_desc(layers=L, q_heads=w.q_heads, kv_heads=w.kv_heads, head_dim=w.head_dim,
                                       tokens=lp * B, page_tokens=B)
@@ -780,14 +891,28 @@ def run_sharded_recall(args, w, world, rank, local):
                    "head_dim": w.head_dim, "tokens": w.tokens, "page_tokens": B, "pages": P,
                    "top_k": w.top_k, "keep": "first+last", "selection": "per layer",
                    "parallelism": f"page-range shards x{world}", "pages_per_rank": lp, "chunks": len(chunk_layers),
+                   "chunk_layers": [n for _, n in chunk_layers],
                    "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)",
-                   "step": "per layer chunk: local page LSE, NCCL all-gather of softmax statistics, local "
-                           "masses and candidates, NCCL all-gather of candidates, global top-k, replicated "
-                           "residency plan; stage-in of each rank's restored pages (K+V) from its own pinned "
-                           "records into rank 0's paged cache over NVLink (CUDA IPC peer writes); one "
-                           "all-reduce ends the step"},
+                   "exchange": args.shard_exchange,
+                   "step": ("per layer chunk: local page LSE, one NCCL all-gather of it, whole-row masses and "
+                            "top-k on every rank" if args.shard_exchange == "lse" else
+                            "per layer chunk: local page LSE, NCCL all-gather of softmax statistics, local "
+                            "masses and candidates, NCCL all-gather of candidates, global top-k") +
+                           ", replicated residency plan; stage-in of each rank's restored pages (K+V) from its "
+                           "own pinned records into rank 0's paged cache over NVLink (CUDA IPC peer writes); "
+                           "one all-reduce ends the step"},
         "restored_pages_per_step": restored_per_step,
         "stage_bytes_per_step": restored_per_step * (page_k + page_v),
+        "breakdown": {"select_ms": select_ms, "collectives_ms": coll_ms, "scorer_ms": kernel_ms,
+                      "gather_ms": gather_ms,
+                      "collectives_per_step": len(bufs[0]) * len(chunk_layers) + 1,
+                      "exchange": args.shard_exchange,
+                      "note": "select_ms: the step without residency plan and stage-in; collectives_ms: its "
+                              "NCCL all-gathers (page LSE, or statistics and candidates) and the closing "
+                              "all-reduce alone; "
+                              "scorer_ms: this rank's page LSE pass alone; gather_ms: this rank's stage-in "
+                              "of one step alone (its own PCIe link, NVLink writes to the decode GPU); all "
+                              "max over ranks"},
         "clocks": clk.summary(),
         "e2e": {"value": token_layers / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

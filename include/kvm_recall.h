@@ -606,6 +606,25 @@ int kvm_shard_merge(kvm_ctx* ctx, const float* cand_scores, const uint32_t* cand
                     uint32_t k, const uint32_t* keep, uint32_t nkeep, uint32_t budget, uint32_t* out_ids,
                     uint32_t* out_n, uint32_t out_stride, void* stream);
 
+/* One collective per step instead of two: every rank all-gathers the page LSE
+ * of its range and finishes the whole rows itself with the single-GPU kernels.
+ *   kvm_shard_page_lse: page LSE of the rank's pages [page0, page0 +
+ *     local_pages) into lse (device f32 [layers][rows][q_heads][local_pages];
+ *     k and desc as kvm_shard_score_partial). All-gather lse over the ranks
+ *     and lay the ranges side by side in page order:
+ *     [layers][rows][q_heads][pages of the whole history].
+ *   kvm_page_mass_from_lse: softmax over the pages and the head / row means
+ *     of a whole-history LSE (device f32 [layers][rows][q_heads][pages],
+ *     pages = ceil(desc->tokens / desc->page_tokens)) -> mass_rows / mass_mean
+ *     exactly as kvm_score_pages writes them. Then kvm_select_topk over the
+ *     mean rows gives every rank the unsharded selection.
+ * The gathered LSE is layers * rows * q_heads * pages * 4 bytes (config 2,
+ * one layer: 48 KiB); no counterpart in the reference. */
+int kvm_shard_page_lse(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                       uint32_t page0, uint32_t local_pages, float* lse, void* stream);
+int kvm_page_mass_from_lse(kvm_ctx* ctx, const kvm_score_desc* desc, uint32_t rows, const float* lse,
+                           float* mass_rows, float* mass_mean, void* stream);
+
 /* Stage-in of one rank's page range, to the owning decode GPU. The ranks of
  * a page-range partition keep identical residency tables (each plans the same
  * merged selection with kvm_plan_residency: the plan is deterministic), and

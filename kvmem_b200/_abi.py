@@ -160,6 +160,9 @@ SIGNATURES = {
     "kvm_layerwise_accumulate": ([_vp, _vp, _u32, _u32, _i, _vp, _vp, _vp], _i),
     "kvm_layerwise_finish": ([_vp, _vp, _u32, _i, _vp, _vp], _i),
     "kvm_recall_step": ([_vp, C.POINTER(StepDesc), _vp, C.POINTER(StageLayout), _vp, _vp, _vp, _vp], _i),
+    "kvm_shard_page_lse": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _u32, _u32, _vp, _vp],
+                           _i),
+    "kvm_page_mass_from_lse": ([_vp, C.POINTER(ScoreDesc), _u32, _vp, _vp, _vp, _vp], _i),
     "kvm_shard_score_partial": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _u32, _u32, _vp,
                                  _vp], _i),
     "kvm_shard_merge_stats": ([_vp, _vp, _u32, _u32, _vp, _vp], _i),

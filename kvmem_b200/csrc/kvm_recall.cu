@@ -1890,6 +1890,35 @@ int kvm_shard_score_partial(kvm_ctx* c, const kvm_score_desc* desc, const kvm_qu
     return KVM_OK;
 }
 
+int kvm_shard_page_lse(kvm_ctx* c, const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
+                       uint32_t page0, uint32_t local_pages, float* lse, void* stream) {
+    if (!c || !desc || !q || !lse || !local_pages) return KVM_ERR_INVALID_ARGUMENT;
+    if (q->row_ids) return KVM_ERR_UNSUPPORTED;
+    kvm_score_desc local = *desc;
+    local.tokens = uint64_t(local_pages) * desc->page_tokens;
+    LseConfig cfg;
+    KVM_TRY(validate_score(&local, q, k, &cfg));
+    const uint64_t first = uint64_t(page0) * desc->page_tokens;
+    const uint64_t visible = desc->tokens > first ? std::min<uint64_t>(desc->tokens - first, local.tokens) : 0;
+    DeviceGuard guard(c->device);
+    return lse_layers(c, &local, q, k, cfg, 0, local.layers, local_pages, visible, lse,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int kvm_page_mass_from_lse(kvm_ctx* c, const kvm_score_desc* desc, uint32_t rows, const float* lse, float* mass_rows,
+                           float* mass_mean, void* stream) {
+    if (!c || !desc || !lse || !rows || !desc->layers || !desc->page_tokens || !desc->kv_heads ||
+        desc->q_heads % desc->kv_heads)
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (desc->groups != 1 && desc->groups != desc->kv_heads) return KVM_ERR_INVALID_ARGUMENT;
+    if (!mass_rows && !mass_mean) return KVM_OK;
+    const uint32_t pages = uint32_t((desc->tokens + desc->page_tokens - 1) / desc->page_tokens);
+    if (!pages) return KVM_ERR_INVALID_ARGUMENT;
+    DeviceGuard guard(c->device);
+    return normalize_layers(c, desc, rows, 0, desc->layers, pages, lse, nullptr, mass_rows, mass_mean,
+                            static_cast<cudaStream_t>(stream));
+}
+
 int kvm_shard_merge_stats(kvm_ctx* c, const float* gathered, uint32_t ranks, uint32_t count, float* global_stats,
                           void* stream) {
     if (!c || !gathered || !global_stats || !ranks || !count) return KVM_ERR_INVALID_ARGUMENT;

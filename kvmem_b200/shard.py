@@ -19,6 +19,7 @@ logic can run with CPU stand-ins on gloo ranks.
 from __future__ import annotations
 
 import ctypes as C
+import math
 from dataclasses import dataclass
 from typing import Optional, Sequence
 
@@ -98,6 +99,24 @@ class ShardCompute:
                                               ci.data_ptr(), self._s()), "kvm_shard_candidates")
         return cs, ci
 
+    def page_lse(self, desc, q, k, geo: ShardGeometry) -> torch.Tensor:
+        lse = torch.empty((geo.layers, geo.rows, geo.q_heads, geo.local_pages), dtype=torch.float32,
+                          device=f"cuda:{self.ctx.device}")
+        A.check(self.lib.kvm_shard_page_lse(self.ctx.h, C.byref(desc), C.byref(q), C.byref(k), geo.page0,
+                                            geo.local_pages, lse.data_ptr(), self._s()), "kvm_shard_page_lse")
+        return lse
+
+    def mass_from_lse(self, desc, geo: ShardGeometry, lse: torch.Tensor) -> torch.Tensor:
+        mass = torch.empty((geo.sel_rows, geo.total_pages), dtype=torch.float32, device=lse.device)
+        A.check(self.lib.kvm_page_mass_from_lse(self.ctx.h, C.byref(desc), geo.rows, lse.data_ptr(), None,
+                                                mass.data_ptr(), self._s()), "kvm_page_mass_from_lse")
+        return mass
+
+    def select_topk(self, mass: torch.Tensor, keep: Sequence[int], budget: int):
+        ids = torch.zeros((mass.shape[0], budget), dtype=torch.int32, device=mass.device)
+        n = torch.zeros((mass.shape[0],), dtype=torch.int32, device=mass.device)
+        return self.ctx.select_topk(mass, keep, budget, out_ids=ids, out_n=n, stream=torch.cuda.current_stream())
+
     def merge(self, cs: torch.Tensor, ci: torch.Tensor, world: int, geo: ShardGeometry, keep: Sequence[int],
               k: int, budget: int):
         ids = torch.zeros((geo.sel_rows, budget), dtype=torch.int32, device=cs.device)
@@ -154,6 +173,44 @@ class ShardedSelector:
         cs, ci = self.compute.candidates(mass, geo, keep, kcand)
         gs, gi = self._all_gather_pair(cs, ci)
         return self.compute.merge(gs, gi, self.world, geo, keep, kcand, budget)
+
+
+class LseGatherSelector(ShardedSelector):
+    """Sharded selection with one collective: every rank all-gathers the page LSE of its
+    range (layers x rows x query heads x its pages), lays the ranges side by side and
+    finishes the whole rows itself (softmax over all pages, head / row means, top-k) with
+    the single-GPU kernels, so every rank holds the unsharded selection. The gathered
+    LSE is small (config 2: 48 KiB per layer), so this trades a few KB of NVLink traffic
+    for one all-gather and four small kernels fewer than ShardedSelector."""
+
+    def select(self, desc, q, k, geo: ShardGeometry, keep: Sequence[int], budget: int):
+        keep = sorted(set(int(x) for x in keep))
+        if len(keep) > budget:
+            raise A.KvmError(A.ERR_BUDGET_EXCEEDED, "sharded select")
+        lse = self.compute.page_lse(desc, q, k, geo)  # [L][R][Hq][local pages]
+        full = self._gather_lse(lse, geo)  # [L][R][Hq][total pages]
+        mass = self.compute.mass_from_lse(desc, geo, full)
+        return self.compute.select_topk(mass, keep, budget)
+
+    def _gather_lse(self, lse: torch.Tensor, geo: ShardGeometry) -> torch.Tensor:
+        if self.world == 1:
+            return lse.contiguous()
+        ranges = page_ranges(geo.total_pages, self.world)
+        widest = max(e - b for b, e in ranges)
+        head = lse.shape[:-1]
+        flat = lse.reshape(-1)
+        if lse.shape[-1] != widest:  # equal-sized slices for the collective
+            pad = torch.empty(math.prod(head) * widest, dtype=lse.dtype, device=lse.device)
+            pad[: flat.numel()].copy_(flat)
+            flat = pad
+        g = self._all_gather(flat)  # [world][slice]
+        if all(e - b == widest for b, e in ranges):
+            return g.view((self.world,) + tuple(head) + (widest,)).movedim(0, -2).reshape(
+                tuple(head) + (geo.total_pages,)).contiguous()
+        full = torch.empty(tuple(head) + (geo.total_pages,), dtype=lse.dtype, device=lse.device)
+        for w, (b, e) in enumerate(ranges):
+            full[..., b:e].copy_(g[w, : flat.numel() // widest * (e - b)].view(tuple(head) + (e - b,)))
+        return full
 
 
 class ShardedRecall:

@@ -69,3 +69,25 @@ class CpuShardCompute:
             ids[row, : len(chosen)] = chosen
             n[row] = len(chosen)
         return torch.tensor(ids), torch.tensor(n)
+
+    # The one-collective strategy (LseGatherSelector): local LSE, whole-row masses, top-k.
+    def page_lse(self, desc, q, k, geo):
+        return torch.tensor(lse_pages(self.q, self.k, self.tokens, self.B, self.scale, geo.page0, geo.local_pages))
+
+    def mass_from_lse(self, desc, geo, lse):
+        x = lse.numpy()  # [L][R][Hq][P]
+        m = x.max(axis=-1, keepdims=True)
+        prob = np.exp(x - m) / np.exp(x - m).sum(axis=-1, keepdims=True)
+        return torch.tensor(prob.mean(axis=2).mean(axis=1))  # groups == 1
+
+    def select_topk(self, mass, keep, budget):
+        from oracle import oracle as O
+        m = mass.numpy()
+        ids = np.zeros((m.shape[0], budget), np.int64)
+        n = np.zeros(m.shape[0], np.int64)
+        for row in range(m.shape[0]):
+            rc, got = O.pick_scored(m.shape[1], list(range(m.shape[1])), m[row], keep, budget)
+            assert rc == 0
+            ids[row, : len(got)] = got
+            n[row] = len(got)
+        return torch.tensor(ids), torch.tensor(n)

@@ -16,11 +16,12 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
-def sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D, B, P, T):
+def sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D, B, P, T, lse_gather=False):
     """ShardedRecall over 3 steps with changing queries: every rank gathers the restores of its
     page range from its own records into rank 0's cache (a CUDA-IPC peer mapping on rank 1);
     rank 0 then checks every resident slot against the full host records, byte for byte."""
-    from kvmem_b200.shard import ShardCompute, ShardedRecall, ShardedSelector, ShardGeometry, page_ranges
+    from kvmem_b200.shard import (LseGatherSelector, ShardCompute, ShardedRecall, ShardedSelector, ShardGeometry,
+                                  page_ranges)
     from tests import util as U
     p0, p1 = page_ranges(P, world)[rank]
     lp = p1 - p0
@@ -55,7 +56,8 @@ def sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D,
                  dev_slot_stride=page_v, bytes=page_v)]))
     geo = ShardGeometry(layers=L, rows=1, q_heads=Hq, kv_heads=Hkv, groups=1, total_pages=P, page0=p0,
                         local_pages=lp)
-    rec = ShardedRecall(ShardedSelector(ShardCompute(ctx)), pools, layouts, chunk_layers, geo, stage_ctas=4)
+    cls = LseGatherSelector if lse_gather else ShardedSelector
+    rec = ShardedRecall(cls(ShardCompute(ctx)), pools, layouts, chunk_layers, geo, stage_ctas=4)
     k_local = torch.from_numpy(np.ascontiguousarray(kb[:, p0 * B:p1 * B]).reshape(-1)).to(dev)
     desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=B)
     kc = K.RecallContext.make_kcache(k_local, U.F16, kv_heads=Hkv, head_dim=D, capacity_tokens=lp * B)
@@ -95,7 +97,7 @@ def sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D,
 
 def main(out_dir):
     import kvmem_b200 as K
-    from kvmem_b200.shard import ShardCompute, ShardedSelector, ShardGeometry, page_ranges
+    from kvmem_b200.shard import LseGatherSelector, ShardCompute, ShardedSelector, ShardGeometry, page_ranges
     from tests import util as U
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ["LOCAL_RANK"])
@@ -121,8 +123,10 @@ def main(out_dir):
         geo = ShardGeometry(layers=L, rows=1, q_heads=Hq, kv_heads=Hkv, groups=1, total_pages=P, page0=p0,
                             local_pages=p1 - p0)
         ids, n = ShardedSelector(ShardCompute(ctx)).select(desc, q, kc, geo, keep=[0, P - 1], budget=10)
+        ids2, n2 = LseGatherSelector(ShardCompute(ctx)).select(desc, q, kc, geo, keep=[0, P - 1], budget=10)
         torch.cuda.synchronize()
-        res = {"ids": [ids[l, : int(n[l])].tolist() for l in range(L)], "status": ctx.status()}
+        res = {"ids": [ids[l, : int(n[l])].tolist() for l in range(L)], "status": ctx.status(),
+               "ids_lse": [ids2[l, : int(n2[l])].tolist() for l in range(L)]}
         if rank == 0:
             k_full = torch.from_numpy(kb.reshape(-1).copy()).to(dev)
             full = K.RecallContext.make_kcache(k_full, U.F16, kv_heads=Hkv, head_dim=D, capacity_tokens=P * B)
@@ -130,6 +134,8 @@ def main(out_dir):
             rid, rn = ctx.select_topk(mass.view(L, P), [0, P - 1], 10)
             res["unsharded"] = [rid[l, : int(rn[l])].tolist() for l in range(L)]
         res["recall"] = sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D, B, P, T)
+        res["recall_lse"] = sharded_recall_check(K, ctx, kb, qb, rank, world, local, dev, L, Hq, Hkv, D, B, P, T,
+                                                 lse_gather=True)
         with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
             json.dump(res, f)
         ctx.close()

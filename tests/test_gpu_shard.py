@@ -1,5 +1,10 @@
 """GPU parity of page-range sharded selection (kvm_shard_*), ranks emulated on one GPU.
 
+Both exchanges are covered: statistics + candidates (kvm_shard_score_partial ...
+kvm_shard_merge) and the one-collective page-LSE gather (kvm_shard_page_lse +
+kvm_page_mass_from_lse + kvm_select_topk), which must reproduce the unsharded
+masses bit for bit.
+
 Each emulated rank has its own context (its page LSE stays in its workspace
 between the partial and finish passes); the all-gathers are torch.stack. The
 sharded masses must equal the unsharded kvm_score_pages masses (fp32 rounding
@@ -85,3 +90,17 @@ def test_emulated_ranks_match_unsharded_and_oracle(world, ktype):
         assert ref_ids[l, : ref_n[l]].tolist() == want.tolist()
     if ktype == U.F16:
         assert compared == L
+
+    # The one-collective exchange: each rank's page LSE (kvm_shard_page_lse), the ranges side
+    # by side, whole-row masses (kvm_page_mass_from_lse): the same LSE values and the same
+    # normaliser as the unsharded call, so the masses and the top-k are identical to it.
+    lses = [comps[r].page_lse(desc, q, kcs[r], geos[r]) for r in range(world)]
+    full_lse = torch.cat(lses, dim=-1)
+    mass2 = comps[0].mass_from_lse(desc, geos[0], full_lse)
+    ids2, n2 = comps[0].select_topk(mass2, keep, budget)
+    torch.cuda.synchronize()
+    assert ctxs[0].status() == 0
+    np.testing.assert_array_equal(mass2.cpu().numpy(), ref_mass.view(L, P).cpu().numpy())
+    ids2, n2 = ids2.cpu().numpy(), n2.cpu().numpy()
+    for l in range(L):
+        assert ids2[l, : n2[l]].tolist() == ref_ids[l, : ref_n[l]].tolist()

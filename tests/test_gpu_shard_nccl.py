@@ -2,7 +2,8 @@
 
 Runs tests/shard_nccl_worker.py under torchrun (one rank per GPU, 127.0.0.1
 rendezvous, bounded by a timeout) and checks that every rank ends with the same
-selection as the unsharded top-k of the whole history, and that the sharded
+selection as the unsharded top-k of the whole history (with either exchange:
+statistics + candidates, or one all-gather of the page LSE), and that the sharded
 recall step (kvmem_b200.shard.ShardedRecall) leaves rank 0's paged cache holding
 exactly the host records of the selected pages, each rank having written the
 pages of its own range (rank 1 through a CUDA-IPC peer mapping).
@@ -32,7 +33,9 @@ def test_two_rank_nccl_sharded_selection(tmp_path):
     res = [json.load(open(tmp_path / f"rank{i}.json")) for i in range(2)]
     assert res[0]["status"] == 0 and res[1]["status"] == 0
     assert res[0]["ids"] == res[1]["ids"] == res[0]["unsharded"]
-    # sharded recall: each rank's restored pages written into rank 0's cache over NVLink
-    for r in res:
-        assert r["recall"]["steps"] == 3 and r["recall"]["status"] == 0
-    assert res[0]["recall"]["bad"] == [], res[0]["recall"]["bad"][:10]
+    assert res[0]["ids_lse"] == res[1]["ids_lse"] == res[0]["unsharded"]
+    # sharded recall (both exchanges): each rank's restored pages written into rank 0's cache over NVLink
+    for key in ("recall", "recall_lse"):
+        for r in res:
+            assert r[key]["steps"] == 3 and r[key]["status"] == 0
+        assert res[0][key]["bad"] == [], res[0][key]["bad"][:10]

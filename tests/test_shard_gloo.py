@@ -1,5 +1,7 @@
-"""Sharded selection on two gloo ranks (CPU): the page partition, the two
-all-gathers and the candidate merge give every rank the unsharded top-k."""
+"""Sharded selection on gloo ranks (CPU): the page partition with either exchange
+(ShardedSelector: statistics and candidate all-gathers; LseGatherSelector: one
+all-gather of the page LSE, ranges of unequal size padded) gives every rank the
+unsharded top-k."""
 import os
 import socket
 
@@ -30,31 +32,32 @@ def problem(seed=0):
     return q, k, T, B, P
 
 
-def worker(rank, world, port, out_q):
+def worker(rank, world, port, out_q, kind):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from kvmem_b200.shard import ShardGeometry, ShardedSelector, page_ranges
+        from kvmem_b200.shard import LseGatherSelector, ShardGeometry, ShardedSelector, page_ranges
         from tests.shard_cpu import CpuShardCompute
         q, k, T, B, P = problem()
         L, R, Hq = q.shape[0], q.shape[1], q.shape[2]
         p0, p1 = page_ranges(P, world)[rank]
         geo = ShardGeometry(layers=L, rows=R, q_heads=Hq, kv_heads=k.shape[2], groups=1, total_pages=P, page0=p0,
                             local_pages=p1 - p0)
-        sel = ShardedSelector(CpuShardCompute(q, k, T, B, 0.25))
+        cls = LseGatherSelector if kind == "lse" else ShardedSelector
+        sel = cls(CpuShardCompute(q, k, T, B, 0.25))
         ids, n = sel.select(None, None, None, geo, keep=[0, P - 1], budget=6)
         out_q.put((rank, ids.numpy().tolist(), n.numpy().tolist()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_selection_equals_unsharded(world):
+@pytest.mark.parametrize("world,kind", [(2, "candidates"), (3, "candidates"), (2, "lse"), (3, "lse")])
+def test_sharded_selection_equals_unsharded(world, kind):
     ctx = mp.get_context("spawn")
     out_q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, world, port, out_q)) for r in range(world)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, out_q, kind)) for r in range(world)]
     for p in procs:
         p.start()
     results = [out_q.get(timeout=120) for _ in range(world)]

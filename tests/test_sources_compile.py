@@ -1,5 +1,6 @@
-"""CPU: every Python file of the repository byte-compiles (scripts that only run
-under torchrun or on a GPU are not imported by the other tests)."""
+"""CPU: every Python file of the package, the tests, the oracle and the entry
+scripts byte-compiles (scripts that only run under torchrun or on a GPU are not
+imported by the other tests)."""
 import os
 import py_compile
 
@@ -8,8 +9,13 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def test_all_python_sources_compile(tmp_path):
     bad = []
-    for d, dirs, files in os.walk(ROOT):
-        dirs[:] = [x for x in dirs if not x.startswith(".") and x not in ("_work", "gpurun_out", "baseline", "_ref")]
+    tops = ["kvmem_b200", "tests", "oracle"]
+    walk = [(ROOT, [], [f for f in os.listdir(ROOT) if f.endswith(".py")])]
+    for t in tops:
+        for d, dirs, files in os.walk(os.path.join(ROOT, t)):
+            dirs[:] = [x for x in dirs if not x.startswith((".", "_"))]
+            walk.append((d, dirs, files))
+    for d, _, files in walk:
         for f in files:
             if f.endswith(".py"):
                 try:
