@@ -181,6 +181,24 @@ int kvm_score_pages(kvm_ctx* ctx, const kvm_score_desc* desc, const kvm_query* q
 int kvm_score_pages_noalloc(const kvm_score_desc* desc, const kvm_query* q, const kvm_kcache* k,
                             float* mass_rows, float* mass_mean, void* stream);
 
+/* ------------------------------------------------------------ score frame */
+
+/* The Query recall's score frame. Replaces kvmem::query_score_frame
+ * (kvmem/src/host/graph_recall.cpp:269-293), host code (no device work):
+ *   n = ceil(accepted / block_tokens) pages; page i starts at token
+ *   i*block_tokens and holds min(block_tokens, accepted - start) tokens;
+ *   score_mask[i] = 1, except that when n > budget and sink + recent < n the
+ *   first `sink` and last `recent` pages are 0 (they are kept, not scored);
+ *   transport_mask[i] = (n > budget), except 0 for every `fixed` page.
+ * Outputs are host arrays of at least `capacity` entries (each may be NULL);
+ * *n_out = n. block_tokens or budget 0, or a fixed page >= n, is
+ * KVM_ERR_INVALID_ARGUMENT (the reference's std::invalid_argument); n above
+ * capacity or UINT32_MAX is KVM_ERR_LENGTH. score_mask feeds kvm_meank_score
+ * and kvm_layerwise_accumulate; the fixed pages are the pickers' keep list. */
+int kvm_query_score_frame(uint64_t accepted, uint32_t block_tokens, uint32_t budget, uint32_t sink, uint32_t recent,
+                          const uint32_t* fixed, uint32_t nfixed, uint64_t capacity, uint64_t* starts,
+                          uint32_t* counts, uint8_t* score_mask, uint8_t* transport_mask, uint64_t* n_out);
+
 /* ------------------------------------------------------------------ top-k */
 
 /* Budgeted top-k with keep pages, one selection per score row. Replaces

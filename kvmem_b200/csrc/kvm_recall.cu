@@ -894,6 +894,29 @@ int kvm_select_topk(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pa
                        out_stride, static_cast<cudaStream_t>(stream));
 }
 
+int kvm_query_score_frame(uint64_t accepted, uint32_t block_tokens, uint32_t budget, uint32_t sink, uint32_t recent,
+                          const uint32_t* fixed, uint32_t nfixed, uint64_t capacity, uint64_t* starts,
+                          uint32_t* counts, uint8_t* score_mask, uint8_t* transport_mask, uint64_t* n_out) {
+    if (!block_tokens || !budget || (nfixed && !fixed)) return KVM_ERR_INVALID_ARGUMENT;
+    const uint64_t n = accepted / block_tokens + (accepted % block_tokens != 0);
+    if (n > UINT32_MAX || n > capacity) return KVM_ERR_LENGTH;
+    for (uint32_t i = 0; i < nfixed; ++i)
+        if (fixed[i] >= n) return KVM_ERR_INVALID_ARGUMENT;
+    const bool transported = n > budget;
+    const bool trim = transported && uint64_t(sink) + recent < n;  // sink + recent < n <= UINT32_MAX
+    for (uint64_t i = 0; i < n; ++i) {
+        const uint64_t start = i * block_tokens;
+        if (starts) starts[i] = start;
+        if (counts) counts[i] = uint32_t(std::min<uint64_t>(block_tokens, accepted - start));
+        if (score_mask) score_mask[i] = (trim && (i < sink || i >= n - recent)) ? 0 : 1;
+        if (transport_mask) transport_mask[i] = transported ? 1 : 0;
+    }
+    if (transport_mask)
+        for (uint32_t i = 0; i < nfixed; ++i) transport_mask[fixed[i]] = 0;
+    if (n_out) *n_out = n;
+    return KVM_OK;
+}
+
 int kvm_select_topk_media(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pages, uint32_t score_stride,
                           const uint32_t* keep, uint32_t nkeep, uint32_t budget, int signed_scores,
                           uint32_t block_tokens, const uint32_t* ranges, uint32_t nranges, uint32_t* out_ids,
