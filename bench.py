@@ -61,7 +61,7 @@ def parse():
                     help="layer chunks of the page-range sharded step (N > 1)")
     ap.add_argument("--shard-exchange", default="lse", choices=["lse", "candidates"],
                     help="N > 1: one all-gather of the page LSE per chunk (lse) or statistics + candidates")
-    ap.add_argument("--first-layers", type=int, default=2,
+    ap.add_argument("--first-layers", type=int, default=1,
                     help="layers of the step's first chunk (starts the stage-in early)")
     ap.add_argument("--kmirror", default="head", choices=["head", "token"],
                     help="config 4: layout of the resident K score mirror (head-major or the engine's token-major)")
