@@ -120,7 +120,15 @@ int ensure_small(kvm_ctx* c, size_t bytes) {
     return KVM_OK;
 }
 
+// The per-call table buffer is rewritten by the next call that needs one: first
+// wait (host side) until the last kernel that read it has finished, so calls on
+// different streams never overwrite a table still in use.
 int ensure_aux(kvm_ctx* c, size_t bytes) {
+    if (!c->aux_done) KVM_CUDA(cudaEventCreateWithFlags(&c->aux_done, cudaEventDisableTiming));
+    if (c->aux_pending) {
+        KVM_CUDA(cudaEventSynchronize(c->aux_done));
+        c->aux_pending = false;
+    }
     if (bytes <= c->aux_bytes) return KVM_OK;
     if (c->aux) {
         cudaDeviceSynchronize();
@@ -131,6 +139,13 @@ int ensure_aux(kvm_ctx* c, size_t bytes) {
     const size_t want = std::max<size_t>(align256(bytes), 1 << 16);
     KVM_CUDA(cudaMalloc(&c->aux, want));
     c->aux_bytes = want;
+    return KVM_OK;
+}
+
+// Marks the table buffer in use until the work enqueued on `s` so far is done.
+int aux_release(kvm_ctx* c, cudaStream_t s) {
+    KVM_CUDA(cudaEventRecord(c->aux_done, s));
+    c->aux_pending = true;
     return KVM_OK;
 }
 
@@ -815,6 +830,7 @@ int kvm_ctx_destroy(kvm_ctx* c) {
     if (c->ws && !c->ws_borrowed) cudaFree(c->ws);
     if (c->small) cudaFree(c->small);
     if (c->aux) cudaFree(c->aux);
+    if (c->aux_done) cudaEventDestroy(c->aux_done);
     for (auto& L : c->copy_lists) {
         if (L.done) cudaEventDestroy(L.done);
         if (L.host) cudaFreeHost(L.host);
@@ -968,7 +984,7 @@ int kvm_select_topk_media(kvm_ctx* c, const float* scores, uint32_t nrows, uint3
                                                                 signed_scores, out_ids, out_n, out_stride, c->status);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
-    return KVM_OK;
+    return aux_release(c, s);
 }
 
 int kvm_pool_create(kvm_ctx* c, uint32_t rows, uint32_t pages, uint32_t slots, kvm_pool** out) {
@@ -1461,7 +1477,7 @@ int kvm_restore_k(kvm_ctx* c, int type, const kvm_restore_item* items, uint32_t 
                                                                        nrot, scale);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
-    return KVM_OK;
+    return aux_release(c, s);
 }
 
 int kvm_propagate_scores(kvm_ctx* c, const float* raw, uint32_t n, const uint64_t* starts,
@@ -1571,7 +1587,7 @@ int kvm_propagate_scores(kvm_ctx* c, const float* raw, uint32_t n, const uint64_
         reinterpret_cast<const uint32_t*>(a + o_insrc), reinterpret_cast<const double*>(a + o_inw), out, c->status);
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
-    return KVM_OK;  // a pageable upload is staged before cudaMemcpyAsync returns: `host` may go
+    return aux_release(c, s);  // a pageable upload is staged before cudaMemcpyAsync returns: `host` may go
 }
 
 int kvm_lrfu_preview(kvm_ctx* c, const float* scores, uint32_t n, const float* prev, uint32_t n_prev, double lambda,

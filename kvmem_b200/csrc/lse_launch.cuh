@@ -26,6 +26,8 @@ struct kvm_ctx {
     size_t small_bytes = 0;
     void* aux = nullptr;  // device copy of per-call host-built tables (propagation weights)
     size_t aux_bytes = 0;
+    cudaEvent_t aux_done = nullptr;  // recorded after the last kernel that read `aux`
+    bool aux_pending = false;
     std::vector<uint32_t> keep_cached;
     bool keep_valid = false;
     uint64_t launches = 0;
