@@ -115,3 +115,33 @@ def test_rejections(ctx):
     ids, n = ctx.select_topk_media(bad, [], 5, block_tokens=4, media_ranges=[])
     torch.cuda.synchronize()
     assert ctx.status() == K._abi.ERR_NONFINITE and int(n[0]) == 0  # reading the status clears it
+
+
+def test_calls_on_two_streams_keep_their_own_groups(ctx):
+    """Back-to-back calls on two streams with different media ranges: the second call's
+    group table must not overwrite the first's while the first kernel may still read it."""
+    pages, block, budget = 4096, 64, 130
+    rng = np.random.default_rng(17)
+    rows = rng.random((8, pages)).astype(np.float32)
+    ranges_a = random_ranges(rng, pages, block, 80)
+    ranges_b = random_ranges(rng, pages, block, 80)
+    s = torch.tensor(rows, device="cuda")
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    outs = []
+    for _ in range(3):
+        with torch.cuda.stream(s1):  # outputs allocated and written on s1
+            ia, na = ctx.select_topk_media(s, [0], budget, block_tokens=block, media_ranges=ranges_a, stream=s1)
+        with torch.cuda.stream(s2):
+            ib, nb = ctx.select_topk_media(s, [0], budget, block_tokens=block, media_ranges=ranges_b, stream=s2)
+        outs.append((ia, na, ib, nb))
+    torch.cuda.synchronize()
+    assert ctx.status() == 0
+    for ia, na, ib, nb in outs:
+        ia, na, ib, nb = ia.cpu().numpy(), na.cpu().numpy(), ib.cpu().numpy(), nb.cpu().numpy()
+        for r in range(len(rows)):
+            rc, exp_a = ref_pick(pages, rows[r], [0], budget, block, ranges_a)
+            rc2, exp_b = ref_pick(pages, rows[r], [0], budget, block, ranges_b)
+            assert rc == 0 and rc2 == 0
+            assert ia[r, : na[r]].tolist() == exp_a.tolist()
+            assert ib[r, : nb[r]].tolist() == exp_b.tolist()
