@@ -199,6 +199,23 @@ int kvm_query_score_frame(uint64_t accepted, uint32_t block_tokens, uint32_t bud
                           const uint32_t* fixed, uint32_t nfixed, uint64_t capacity, uint64_t* starts,
                           uint32_t* counts, uint8_t* score_mask, uint8_t* transport_mask, uint64_t* n_out);
 
+/* The keep set of a Query selection. Replaces KvMemStore::query_fixed_blocks
+ * (kvmem/src/host/kvmem_store.cpp:381-405), host code (no device work), for a
+ * store of ceil(total_tokens / block_tokens) pages:
+ *   budget 0 or pages <= budget: every page; else, each page with its whole
+ *   media group (the closure of scored_media_group, ranges as in
+ *   kvm_select_topk_media): the first `sink` pages, the page of the newest
+ *   media range (the last of `ranges`, when it starts before total_tokens)
+ *   and every `mandatory` page (required: a group that does not fit the
+ *   budget is KVM_ERR_BUDGET_EXCEEDED, a page past the end
+ *   KVM_ERR_INVALID_ARGUMENT), then the last `recent` pages, newest first,
+ *   while they fit. out: host u32 [capacity], ascending; *n_out its length
+ *   (KVM_ERR_LENGTH when capacity is too small). The result is the keep list
+ *   of kvm_select_topk / kvm_select_topk_media. */
+int kvm_query_fixed_blocks(uint64_t total_tokens, uint32_t block_tokens, uint32_t budget, uint32_t sink,
+                           uint32_t recent, const uint32_t* ranges, uint32_t nranges, const uint32_t* mandatory,
+                           uint32_t nmandatory, uint32_t* out, uint32_t capacity, uint32_t* n_out);
+
 /* ------------------------------------------------------------------ top-k */
 
 /* Budgeted top-k with keep pages, one selection per score row. Replaces

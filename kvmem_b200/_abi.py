@@ -122,6 +122,8 @@ SIGNATURES = {
     "kvm_ctx_device_bytes": ([_vp], C.c_size_t),
     "kvm_score_pages": ([_vp, C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _vp, _vp, _vp], _i),
     "kvm_score_pages_noalloc": ([C.POINTER(ScoreDesc), C.POINTER(Query), C.POINTER(KCache), _vp, _vp, _vp], _i),
+    "kvm_query_fixed_blocks": ([C.c_uint64, _u32, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32,
+                                C.POINTER(C.c_uint32), _u32, C.POINTER(C.c_uint32), _u32, C.POINTER(C.c_uint32)], _i),
     "kvm_query_score_frame": ([C.c_uint64, _u32, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, C.c_uint64, _vp,
                                _vp, _vp, _vp, C.POINTER(C.c_uint64)], _i),
     "kvm_select_topk": ([_vp, _vp, _u32, _u32, _u32, C.POINTER(C.c_uint32), _u32, _u32, _i, _vp, _vp, _u32, _vp],

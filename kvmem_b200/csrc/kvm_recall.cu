@@ -910,6 +910,83 @@ int kvm_select_topk(kvm_ctx* c, const float* scores, uint32_t nrows, uint32_t pa
                        out_stride, static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+// Media groups of a row of `pages` pages: each range [first, second) covers pages
+// [first / block, ceil(second / block)) clipped to the row; chains of strictly
+// overlapping spans merge into one group, which is the fixed point that
+// scored_media_group (kvmem/src/host/kvmem_store.cpp:18-32) reaches from any page
+// inside them. gb[p] / ge[p]: first page / one past the last page of p's group
+// (p alone when no range covers it).
+void media_group_table(uint32_t pages, uint32_t block_tokens, const uint32_t* ranges, uint32_t nranges,
+                       std::vector<uint32_t>& gb, std::vector<uint32_t>& ge) {
+    std::vector<std::pair<uint32_t, uint32_t>> spans;
+    for (uint32_t i = 0; i < nranges; ++i) {
+        const uint32_t lo = ranges[2 * i] / block_tokens;
+        const uint32_t hi =
+            uint32_t(std::min<uint64_t>(pages, (uint64_t(ranges[2 * i + 1]) + block_tokens - 1) / block_tokens));
+        if (lo < hi) spans.emplace_back(lo, hi);
+    }
+    std::sort(spans.begin(), spans.end());
+    gb.resize(pages);
+    ge.resize(pages);
+    for (uint32_t p = 0; p < pages; ++p) gb[p] = p, ge[p] = p + 1;
+    for (size_t i = 0; i < spans.size();) {
+        uint32_t b = spans[i].first, e = spans[i].second;
+        size_t j = i + 1;
+        for (; j < spans.size() && spans[j].first < e; ++j) e = std::max(e, spans[j].second);
+        for (uint32_t p = b; p < e; ++p) gb[p] = b, ge[p] = e;
+        i = j;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int kvm_query_fixed_blocks(uint64_t total_tokens, uint32_t block_tokens, uint32_t budget, uint32_t sink,
+                           uint32_t recent, const uint32_t* ranges, uint32_t nranges, const uint32_t* mandatory,
+                           uint32_t nmandatory, uint32_t* out, uint32_t capacity, uint32_t* n_out) {
+    if (!block_tokens || !out || !n_out || (nranges && !ranges) || (nmandatory && !mandatory))
+        return KVM_ERR_INVALID_ARGUMENT;
+    const uint64_t n64 = total_tokens / block_tokens + (total_tokens % block_tokens != 0);
+    if (n64 > UINT32_MAX) return KVM_ERR_LENGTH;
+    const uint32_t n = uint32_t(n64);
+    std::vector<uint8_t> kept(n, 0);
+    if (!budget || n <= budget) {
+        std::fill(kept.begin(), kept.end(), 1);
+    } else {
+        std::vector<uint32_t> gb, ge;
+        media_group_table(n, block_tokens, ranges, nranges, gb, ge);
+        uint32_t count = 0;
+        // One page with its whole group; a required one that does not fit is an error.
+        auto keep = [&](uint32_t id, bool required) -> int {
+            if (id >= n) return KVM_ERR_INVALID_ARGUMENT;
+            uint32_t need = 0;
+            for (uint32_t b = gb[id]; b < ge[id]; ++b) need += !kept[b];
+            if (count + need > budget) return required ? KVM_ERR_BUDGET_EXCEEDED : KVM_OK;
+            for (uint32_t b = gb[id]; b < ge[id]; ++b) kept[b] = 1;
+            count += need;
+            return KVM_OK;
+        };
+        for (uint32_t i = 0; i < std::min(n, sink); ++i) KVM_TRY(keep(i, true));
+        if (nranges && uint64_t(ranges[2 * (nranges - 1)]) < total_tokens)
+            KVM_TRY(keep(ranges[2 * (nranges - 1)] / block_tokens, true));  // the newest media item
+        for (uint32_t i = 0; i < nmandatory; ++i) KVM_TRY(keep(mandatory[i], true));
+        for (uint32_t i = 0; i < std::min(n, recent); ++i) KVM_TRY(keep(n - 1 - i, false));
+    }
+    uint32_t m = 0;
+    for (uint32_t p = 0; p < n; ++p) m += kept[p];
+    if (m > capacity) return KVM_ERR_LENGTH;
+    m = 0;
+    for (uint32_t p = 0; p < n; ++p)
+        if (kept[p]) out[m++] = p;
+    *n_out = m;
+    return KVM_OK;
+}
+
 int kvm_query_score_frame(uint64_t accepted, uint32_t block_tokens, uint32_t budget, uint32_t sink, uint32_t recent,
                           const uint32_t* fixed, uint32_t nfixed, uint64_t capacity, uint64_t* starts,
                           uint32_t* counts, uint8_t* score_mask, uint8_t* transport_mask, uint64_t* n_out) {
@@ -942,26 +1019,10 @@ int kvm_select_topk_media(kvm_ctx* c, const float* scores, uint32_t nrows, uint3
     if ((nkeep && !keep) || (nranges && !ranges)) return KVM_ERR_INVALID_ARGUMENT;
     if (pages > kMediaMaxPages) return KVM_ERR_LENGTH;
     if (score_stride < pages || out_stride < std::min(budget, pages)) return KVM_ERR_INVALID_ARGUMENT;
-    // Media groups: each range covers pages [first / block, ceil(second / block)) (clipped
-    // to the row); chains of strictly overlapping spans merge into one group, which is
-    // what scored_media_group's fixed point reaches from any page inside them.
-    std::vector<std::pair<uint32_t, uint32_t>> spans;
-    for (uint32_t i = 0; i < nranges; ++i) {
-        const uint32_t lo = ranges[2 * i] / block_tokens;
-        const uint32_t hi = uint32_t(std::min<uint64_t>(pages, (uint64_t(ranges[2 * i + 1]) + block_tokens - 1) /
-                                                                   block_tokens));
-        if (lo < hi) spans.emplace_back(lo, hi);
-    }
-    std::sort(spans.begin(), spans.end());
+    std::vector<uint32_t> gb, ge;
+    media_group_table(pages, block_tokens, ranges, nranges, gb, ge);
     std::vector<uint32_t> group(pages);
-    for (uint32_t p = 0; p < pages; ++p) group[p] = p | ((p + 1) << 15);
-    for (size_t i = 0; i < spans.size();) {
-        uint32_t b = spans[i].first, e = spans[i].second;
-        size_t j = i + 1;
-        for (; j < spans.size() && spans[j].first < e; ++j) e = std::max(e, spans[j].second);
-        for (uint32_t p = b; p < e; ++p) group[p] = b | (e << 15);
-        i = j;
-    }
+    for (uint32_t p = 0; p < pages; ++p) group[p] = gb[p] | (ge[p] << 15);
     // Keep pages first, each with its whole group, in the caller's order.
     uint32_t count = 0;
     for (uint32_t i = 0; i < nkeep; ++i) {

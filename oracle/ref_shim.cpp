@@ -112,6 +112,30 @@ int kvref_pick_scored(uint32_t n, const uint32_t* candidates, const double* scor
     });
 }
 
+// KvMemStore::query_fixed_blocks (kvmem/src/host/kvmem_store.cpp:381) on a store
+// of `total_tokens` appended tokens in blocks of `block`, a selection budget of
+// `budget` blocks, sink / recent blocks and media ranges. Exceptions: 1 for
+// std::invalid_argument, 2 for any other (the budget overflow).
+int kvref_query_fixed_blocks(uint32_t total_tokens, uint32_t block, uint32_t budget, uint32_t sink, uint32_t recent,
+                             const uint32_t* ranges, uint32_t nranges, const uint32_t* mandatory, uint32_t nmand,
+                             uint32_t* out, uint32_t* out_n) {
+    return guarded([&] {
+        kvmem::KvMemStoreConfig cfg;
+        cfg.block_tokens = block;
+        cfg.select_budget = budget * block;
+        cfg.sink_blocks = sink;
+        cfg.recent_blocks = recent;
+        kvmem::KvMemStore store(cfg);
+        store.register_append(total_tokens);
+        std::vector<std::pair<uint32_t, uint32_t>> media;
+        for (uint32_t i = 0; i < nranges; ++i) media.push_back({ranges[2 * i], ranges[2 * i + 1]});
+        store.set_media_ranges(media);
+        const auto r = store.query_fixed_blocks(std::vector<uint32_t>(mandatory, mandatory + nmand));
+        std::memcpy(out, r.data(), r.size() * sizeof(uint32_t));
+        *out_n = uint32_t(r.size());
+    });
+}
+
 // plan_residency (kvmem/src/host/memory_contract.cpp:135).
 int kvref_plan_residency(const uint64_t* resident, uint32_t nres, const uint64_t* selected, uint32_t nsel,
                          int force_reload, uint64_t* evict, uint32_t* nevict, uint64_t* retain,
