@@ -96,8 +96,11 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, devices, enabled: bool = True):
+        # devices: CUDA device ordinals of this node to sample (one sampler process for all
+        # of them, so a multi-rank run starts one nvidia-smi, on rank 0, not one per rank)
+        self.devices = [devices] if isinstance(devices, int) else list(devices)
+        self.enabled = enabled
         self.proc = None
         self.rows = []  # (host time, csv fields)
         self.t_begin = self.t_end = 0.0
@@ -108,10 +111,26 @@ class ClockSampler:
             if len(r) >= 9:
                 self.rows.append((time.time(), r))
 
+    def _ids(self):
+        """nvidia-smi ids of the sampled devices: their PCI addresses (right under any
+        CUDA_VISIBLE_DEVICES remapping), else the ordinals."""
+        try:
+            import torch
+            ids = []
+            for d in self.devices:
+                p = torch.cuda.get_device_properties(d)
+                ids.append(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+            return ",".join(ids)
+        except Exception:
+            return ",".join(str(d) for d in self.devices)
+
     def __enter__(self):
         import threading
+        self.t_begin = time.time()
+        if not self.enabled:
+            return self
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self._ids()}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
@@ -635,7 +654,7 @@ def sharded_selection(args, w, world, rank, local):
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0 = ctx.launches
-    with ClockSampler(local) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
         ev0.record()
         for i in range(steps):
             sel.select(desc, qds[(warm + i) % len(qds)], kc, geo, w.keep, w.budget)
@@ -758,7 +777,7 @@ def run_sharded_recall(args, w, world, rank, local):
     barrier(world)
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
@@ -1096,7 +1115,7 @@ def run_replay(args, w, world, rank, local):
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
-    with ClockSampler(local) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):

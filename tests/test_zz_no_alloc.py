@@ -69,3 +69,44 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     rc = lib.kvm_score_pages_noalloc(C.byref(desc), C.byref(q), C.byref(k), None, None,
                                      torch.cuda.current_stream().cuda_stream)
     assert rc == K._abi.ERR_LENGTH
+
+
+def test_noalloc_mask_and_replay_batch_against_oracle():
+    """A replay-shaped batch (4 rows x 5 query heads per KV head: the tcgen05 scorer) with an
+    additive mask (a causal tail per row and a hidden span), through the no-allocation entry
+    point, checked against the FP64 oracle as well as against kvm_score_pages."""
+    import kvmem_b200 as K
+    from oracle import oracle as O
+    lib = K._abi.load()
+    rng = np.random.default_rng(21)
+    L, R, Hq, Hkv, D, T, page = 2, 4, 40, 8, 128, 1024, 128
+    mask = np.zeros((R, T), np.float32)
+    mask[0, 200:400] = -np.inf
+    for r in range(1, R):
+        mask[r, T - 60 * r:] = -np.inf
+    kb = U.make_k(rng, U.F16, L, T, Hkv, D)
+    qb = U.make_q(rng, U.F32, L, R, Hq, D)
+    dev = torch.device("cuda", 0)
+    k_d = torch.from_numpy(kb.reshape(-1).copy()).to(dev)
+    q_d = torch.from_numpy(qb.reshape(-1).copy()).to(dev).view(torch.float32).view(L, R, Hq, D)
+    m_d = torch.from_numpy(mask).to(dev)
+    desc = K.RecallContext.make_desc(layers=L, q_heads=Hq, kv_heads=Hkv, head_dim=D, tokens=T, page_tokens=page,
+                                     mask=m_d)
+    q = K.RecallContext.make_query(q_d, R)
+    k = K.RecallContext.make_kcache(k_d, U.F16, kv_heads=Hkv, head_dim=D, capacity_tokens=T)
+    P = T // page
+    got_rows = torch.full((L, 1, R, P), float("nan"), device="cuda")
+    rc = lib.kvm_score_pages_noalloc(C.byref(desc), C.byref(q), C.byref(k), got_rows.data_ptr(), None,
+                                     torch.cuda.current_stream().cuda_stream)
+    assert rc == K._abi.OK, K._abi.STATUS_NAMES.get(rc)
+    torch.cuda.synchronize()
+    exp = O.page_mass(qb, U.F32, kb, U.F16, layers=L, rows=R, heads=Hq, kv_heads=Hkv, dim=D, tokens=T,
+                      page_tokens=page, scale=float(np.float32(1) / np.sqrt(np.float32(D))), mask=mask)
+    ok, worst, _ = U.close(got_rows.cpu().numpy(), exp, REL, ABS)
+    assert ok, f"noalloc masses differ from the FP64 oracle (worst {worst:.3g})"
+    ctx = K.RecallContext(0)
+    want_rows, _ = ctx.score_pages(desc, q, k, want_mean=False)
+    torch.cuda.synchronize()
+    ok, worst, _ = U.close(got_rows.cpu().numpy(), want_rows.cpu().numpy(), REL, ABS)
+    assert ok, f"noalloc masses differ from kvm_score_pages (worst {worst:.3g})"
+    ctx.close()
