@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--chunks", type=int, default=8)
     ap.add_argument("--chunks-sharded", type=int, default=4,
                     help="layer chunks of the page-range sharded step (N > 1)")
+    ap.add_argument("--graph", action="store_true",
+                    help="N > 1: replay the sharded step as one CUDA graph (at N = 2 it measured the same as the "
+                         "eager step, 3.19 vs 3.21 ms)")
     ap.add_argument("--shard-exchange", default="lse", choices=["lse", "candidates"],
                     help="N > 1: one all-gather of the page LSE per chunk (lse) or statistics + candidates")
     ap.add_argument("--first-layers", type=int, default=1,
@@ -85,25 +88,64 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms around the timed region.
+    """SM clocks and clock-event (throttle) reasons sampled every 100 ms around the timed
+    region, for the GPUs of `devices`, through NVML in a thread of this process (a few
+    cheap driver queries per sample; an `nvidia-smi -lms` process stalled the ranks of a
+    multi-GPU step at every sample, so it is only the fallback where NVML is missing).
 
     The timed region starts only after the first sample has arrived and the sampler
     keeps running until one sample after the region has arrived, so even a region
     shorter than the sampling period is bracketed by samples; the summary uses the
-    samples taken within 250 ms of the region."""
+    samples taken within 250 ms of the region. A multi-rank run samples on rank 0 only,
+    all ranks' GPUs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits: SW power cap, HW slowdown, SW thermal, HW thermal
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+    PERIOD_S = 0.1
 
-    def __init__(self, devices, enabled: bool = True):
-        # devices: CUDA device ordinals of this node to sample (one sampler process for all
-        # of them, so a multi-rank run starts one nvidia-smi, on rank 0, not one per rank)
+    def __init__(self, devices, enabled: bool = True, edges_only: bool = False):
+        # devices: CUDA device ordinals of this node to sample. edges_only: one sample right
+        # before and one right after the region, none inside it (multi-GPU steps: NVML
+        # queries during the region stalled the sharded step by about 1 ms per step at N = 2)
         self.devices = [devices] if isinstance(devices, int) else list(devices)
         self.enabled = enabled
+        self.edges_only = edges_only
+        self.nvml = self.handles = None
         self.proc = None
-        self.rows = []  # (host time, csv fields)
+        self.thread = None
+        self.stop = False
+        self.rows = []  # (host time, [index, sm MHz, max MHz, reasons...])
         self.t_begin = self.t_end = 0.0
+
+    def _pci_ids(self):
+        import torch
+        out = []
+        for d in self.devices:
+            p = torch.cuda.get_device_properties(d)
+            out.append(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+        return out
+
+    def _sample(self, handles, nvml):
+        get_reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        for i, h in enumerate(handles):
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                mx = nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM)
+                bits = get_reasons(h)
+            except Exception:
+                continue
+            flags = ["Active" if bits & self.BITS[k] else "Not Active"
+                     for k in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")]
+            self.rows.append((time.time(), [str(i), str(sm), str(mx), "", hex(bits)] + flags))
+
+    def _nvml_loop(self, handles, nvml):
+        while not self.stop:
+            self._sample(handles, nvml)
+            time.sleep(self.PERIOD_S)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -111,29 +153,40 @@ class ClockSampler:
             if len(r) >= 9:
                 self.rows.append((time.time(), r))
 
-    def _ids(self):
-        """nvidia-smi ids of the sampled devices: their PCI addresses (right under any
-        CUDA_VISIBLE_DEVICES remapping), else the ordinals."""
+    def _start_nvml(self) -> bool:
+        import threading
         try:
-            import torch
-            ids = []
-            for d in self.devices:
-                p = torch.cuda.get_device_properties(d)
-                ids.append(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
-            return ",".join(ids)
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handles = [nvml.nvmlDeviceGetHandleByPciBusId(pid) for pid in self._pci_ids()]
         except Exception:
-            return ",".join(str(d) for d in self.devices)
+            return False
+        self.nvml, self.handles = nvml, handles
+        if self.edges_only:
+            self._sample(handles, nvml)
+            return True
+        self.thread = threading.Thread(target=self._nvml_loop, args=(handles, nvml), daemon=True)
+        self.thread.start()
+        return True
+
+    def _start_smi(self):
+        import threading
+        try:
+            ids = ",".join(self._pci_ids())
+        except Exception:
+            ids = ",".join(str(d) for d in self.devices)
+        self.proc = subprocess.Popen(["nvidia-smi", f"--id={ids}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                     stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        threading.Thread(target=self._read, daemon=True).start()
 
     def __enter__(self):
-        import threading
         self.t_begin = time.time()
         if not self.enabled:
             return self
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self._ids()}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            threading.Thread(target=self._read, daemon=True).start()
+            if not self._start_nvml():
+                self._start_smi()
             t0 = time.time()
             while not self.rows and time.time() - t0 < 5.0:
                 time.sleep(0.01)
@@ -144,9 +197,15 @@ class ClockSampler:
 
     def __exit__(self, *a):
         self.t_end = time.time()
-        if self.proc:
+        if self.edges_only and self.handles is not None:
+            self._sample(self.handles, self.nvml)
+        if self.thread or self.proc:
             while not any(t >= self.t_end for t, _ in self.rows) and time.time() - self.t_end < 1.0:
                 time.sleep(0.01)
+        if self.thread:
+            self.stop = True
+            self.thread.join(timeout=2)
+        if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -163,7 +222,9 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows),
+                "source": ("nvml, right before and after the region" if self.edges_only and self.handles is not None
+                           else "nvml every 100 ms" if self.thread else "nvidia-smi every 200 ms")}
 
 
 def dist_setup(args):
@@ -654,7 +715,7 @@ def sharded_selection(args, w, world, rank, local):
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0 = ctx.launches
-    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
         ev0.record()
         for i in range(steps):
             sel.select(desc, qds[(warm + i) % len(qds)], kc, geo, w.keep, w.budget)
@@ -774,18 +835,33 @@ def run_sharded_recall(args, w, world, rank, local):
     for i in range(args.warmup):
         rec.step(desc, qs[i % len(qs)], kc, w.keep, w.budget)
     torch.cuda.synchronize()
+    # The step as one CUDA graph (the step's queries copied into q_static first): the host
+    # then issues one launch per step instead of a few dozen library calls and collectives.
+    q_static = qs[0].clone()
+    graphed = args.graph and rec.capture(desc, q_static, kc, w.keep, w.budget)
+
+    def run_step(i, q_src=None, non_blocking=False):
+        q = qs[i % len(qs)] if q_src is None else q_src
+        if graphed:
+            q_static.copy_(q, non_blocking=non_blocking)
+            return rec.replay()
+        return rec.step(desc, q, kc, w.keep, w.budget)
+
+    for i in range(2):
+        run_step(i)
+    torch.cuda.synchronize()
     barrier(world)
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
-            rec.step(desc, qs[(args.warmup + i) % len(qs)], kc, w.keep, w.budget)
+            run_step(args.warmup + i)
         ev1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
-    launches = ctx.launches - a0
+    launches = rec.graph_launches * args.steps if graphed else ctx.launches - a0
     ms_step = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
     ctx.check_status("sharded recall steps")
     start = args.warmup + args.steps
@@ -794,7 +870,7 @@ def run_sharded_recall(args, w, world, rank, local):
     import numpy as np
     restored, prev = [], None
     for i in range(start, start + min(args.steps, 8) + 1):
-        ids, n = rec.step(desc, qs[i % len(qs)], kc, w.keep, w.budget)
+        ids, n = run_step(i)
         ih, nh = ids.cpu().numpy(), n.cpu().numpy()
         cur = [set(ih[r, : nh[r]].tolist()) for r in range(L)]
         if prev is not None:
@@ -811,8 +887,11 @@ def run_sharded_recall(args, w, world, rank, local):
     n_host = torch.empty((L,), dtype=torch.int32, pin_memory=True)
 
     def e2e_step(j):
-        q_dev.copy_(q_host[j % len(q_host)], non_blocking=True)
-        ids, n = rec.step(desc, q_dev, kc, w.keep, w.budget)
+        if graphed:  # straight from pinned host memory into the graph's query buffer
+            ids, n = run_step(j, q_src=q_host[j % len(q_host)], non_blocking=True)
+        else:
+            q_dev.copy_(q_host[j % len(q_host)], non_blocking=True)
+            ids, n = rec.step(desc, q_dev, kc, w.keep, w.budget)
         if rank == 0:
             ids_host.copy_(ids, non_blocking=True)
             n_host.copy_(n, non_blocking=True)
@@ -886,6 +965,7 @@ def run_sharded_recall(args, w, world, rank, local):
     kernel_ms = max_over_ranks(ev0.elapsed_time(ev1) / 5, world)
     kbytes_local = L * lp * page_k
     hbm_peak, peak_src = peaks()
+    rec.release()  # the graph holds NCCL work: drop it before the process group goes
     for p in pools:
         p.close()
     ctx.close()
@@ -912,7 +992,7 @@ def run_sharded_recall(args, w, world, rank, local):
                    "parallelism": f"page-range shards x{world}", "pages_per_rank": lp, "chunks": len(chunk_layers),
                    "chunk_layers": [n for _, n in chunk_layers],
                    "l2": f"inputs larger than L2 ({kbytes_local / 1e9:.1f} GB of K per rank per step)",
-                   "exchange": args.shard_exchange,
+                   "exchange": args.shard_exchange, "cuda_graph": graphed,
                    "step": ("per layer chunk: local page LSE, one NCCL all-gather of it, whole-row masses and "
                             "top-k on every rank" if args.shard_exchange == "lse" else
                             "per layer chunk: local page LSE, NCCL all-gather of softmax statistics, local "
@@ -1115,7 +1195,7 @@ def run_replay(args, w, world, rank, local):
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
-    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):

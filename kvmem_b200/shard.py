@@ -217,8 +217,8 @@ class ShardedRecall:
     """A whole decode-step recall over a page-range partition: selection and stage-in.
 
     The step is cut into layer chunks, pipelined as in kvm_recall_step. Per chunk, on
-    every rank: the sharded selection of the chunk's layers (ShardedSelector: two
-    all-gathers), the residency plan of those rows on this rank's copy of the pool
+    every rank: the sharded selection of the chunk's layers (a ShardedSelector or
+    LseGatherSelector), the residency plan of those rows on this rank's copy of the pool
     (every rank plans the same merged selection with the same deterministic kernel, so
     the copies stay identical without a collective), then, on a side stream, the
     gather of the planned restores that lie in this rank's page range, from this rank's
@@ -243,6 +243,8 @@ class ShardedRecall:
         self.side = torch.cuda.Stream(device=dev)
         self.events = [torch.cuda.Event() for _ in chunk_layers]
         self.flag = torch.ones(1, dtype=torch.int32, device=dev)
+        self.graph = None
+        self.graph_launches = 0
         self.ids = torch.zeros((geo.sel_rows, 1), dtype=torch.int32, device=dev)
         self.n = torch.zeros((geo.sel_rows,), dtype=torch.int32, device=dev)
 
@@ -280,3 +282,44 @@ class ShardedRecall:
         if self.sel.world > 1:
             dist.all_reduce(self.flag, op=dist.ReduceOp.MAX, group=self.sel.group)  # the decode cache is complete
         return self.ids, self.n
+
+    def capture(self, desc, q_static: torch.Tensor, k, keep: Sequence[int], budget: int, *, warmup: int = 2) -> bool:
+        """Records one step (queries read from q_static) into a CUDA graph, so that a step
+        costs one launch on the host instead of a few dozen kernel launches, library calls
+        and collectives. Every rank must call it at the same point; the ranks agree (one
+        all-reduce, outside any graph) to use the graphs only if every rank captured one.
+        Returns whether replay() is available."""
+        ok = 1
+        graph = None
+        launches0 = self.sel.compute.ctx.launches
+        try:
+            s = torch.cuda.Stream(device=q_static.device)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(warmup):
+                    self.step(desc, q_static, k, keep, budget)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            launches0 = self.sel.compute.ctx.launches
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.step(desc, q_static, k, keep, budget)
+            torch.cuda.synchronize()
+        except Exception:
+            ok, graph = 0, None
+        self.graph_launches = self.sel.compute.ctx.launches - launches0 if graph is not None else 0
+        if self.sel.world > 1:
+            t = torch.tensor([ok], dtype=torch.int32, device=q_static.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.sel.group)
+            ok = int(t.item())
+        self.graph = graph if ok else None
+        return self.graph is not None
+
+    def replay(self):
+        """One recorded step (capture() first; refresh q_static before each)."""
+        self.graph.replay()
+        return self.ids, self.n
+
+    def release(self) -> None:
+        """Drops the recorded graph (before the process group is destroyed)."""
+        self.graph = None
