@@ -90,8 +90,8 @@ def peaks():
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons sampled every 100 ms around the timed
     region, for the GPUs of `devices`, through NVML in a thread of this process (a few
-    cheap driver queries per sample; an `nvidia-smi -lms` process stalled the ranks of a
-    multi-GPU step at every sample, so it is only the fallback where NVML is missing).
+    cheap driver queries per sample; `nvidia-smi -lms 200` is the fallback where NVML is
+    missing).
 
     The timed region starts only after the first sample has arrived and the sampler
     keeps running until one sample after the region has arrived, so even a region
@@ -106,13 +106,12 @@ class ClockSampler:
     BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
     PERIOD_S = 0.1
 
-    def __init__(self, devices, enabled: bool = True, edges_only: bool = False):
-        # devices: CUDA device ordinals of this node to sample. edges_only: one sample right
-        # before and one right after the region, none inside it (multi-GPU steps: NVML
-        # queries during the region stalled the sharded step by about 1 ms per step at N = 2)
+    def __init__(self, devices, enabled: bool = True):
+        # devices: CUDA device ordinals of this node to sample (a multi-rank run samples on
+        # rank 0 only; its ranks synchronise after entering the sampler, so the sampler's
+        # start-up never delays one rank's timed region against the others')
         self.devices = [devices] if isinstance(devices, int) else list(devices)
         self.enabled = enabled
-        self.edges_only = edges_only
         self.nvml = self.handles = None
         self.proc = None
         self.thread = None
@@ -153,18 +152,31 @@ class ClockSampler:
             if len(r) >= 9:
                 self.rows.append((time.time(), r))
 
+    _nvml = None  # NVML, initialised once per process (init_nvml), outside every timed region
+
+    @classmethod
+    def init_nvml(cls):
+        """Initialises NVML once, early: its first initialisation stalled the work that followed
+        it for some milliseconds, so it must not happen next to a timed region."""
+        if cls._nvml is None:
+            try:
+                import pynvml as nvml
+                nvml.nvmlInit()
+                cls._nvml = nvml
+            except Exception:
+                cls._nvml = False
+        return cls._nvml or None
+
     def _start_nvml(self) -> bool:
         import threading
+        nvml = self.init_nvml()
+        if nvml is None:
+            return False
         try:
-            import pynvml as nvml
-            nvml.nvmlInit()
             handles = [nvml.nvmlDeviceGetHandleByPciBusId(pid) for pid in self._pci_ids()]
         except Exception:
             return False
         self.nvml, self.handles = nvml, handles
-        if self.edges_only:
-            self._sample(handles, nvml)
-            return True
         self.thread = threading.Thread(target=self._nvml_loop, args=(handles, nvml), daemon=True)
         self.thread.start()
         return True
@@ -197,8 +209,6 @@ class ClockSampler:
 
     def __exit__(self, *a):
         self.t_end = time.time()
-        if self.edges_only and self.handles is not None:
-            self._sample(self.handles, self.nvml)
         if self.thread or self.proc:
             while not any(t >= self.t_end for t, _ in self.rows) and time.time() - self.t_end < 1.0:
                 time.sleep(0.01)
@@ -223,8 +233,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows),
-                "source": ("nvml, right before and after the region" if self.edges_only and self.handles is not None
-                           else "nvml every 100 ms" if self.thread else "nvidia-smi every 200 ms")}
+                "source": "nvml every 100 ms" if self.thread else "nvidia-smi every 200 ms"}
 
 
 def dist_setup(args):
@@ -712,10 +721,10 @@ def sharded_selection(args, w, world, rank, local):
     steps = max(5, min(args.steps, 10))
     for i in range(warm):
         sel.select(desc, qds[i % len(qds)], kc, geo, w.keep, w.budget)
-    barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0 = ctx.launches
-    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+        barrier(world)  # every rank starts together, after rank 0's sampler is up
         ev0.record()
         for i in range(steps):
             sel.select(desc, qds[(warm + i) % len(qds)], kc, geo, w.keep, w.budget)
@@ -850,10 +859,10 @@ def run_sharded_recall(args, w, world, rank, local):
     for i in range(2):
         run_step(i)
     torch.cuda.synchronize()
-    barrier(world)
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+        barrier(world)  # every rank starts together, after rank 0's sampler is up
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
@@ -1194,8 +1203,8 @@ def run_replay(args, w, world, rank, local):
     torch.cuda.synchronize()
     a0 = ctx.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    with ClockSampler(list(range(world)), enabled=rank == 0, edges_only=world > 1) as clk:
+    with ClockSampler(list(range(world)), enabled=rank == 0) as clk:
+        barrier(world)  # every rank starts together, after rank 0's sampler is up
         torch.cuda.nvtx.range_push("timed")
         ev0.record(stream)
         for i in range(args.steps):
@@ -1378,6 +1387,7 @@ def run_reference(args, world, rank, local):
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
+    ClockSampler.init_nvml()
     try:
         if args.impl == "reference":
             run_reference(args, world, rank, local)
