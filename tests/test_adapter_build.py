@@ -1,5 +1,5 @@
 """CPU: the C++ adapters (kvmem_b200/adapter: the memory backend, llama_kvmem_attention_cuda,
-kvmem::PageSoftmaxCuda) and their tests compile against the reference's own headers and link
+kvmem::PageSoftmaxCuda, the page-range sharded recall step) and their tests compile against the reference's own headers and link
 against libkvm_b200.so and the reference build (runs where the reference headers and the
 libraries are present)."""
 import os
@@ -23,3 +23,4 @@ def test_adapter_compiles_against_the_reference_contract(tmp_path):
     assert r.returncode == 0, r.stdout + r.stderr
     assert os.path.exists(os.path.join(tmp_path, "memory_session_test"))
     assert os.path.exists(os.path.join(tmp_path, "adapters_test"))
+    assert os.path.exists(os.path.join(tmp_path, "sharded_step_test"))
