@@ -687,6 +687,49 @@ int kvm_ipc_export(const void* dev_ptr, void* handle);
 int kvm_ipc_open(int device, const void* handle, void** dev_ptr);
 int kvm_ipc_close(int device, void* dev_ptr);
 
+/* ------------------------------------------- prefill page-LSE capture */
+
+/* Causal prompt attention with the page LSE of sampled prompt rows captured in
+ * the same pass. Replaces the engine's prompt attention with capture,
+ * causal_softmax_attention_with_page_lse / try_dense_prompt_page_lse
+ * (backends/patches/ninfer-prefill-page-lse-kv-coverage.patch:30-83, the
+ * capture itself PromptPageLseRows in prompt_page_lse_tile.cuh, :891-1006 of
+ * that patch), for fp16 / bf16 operands (the engine's FP8 KV row codec is not
+ * part of the reference).
+ *   Prompt row i (0 <= i < width) sits at position base + i and attends to
+ *   cache keys 0 .. base + i (K and V of the prompt rows already appended).
+ *   out[i][h]          = softmax_t(scale * <q_ih, K_t,h/G>) . V_t,h/G
+ *   page_lse[s][h][p]  = log sum_{t in page p, t <= base + rows[s]} exp(scale * <q_rows[s],h, K_t,h/G>)
+ *                        (-inf for a page with no visible key; natural log)
+ * q: device [width] rows of q_heads x head_dim elements of `type`, rows
+ * q_row_stride bytes apart, heads q_head_stride apart; k, v: the cache's K and
+ * V views (kvm_kcache: token_stride, head_stride; the layer fields are
+ * unused), capacity_tokens >= base + width; out: device, like q. page_lse:
+ * device f32 [samples][q_heads][pages] (pages >= ceil((base + width) /
+ * page_tokens)), or NULL with samples = 0 (attention only). sample_rows: host,
+ * strictly ascending, < width, at most KVM_PREFILL_MAX_SAMPLES. head_dim 128 or
+ * 256; page_tokens 16, 32 or a multiple of 64; all base pointers and strides
+ * 16-byte aligned. kvm_page_mass_from_lse(desc = {layers 1, q_heads, kv_heads,
+ * page_tokens, tokens = pages * page_tokens, groups 1}, rows = samples) turns
+ * page_lse into the reference's attention_page_mass_from_lse output (softmax
+ * over pages, mean over heads). Asynchronous on `stream`. */
+#define KVM_PREFILL_MAX_SAMPLES 64
+typedef struct kvm_prefill_desc {
+    uint32_t q_heads, kv_heads, head_dim;
+    int32_t type;         /* KVM_F16 or KVM_BF16: q, k, v and out */
+    uint64_t base;        /* cache tokens before prompt row 0 */
+    uint32_t width;       /* prompt rows */
+    float scale;          /* logit scale; 0 selects 1/sqrt(head_dim) */
+    uint32_t page_tokens; /* capture page size */
+    uint32_t pages;       /* capture columns per (sample, head) */
+    uint32_t samples;     /* sampled rows (0: no capture) */
+    uint32_t reserved;
+    const uint32_t* sample_rows;
+} kvm_prefill_desc;
+int kvm_prefill_attention(kvm_ctx* ctx, const kvm_prefill_desc* desc, const void* q, uint64_t q_row_stride,
+                          uint64_t q_head_stride, const kvm_kcache* k, const kvm_kcache* v, void* out,
+                          uint64_t out_row_stride, uint64_t out_head_stride, float* page_lse, void* stream);
+
 /* Bytes of one D-element row of `type` (0 for an unknown type). */
 uint64_t kvm_row_bytes(int type, uint32_t dim);
 

@@ -112,6 +112,15 @@ class Graph(C.Structure):
                 ("nspans", C.c_uint32), ("reserved", C.c_uint32)]
 
 
+class PrefillDesc(C.Structure):
+    _fields_ = [("q_heads", C.c_uint32), ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("type", C.c_int32),
+                ("base", C.c_uint64), ("width", C.c_uint32), ("scale", C.c_float), ("page_tokens", C.c_uint32),
+                ("pages", C.c_uint32), ("samples", C.c_uint32), ("reserved", C.c_uint32),
+                ("sample_rows", C.POINTER(C.c_uint32))]
+
+
+PREFILL_MAX_SAMPLES = 64
+
 SIGNATURES = {
     "kvm_ctx_create": ([_i, C.POINTER(C.c_void_p)], _i),
     "kvm_ctx_destroy": ([_vp], _i),
@@ -179,6 +188,8 @@ SIGNATURES = {
     "kvm_ipc_export": ([_vp, _vp], _i),
     "kvm_ipc_open": ([_i, _vp, C.POINTER(C.c_void_p)], _i),
     "kvm_ipc_close": ([_i, _vp], _i),
+    "kvm_prefill_attention": ([_vp, C.POINTER(PrefillDesc), _vp, _u64, _u64, C.POINTER(KCache), C.POINTER(KCache),
+                               _vp, _u64, _u64, _vp, _vp], _i),
     "kvm_row_bytes": ([_i, _u32], _u64),
     "kvm_ctx_launches": ([_vp], _u64),
 }

@@ -16,6 +16,7 @@
 #include "meank.cuh"
 #include "page_norm.cuh"
 #include "post.cuh"
+#include "prefill_attn.cuh"
 #include "restore.cuh"
 #include "rows.cuh"
 #include "select.cuh"
@@ -2085,6 +2086,84 @@ int kvm_shard_merge(kvm_ctx* c, const float* cand_scores, const uint32_t* cand_i
     ++c->launches;
     KVM_CUDA(cudaGetLastError());
     return KVM_OK;
+}
+
+int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, uint64_t q_row_stride,
+                          uint64_t q_head_stride, const kvm_kcache* k, const kvm_kcache* v, void* out,
+                          uint64_t out_row_stride, uint64_t out_head_stride, float* page_lse, void* stream) {
+    if (!c || !d || !q || !k || !v || !out || !k->data || !v->data) return KVM_ERR_INVALID_ARGUMENT;
+    if (d->head_dim != 128 && d->head_dim != 256) return KVM_ERR_UNSUPPORTED;
+    if (d->type != KVM_F16 && d->type != KVM_BF16) return KVM_ERR_UNSUPPORTED;
+    if (k->type != d->type || v->type != d->type) return KVM_ERR_INVALID_ARGUMENT;
+    if (!d->q_heads || !d->kv_heads || d->q_heads % d->kv_heads) return KVM_ERR_INVALID_ARGUMENT;
+    if (!(d->scale >= 0.f) || !std::isfinite(d->scale)) return KVM_ERR_INVALID_ARGUMENT;
+    if (!d->width) return KVM_OK;
+    const uint64_t keys = d->base + d->width;
+    if (keys > 0x7fffffffull || keys > k->capacity_tokens || keys > v->capacity_tokens) return KVM_ERR_LENGTH;
+    const uint64_t rb = uint64_t(d->head_dim) * 2;
+    auto al16 = [](uint64_t x) { return (x & 15) == 0; };
+    auto p16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!p16(q) || !p16(out) || !p16(k->data) || !p16(v->data) || !al16(q_row_stride) || !al16(q_head_stride) ||
+        !al16(out_row_stride) || !al16(out_head_stride) || !al16(k->token_stride) || !al16(k->head_stride) ||
+        !al16(v->token_stride) || !al16(v->head_stride))
+        return KVM_ERR_UNSUPPORTED;
+    if (q_head_stride < rb || out_head_stride < rb || k->head_stride < rb || v->head_stride < rb ||
+        k->token_stride < rb || v->token_stride < rb || q_row_stride < rb || out_row_stride < rb)
+        return KVM_ERR_INVALID_ARGUMENT;
+    if (d->samples > KVM_PREFILL_MAX_SAMPLES) return KVM_ERR_LENGTH;
+    kvmb::PrefillParams p{};
+    if (d->samples) {
+        if (!page_lse || !d->sample_rows || !d->page_tokens) return KVM_ERR_INVALID_ARGUMENT;
+        if (d->page_tokens != 16 && d->page_tokens != 32 && d->page_tokens % kvmb::kPfKeys) return KVM_ERR_UNSUPPORTED;
+        if (uint64_t(d->pages) * d->page_tokens < keys) return KVM_ERR_LENGTH;
+        for (uint32_t i = 0; i < d->samples; ++i) {
+            if (d->sample_rows[i] >= d->width || (i && d->sample_rows[i] <= d->sample_rows[i - 1]))
+                return KVM_ERR_INVALID_ARGUMENT;
+            p.rows[i] = d->sample_rows[i];
+        }
+        p.lse = page_lse;
+        p.pages = d->pages;
+        p.page_tokens = d->page_tokens;
+        p.samples = d->samples;
+    }
+    TensorMapEncodeFn enc = tensor_map_encoder();
+    if (!enc) return KVM_ERR_CUDA;
+    const CUtensorMapDataType dt =
+        d->type == KVM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMap maps[3];
+    {
+        const cuuint64_t dims[3] = {d->head_dim, d->q_heads, d->width};
+        const cuuint64_t strides[2] = {q_head_stride, q_row_stride};
+        const cuuint32_t box[3] = {64, 1, uint32_t(kvmb::kPfRows)};
+        if (enc(&maps[0], dt, 3, const_cast<void*>(q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KVM_ERR_CUDA;
+    }
+    const kvm_kcache* kv[2] = {k, v};
+    for (int i = 0; i < 2; ++i) {
+        const cuuint64_t dims[3] = {d->head_dim, d->kv_heads, std::min<uint64_t>(kv[i]->capacity_tokens, 0x7fffffffull)};
+        const cuuint64_t strides[2] = {kv[i]->head_stride, kv[i]->token_stride};
+        const cuuint32_t box[3] = {64, 1, uint32_t(kvmb::kPfKeys)};
+        if (enc(&maps[1 + i], dt, 3, const_cast<void*>(kv[i]->data), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return KVM_ERR_CUDA;
+    }
+    p.q_heads = d->q_heads;
+    p.kv_heads = d->kv_heads;
+    p.width = d->width;
+    p.q_tiles = (d->width + kvmb::kPfRows - 1) / kvmb::kPfRows;
+    p.base = uint32_t(d->base);
+    const float scale = d->scale > 0.f ? d->scale : 1.f / std::sqrt(float(d->head_dim));
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = static_cast<uint8_t*>(out);
+    p.out_row = out_row_stride;
+    p.out_head = out_head_stride;
+    p.status = c->status;
+    DeviceGuard guard(c->device);
+    return kvmb::launch_prefill(c, maps, p, d->head_dim, d->type == KVM_BF16, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -168,6 +168,13 @@ int launch_lse_q_kt(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int 
 int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka, int lm, size_t smem,
                   cudaStream_t s);
 
+// Causal prompt attention with page-LSE capture (prefill_attn.cu): maps =
+// the 3-D TMA tensor maps of Q, K and V built by the caller; head_dim 128 or
+// 256; fp16 (bf16 = false) or bf16 operands.
+struct PrefillParams;
+int launch_prefill(kvm_ctx* c, const CUtensorMap* maps, const PrefillParams& p, uint32_t head_dim, bool bf16,
+                   cudaStream_t s);
+
 // Instantiated once each in lse_<type>.cu.
 extern template int launch_lse_kt<KVM_F32>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);
 extern template int launch_lse_kt<KVM_F16>(kvm_ctx*, const LseParams&, int, int, size_t, cudaStream_t);

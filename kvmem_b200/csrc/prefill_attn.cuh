@@ -1,0 +1,441 @@
+// Causal prompt (prefill) attention with the page log-sum-exp of sampled rows
+// captured in the same pass, on the 5th-generation tensor cores (tcgen05).
+//
+// The engine's prefill attention already computes every logit of every prompt
+// row; the page statistics KVMem needs for a few sampled rows (per (row, query
+// head, page): log sum over the page's visible keys of exp(scale * q.k)) are a
+// by-product of its online softmax. The reference captures them inside its FP8
+// prompt kernels (backends/patches/ninfer-prefill-page-lse-kv-coverage.patch:
+// prompt_page_lse_tile.cuh, PromptPageLseRows at :953-984 and the -inf
+// clear of unvisited pages at :925-928, :945-947) instead of a second Q.K^T pass over
+// the sampled rows. This kernel does the same on B200 for fp16 / bf16 caches:
+//
+//  * one CTA per (128 prompt rows, query head); K and V tiles of 64 keys of the
+//    head's KV head (GQA) are loaded by TMA (3-D maps over [tokens][kv_heads]
+//    [head_dim], 64-dim boxes, 128-byte swizzle) into two-stage rings; the
+//    query tile once;
+//  * one thread issues tcgen05.mma kind::f16: S = Q.K^T (M = 128 rows, N = 64
+//    keys, fp32 in tensor memory, double buffered), then O += P.V (M = 128,
+//    N = head_dim, K = 64 keys; V is the MN-major operand straight from its
+//    token-major tile). S of tile j + 2 is issued right after P.V of tile j,
+//    so the tensor core works on one tile while the softmax warps read the
+//    next;
+//  * four softmax warps own one row each per thread (tensor-memory lane =
+//    row): causal mask, online max in the log2 domain with lazy rescaling (the
+//    O accumulator in tensor memory is rescaled only when a row's max grows by
+//    more than 2^8), P = exp2(x - m) written as fp16 / bf16 into a swizzled
+//    shared-memory tile for the P.V MMA, and for a sampled row the page sums
+//    of P, flushed as natural-log page LSE when a page ends;
+//  * the epilogue divides O by the row sum and stores fp16 / bf16 rows.
+// Every wait is bounded: a timeout records KVM_ERR_TIMEOUT, raises the CTA's
+// abort flag, lets in-flight copies and MMAs finish and frees the tensor
+// memory before the CTA exits.
+#pragma once
+#include <cuda.h>
+
+#include "page_mass_tc.cuh"
+
+namespace kvmb {
+
+constexpr int kPfRows = 128;         // prompt rows per CTA (M)
+constexpr int kPfKeys = 64;          // keys per tile
+constexpr int kPfMaxSamples = 64;    // sampled rows per call (the reference's PromptPageLse::max_samples)
+constexpr int kPfThreads = 256;      // warp 0: Q + K loads, 1: MMA, 2: V loads, 3: idle, 4-7: softmax
+constexpr float kPfRescale = 8.f;    // lazy rescale threshold (log2 units)
+
+struct PrefillParams {
+    uint32_t q_heads, kv_heads, width, q_tiles;
+    uint32_t base;        // cache tokens before prompt row 0 (row i sits at base + i)
+    float scale_log2;     // logit scale * log2(e)
+    uint8_t* out;
+    uint64_t out_row, out_head;
+    float* lse;           // [samples][q_heads][pages] or null
+    uint32_t pages, page_tokens, samples, reserved;
+    uint32_t rows[kPfMaxSamples];  // sampled prompt rows, ascending
+    DeviceStatus* status;
+};
+
+__host__ __device__ constexpr uint32_t pf_q_bytes(int KA) { return uint32_t(KA) * kPfRows * 128; }
+__host__ __device__ constexpr uint32_t pf_kv_stage(int KA) { return uint32_t(KA) * kPfKeys * 128; }
+__host__ __device__ constexpr uint32_t pf_p_bytes() { return kPfRows * 128; }
+__host__ __device__ constexpr size_t pf_smem_bytes(int KA) {
+    return 1024 + pf_q_bytes(KA) + 4 * pf_kv_stage(KA) + 2 * pf_p_bytes() + 256;
+}
+// Tensor-memory columns: S double buffer (2 x 64) then O (head_dim).
+__host__ __device__ constexpr uint32_t pf_tmem_cols(int KA) { return KA == 4 ? 512u : 256u; }
+
+// Shared-memory descriptor of an MN-major operand in the 128-byte-swizzle
+// layout: for each K index a row of 64 contiguous MN elements (128 bytes),
+// 8-row groups 1024 bytes apart (stride byte offset), consecutive 64-element
+// MN blocks `lbo` bytes apart (leading byte offset).
+__device__ __forceinline__ uint64_t pf_desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+    return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+           (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 D, A and B both fp16 (fmt 0) or both
+// bf16 (fmt 1), A K-major, B K-major or MN-major (bit 16), N >> 3, M >> 4.
+__host__ __device__ constexpr uint32_t pf_idesc(uint32_t M, uint32_t N, bool bf16, bool b_mn) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn ? 1u : 0u) << 16) |
+           ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// Tiled 3-D TMA load of one box into this CTA's shared memory (this CTA only).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// All lanes poll the barrier (each gets the acquire), then agree.
+__device__ __forceinline__ bool pf_warp_wait(uint64_t* bar, uint32_t parity) {
+    const bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pf_pack2(float a, float b) {
+    if constexpr (BF16) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    } else {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+template <int KA, bool BF16>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, const PrefillParams P) {
+    constexpr uint32_t D = KA * 64;
+    constexpr uint32_t kQ = pf_q_bytes(KA), kStage = pf_kv_stage(KA), kP = pf_p_bytes();
+    constexpr uint32_t kAtomQ = kPfRows * 128, kAtomKV = kPfKeys * 128;
+    constexpr uint32_t kCols = pf_tmem_cols(KA);
+    constexpr uint32_t kColO = 2 * kPfKeys;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    uint8_t* qsm = smem_raw + pad;
+    uint8_t* ksm = qsm + kQ;               // [2] stages
+    uint8_t* vsm = ksm + 2 * kStage;       // [2] stages
+    uint8_t* psm = vsm + 2 * kStage;       // [2] P tiles
+    uint64_t* bars = reinterpret_cast<uint64_t*>(psm + 2 * kP);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;    // [2]
+    uint64_t* v_empty = bars + 7;   // [2]
+    uint64_t* s_full = bars + 9;    // [2]
+    uint64_t* p_full = bars + 11;   // [2]
+    uint64_t* pv_done = bars + 13;  // [2]
+    uint64_t* fin = bars + 15;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t h = blockIdx.x % P.q_heads;
+    const uint32_t qt = P.q_tiles - 1 - blockIdx.x / P.q_heads;  // heaviest (last) row tiles first
+    const uint32_t kvh = h / (P.q_heads / P.kv_heads);
+    const uint32_t r0 = qt * kPfRows, r1 = min(P.width, r0 + kPfRows);
+    const uint32_t n = (P.base + r1 + kPfKeys - 1) / kPfKeys;  // key tiles this CTA visits
+    const uint32_t unmasked = P.base + r0 + 1;                  // keys every row of the tile sees
+
+    if (tid == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&pv_done[i], 1);
+        }
+        mbar_init(fin, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 || warp == 2) {
+        // ---- TMA producers: warp 0 the query tile and K, warp 2 V ----
+        if (lane == 0) {
+            const bool is_k = warp == 0;
+            uint8_t* ring = is_k ? ksm : vsm;
+            uint64_t* full = is_k ? k_full : v_full;
+            uint64_t* empty = is_k ? k_empty : v_empty;
+            const CUtensorMap* map = is_k ? &kmap : &vmap;
+            if (is_k) {
+                mbar_arrive_expect_tx(q_full, kQ);
+#pragma unroll
+                for (int a = 0; a < KA; ++a) tma_load_3d(qsm + a * kAtomQ, &qmap, a * 64, int(h), int(r0), q_full);
+            }
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < n; ++j) {
+                if (*abort_flag) break;
+                const uint32_t s = j & 1;
+                if (j >= 2 && !mbar_wait(&empty[s], ((j - 2) >> 1) & 1)) {
+                    record_error(P.status, KVM_ERR_TIMEOUT, is_k ? 70 : 71);
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], kStage);
+#pragma unroll
+                for (int a = 0; a < KA; ++a)
+                    tma_load_3d(ring + s * kStage + a * kAtomKV, map, a * 64, int(kvh), int(j * kPfKeys), &full[s]);
+                issued = j + 1;
+            }
+            // Every issued copy lands before the CTA frees its shared memory.
+            for (uint32_t j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+                if (!mbar_wait(&full[j & 1], (j >> 1) & 1)) record_error(P.status, KVM_ERR_TIMEOUT, 72);
+            if (is_k && !mbar_wait(q_full, 0)) record_error(P.status, KVM_ERR_TIMEOUT, 73);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue: one thread ----
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = pf_idesc(kPfRows, kPfKeys, BF16, false);
+            constexpr uint32_t idesc_pv = pf_idesc(kPfRows, D, BF16, true);
+            int err = 0;
+            const uint32_t qb = smem_u32(qsm);
+            auto issue_s = [&](uint32_t j) -> bool {
+                const uint32_t s = j & 1;
+                if (!mbar_wait(&k_full[s], (j >> 1) & 1)) return false;
+                tc_fence_after();
+                const uint32_t kb = smem_u32(ksm + s * kStage);
+#pragma unroll
+                for (int a = 0; a < KA; ++a)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma(tmem + s * kPfKeys, tc_desc_sw128(qb + a * kAtomQ + kk * 32),
+                               tc_desc_sw128(kb + a * kAtomKV + kk * 32), idesc_qk, (a | kk) != 0);
+                tc_commit(&s_full[s]);
+                tc_commit(&k_empty[s]);
+                return true;
+            };
+            if (!mbar_wait(q_full, 0)) err = 80;
+            if (!err && !issue_s(0)) err = 81;
+            if (!err && n > 1 && !issue_s(1)) err = 81;
+            for (uint32_t j = 0; j < n && !err; ++j) {
+                if (*abort_flag) {
+                    err = -1;
+                    break;
+                }
+                const uint32_t b = j & 1;
+                if (!mbar_wait(&p_full[b], (j >> 1) & 1) || !mbar_wait(&v_full[b], (j >> 1) & 1)) {
+                    err = 82;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t pb = smem_u32(psm + b * kP), vb = smem_u32(vsm + b * kStage);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma(tmem + kColO, tc_desc_sw128(pb + kk * 32), pf_desc_mn_sw128(vb + kk * 2048, kAtomKV),
+                           idesc_pv, (j | kk) != 0);
+                tc_commit(&pv_done[b]);
+                tc_commit(&v_empty[b]);
+                if (j + 2 < n && !issue_s(j + 2)) {
+                    err = 81;
+                    break;
+                }
+            }
+            if (err > 0) {
+                record_error(P.status, KVM_ERR_TIMEOUT, err);
+                *abort_flag = 1;
+            }
+            // Every MMA this thread issued is complete before the tensor memory is freed.
+            tc_commit(fin);
+            if (!mbar_wait(fin, 0)) record_error(P.status, KVM_ERR_TIMEOUT, 83);
+        }
+    } else if (warp >= 4) {
+        // ---- softmax, page capture and epilogue: thread = row = tensor-memory lane ----
+        const uint32_t row = uint32_t(tid - 128);
+        const uint32_t lane_addr = tmem + ((32u * uint32_t(warp & 3)) << 16);
+        const uint32_t r = r0 + row;
+        const uint32_t pos = P.base + min(r, P.width - 1);  // last key this row sees
+        // Sampled slot of this row (binary search of the ascending list), -1 if none.
+        int slot = -1;
+        if (P.lse && r < P.width) {
+            uint32_t lo = 0, hi = P.samples;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (P.rows[mid] < r) lo = mid + 1;
+                else hi = mid;
+            }
+            if (lo < P.samples && P.rows[lo] == r) slot = int(lo);
+        }
+        float* lse_row = slot >= 0 ? P.lse + (size_t(slot) * P.q_heads + h) * P.pages : nullptr;
+        const uint32_t pt = P.page_tokens;
+        const float c = P.scale_log2;
+        float m_used = -INFINITY, l = 0.f, page_acc = 0.f;
+        bool ok = true;
+        for (uint32_t j = 0; j < n; ++j) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
+                ok = false;
+                break;
+            }
+            const uint32_t b = j & 1;
+            if (!pf_warp_wait(&s_full[b], (j >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float x[kPfKeys];
+            {
+                uint32_t u[kPfKeys];
+                tc_ld32(lane_addr + b * kPfKeys, u);
+                tc_ld32(lane_addr + b * kPfKeys + 32, u + 32);
+                tc_wait_ld(u);
+                tc_wait_ld(u + 32);
+#pragma unroll
+                for (int k = 0; k < kPfKeys; ++k) x[k] = __uint_as_float(u[k]);
+            }
+            const uint32_t k0 = j * kPfKeys;
+            float smax = -INFINITY;
+            if (k0 + kPfKeys > unmasked) {
+#pragma unroll
+                for (int k = 0; k < kPfKeys; ++k)
+                    if (k0 + k > pos) x[k] = -INFINITY;
+            }
+#pragma unroll
+            for (int k = 0; k < kPfKeys; ++k) smax = fmaxf(smax, x[k]);
+            const float mt = smax * c;  // this tile's max in log2 units (-inf: nothing visible)
+            float alpha = 1.f;
+            if (j == 0) {
+                m_used = mt;  // key 0 is visible to every row
+            } else {
+                const bool need = mt > m_used + kPfRescale;
+                if (__any_sync(0xffffffffu, need)) {
+                    if (need) {
+                        alpha = fast_exp2(m_used - mt);
+                        m_used = mt;
+                        l *= alpha;
+                        page_acc *= alpha;
+                    }
+                    // O holds P.V of tiles < j once that MMA is done; rescale this warp's rows.
+                    if (!pf_warp_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll 1
+                    for (uint32_t cc = 0; cc < D; cc += 32) {
+                        uint32_t o[32];
+                        tc_ld32(lane_addr + kColO + cc, o);
+                        tc_wait_ld(o);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tc_st32(lane_addr + kColO + cc, o);
+                    }
+                    tc_wait_st();
+                }
+            }
+            const float mneg = -m_used;
+            float q16[4] = {0.f, 0.f, 0.f, 0.f};  // sums of P over keys 0-15, 16-31, 32-47, 48-63
+#pragma unroll
+            for (int k = 0; k < kPfKeys; ++k) {
+                x[k] = fast_exp2(fmaf(x[k], c, mneg));
+                q16[k >> 4] += x[k];
+            }
+            const float tsum = (q16[0] + q16[1]) + (q16[2] + q16[3]);
+            l += tsum;
+            if (lse_row) {
+                // Page sums of this tile's P; a page's LSE is written when it ends.
+                if (pt >= uint32_t(kPfKeys)) {
+                    page_acc += tsum;
+                    const uint32_t kend = k0 + kPfKeys;
+                    if (kend % pt == 0 || j + 1 == n) {
+                        const uint32_t pg = k0 / pt;
+                        if (pg < P.pages)
+                            lse_row[pg] = page_acc > 0.f ? (m_used + fast_log2(page_acc)) * kLn2 : -INFINITY;
+                        page_acc = 0.f;
+                    }
+                } else {
+                    // Pages of 16 or 32 keys: four or two per tile.
+                    const float part[4] = {pt == 16 ? q16[0] : q16[0] + q16[1], pt == 16 ? q16[1] : q16[2] + q16[3],
+                                           q16[2], q16[3]};
+                    const uint32_t per = uint32_t(kPfKeys) / pt;
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) {
+                        const uint32_t pg = k0 / pt + i;
+                        if (i < per && pg < P.pages)
+                            lse_row[pg] = part[i] > 0.f ? (m_used + fast_log2(part[i])) * kLn2 : -INFINITY;
+                    }
+                }
+            }
+            // P tile b is free once P.V of tile j - 2 is done.
+            if (j >= 2 && !pf_warp_wait(&pv_done[b], ((j - 2) >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            uint8_t* prow = psm + b * kP + row * 128;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+                uint4 v;
+                v.x = pf_pack2<BF16>(x[8 * cc + 0], x[8 * cc + 1]);
+                v.y = pf_pack2<BF16>(x[8 * cc + 2], x[8 * cc + 3]);
+                v.z = pf_pack2<BF16>(x[8 * cc + 4], x[8 * cc + 5]);
+                v.w = pf_pack2<BF16>(x[8 * cc + 6], x[8 * cc + 7]);
+                *reinterpret_cast<uint4*>(prow + ((uint32_t(cc) ^ (row & 7)) << 4)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&p_full[b]);
+        }
+        if (lse_row) {
+            // Pages past the last visited key: no visible key, zero probability.
+            const uint32_t first = (n * kPfKeys + pt - 1) / pt;
+            for (uint32_t pg = first; pg < P.pages; ++pg) lse_row[pg] = -INFINITY;
+        }
+        const bool go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0) != 0;
+        if (go) {
+            // ---- epilogue: O / l ----
+            if (pf_warp_wait(&pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) {
+                tc_fence_after();
+                const float inv = 1.f / l;
+                uint8_t* orow = P.out + size_t(r) * P.out_row + size_t(h) * P.out_head;
+#pragma unroll 1
+                for (uint32_t cc = 0; cc < D; cc += 32) {
+                    uint32_t o[32];
+                    tc_ld32(lane_addr + kColO + cc, o);
+                    tc_wait_ld(o);
+                    if (r < P.width) {
+                        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 2);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            uint4 v;
+                            v.x = pf_pack2<BF16>(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+                            v.y = pf_pack2<BF16>(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+                            v.z = pf_pack2<BF16>(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+                            v.w = pf_pack2<BF16>(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+                            dst[i] = v;
+                        }
+                    }
+                }
+            } else {
+                record_error(P.status, KVM_ERR_TIMEOUT, 84);
+                *abort_flag = 1;
+            }
+        } else if (!ok) {
+            record_error(P.status, KVM_ERR_TIMEOUT, 85);
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+}
+
+}  // namespace kvmb

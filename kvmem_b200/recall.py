@@ -140,6 +140,66 @@ class RecallContext:
         A.check(rc, "kvm_score_pages")
         return out_rows, out_mean
 
+    def prefill_attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, base: int,
+                          sample_rows: Sequence[int] = (), page_tokens: int = 64, pages: Optional[int] = None,
+                          scale: float = 0.0, out: Optional[torch.Tensor] = None,
+                          page_lse: Optional[torch.Tensor] = None, stream=None):
+        """Causal prompt attention with the page LSE of the sampled rows captured in the same pass
+        (kvm_prefill_attention; the engine's causal_softmax_attention_with_page_lse).
+
+        q: [width][q_heads][head_dim] fp16 / bf16 prompt rows at positions base .. base + width - 1;
+        k, v: [capacity][kv_heads][head_dim] cache views holding keys 0 .. base + width - 1.
+        Returns (out [width][q_heads][head_dim], page_lse [samples][q_heads][pages] or None)."""
+        assert q.dim() == 3 and k.dim() == 3 and v.dim() == 3 and q.dtype == k.dtype == v.dtype
+        width, hq, dim = q.shape
+        cap, hkv, _ = k.shape
+        t = _TORCH_QTYPE[q.dtype]
+        d = A.PrefillDesc()
+        d.q_heads, d.kv_heads, d.head_dim, d.type = hq, hkv, dim, t
+        d.base, d.width, d.scale = base, width, scale
+        rows = list(sample_rows)
+        d.samples = len(rows)
+        d.page_tokens = page_tokens
+        d.pages = pages if pages is not None else -(-(base + width) // page_tokens)
+        ids = (C.c_uint32 * max(1, len(rows)))(*rows)
+        d.sample_rows = C.cast(ids, C.POINTER(C.c_uint32))
+        if out is None:
+            out = torch.empty_like(q)
+        if rows and page_lse is None:
+            page_lse = torch.empty((len(rows), hq, d.pages), dtype=torch.float32, device=q.device)
+        es = q.element_size()
+
+        def view(x: torch.Tensor) -> A.KCache:
+            kc = A.KCache()
+            kc.data, kc.type = x.data_ptr(), t
+            kc.token_stride, kc.head_stride = x.stride(0) * es, x.stride(1) * es
+            kc.layer_stride, kc.capacity_tokens = 0, x.shape[0]
+            return kc
+
+        kc, vc = view(k), view(v)
+        rc = self.lib.kvm_prefill_attention(self.h, C.byref(d), q.data_ptr(), q.stride(0) * es, q.stride(1) * es,
+                                            C.byref(kc), C.byref(vc), out.data_ptr(), out.stride(0) * es,
+                                            out.stride(1) * es, page_lse.data_ptr() if rows else None,
+                                            _stream_ptr(stream))
+        A.check(rc, "kvm_prefill_attention")
+        return out, (page_lse if rows else None)
+
+    def page_mass_from_lse(self, desc: A.ScoreDesc, rows: int, lse: torch.Tensor, *, want_rows=True,
+                           want_mean=True, stream=None):
+        """Whole-history page LSE [layers][rows][q_heads][pages] -> (mass_rows, mass_mean) as score_pages."""
+        pages = -(-desc.tokens // desc.page_tokens)
+        dev = lse.device
+        out_rows = torch.empty((desc.layers, desc.groups, rows, pages), dtype=torch.float32, device=dev) \
+            if want_rows else None
+        out_mean = torch.empty((desc.layers, desc.groups, pages), dtype=torch.float32, device=dev) \
+            if want_mean else None
+        rc = self.lib.kvm_page_mass_from_lse(self.h, C.byref(desc), rows, lse.data_ptr(),
+                                             out_rows.data_ptr() if out_rows is not None else None,
+                                             out_mean.data_ptr() if out_mean is not None else None,
+                                             _stream_ptr(stream))
+        A.check(rc, "kvm_page_mass_from_lse")
+        return out_rows, out_mean
+
     def select_topk(self, scores: torch.Tensor, keep: Sequence[int], budget: int, *, signed: bool = False,
                     out_ids: Optional[torch.Tensor] = None, out_n: Optional[torch.Tensor] = None, stream=None):
         """scores [nrows][pages] f32 on the device -> (ids [nrows][min(budget,pages)], n [nrows])."""

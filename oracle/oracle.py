@@ -444,3 +444,57 @@ def restore_k(ktype: int, src: np.ndarray, *, tokens: int, n_head: int, dim: int
     th = np.ascontiguousarray(list(theta)[: n_rot // 2] if theta is not None and n_rot else [1.0], np.float32)
     rc = lib().kvo_restore_k(ktype, src, dst, tokens, n_head, dim, n_rot, pos0, th, nrot)
     return int(rc), dst
+
+
+def prefill_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, base: int, rows, sample_rows=(),
+                      page_tokens: int = 64, pages: int = 0, scale: float = 0.0):
+    """FP64 restatement of causal prompt attention with page-LSE capture (the engine's
+    causal_softmax_attention_with_page_lse; capture semantics of PromptPageLseRows,
+    backends/patches/ninfer-prefill-page-lse-kv-coverage.patch:953-984: per sampled row and
+    query head, page LSE = max + log(sum of exp over the page's visible keys); pages with no
+    visible key stay at the -inf of clear_prompt_page_lse, :925-928 and :945-947).
+
+    q [width][Hq][D], k / v [T][Hkv][D] (any float dtype, read as float64); prompt row i sits at
+    position base + i and sees keys 0 .. base + i. Returns (out [len(rows)][Hq][D] for the listed
+    rows, lse [len(sample_rows)][Hq][pages] natural log)."""
+    width, hq, dim = q.shape
+    hkv = k.shape[1]
+    g = hq // hkv
+    sc = scale if scale > 0 else 1.0 / np.sqrt(dim)
+    pages = pages or -(-(base + width) // page_tokens)
+
+    def logits(r):
+        n = base + r + 1
+        qr = q[r].astype(np.float64)                                   # [Hq][D]
+        kk = k[:n].astype(np.float64)                                  # [n][Hkv][D]
+        kq = np.repeat(kk, g, axis=1)                                  # [n][Hq][D]
+        return sc * np.einsum("hd,nhd->hn", qr, kq), n                 # [Hq][n]
+
+    out = np.zeros((len(rows), hq, dim), np.float64)
+    for i, r in enumerate(rows):
+        s, n = logits(r)
+        m = s.max(axis=1, keepdims=True)
+        p = np.exp(s - m)
+        vv = np.repeat(v[:n].astype(np.float64), g, axis=1)            # [n][Hq][D]
+        out[i] = np.einsum("hn,nhd->hd", p, vv) / p.sum(axis=1)[:, None]
+    lse = np.full((len(sample_rows), hq, pages), -np.inf, np.float64)
+    for i, r in enumerate(sample_rows):
+        s, n = logits(r)
+        npg = -(-n // page_tokens)
+        padded = np.full((hq, npg * page_tokens), -np.inf)
+        padded[:, :n] = s
+        blk = padded.reshape(hq, npg, page_tokens)                     # every page has a visible key
+        m = blk.max(axis=2)
+        lse[i, :, :npg] = m + np.log(np.exp(blk - m[..., None]).sum(axis=2))
+    return out, lse
+
+
+def page_mass_from_lse(lse: np.ndarray) -> np.ndarray:
+    """FP64 page mass of captured prefill LSE [samples][Hq][pages]: softmax over the pages of
+    each (sample, head), then the mean over heads (attention_page_mass_from_lse,
+    ninfer-prefill-page-lse-kv-coverage.patch:6-7, "exactly as in the independent
+    attention_page_mass path": the normalize / average kernels of
+    src/adapter/llama-kvmem-attention-cuda.cu:98-121). Returns [samples][pages]."""
+    m = lse.max(axis=2, keepdims=True)
+    e = np.where(np.isfinite(lse), np.exp(lse - m), 0.0)
+    return (e / e.sum(axis=2, keepdims=True)).mean(axis=1)
