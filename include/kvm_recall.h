@@ -712,7 +712,9 @@ int kvm_ipc_close(int device, void* dev_ptr);
  * 16-byte aligned. kvm_page_mass_from_lse(desc = {layers 1, q_heads, kv_heads,
  * page_tokens, tokens = pages * page_tokens, groups 1}, rows = samples) turns
  * page_lse into the reference's attention_page_mass_from_lse output (softmax
- * over pages, mean over heads). Asynchronous on `stream`. */
+ * over pages, mean over heads). Long histories split each row tile's keys
+ * into chunks merged by a second pass whose partial rows live in the context's
+ * scoring workspace (as kvm_score_pages's LSE does). Asynchronous on `stream`. */
 #define KVM_PREFILL_MAX_SAMPLES 64
 typedef struct kvm_prefill_desc {
     uint32_t q_heads, kv_heads, head_dim;

@@ -2131,26 +2131,20 @@ int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, 
     const CUtensorMapDataType dt =
         d->type == KVM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const cuuint32_t estr[3] = {1, 1, 1};
-    CUtensorMap maps[3];
-    {
-        const cuuint64_t dims[3] = {d->head_dim, d->q_heads, d->width};
-        const cuuint64_t strides[2] = {q_head_stride, q_row_stride};
-        const cuuint32_t box[3] = {64, 1, uint32_t(kvmb::kPfRows)};
-        if (enc(&maps[0], dt, 3, const_cast<void*>(q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return KVM_ERR_CUDA;
-    }
+    CUtensorMap maps[2];
     const kvm_kcache* kv[2] = {k, v};
     for (int i = 0; i < 2; ++i) {
         const cuuint64_t dims[3] = {d->head_dim, d->kv_heads, std::min<uint64_t>(kv[i]->capacity_tokens, 0x7fffffffull)};
         const cuuint64_t strides[2] = {kv[i]->head_stride, kv[i]->token_stride};
         const cuuint32_t box[3] = {64, 1, uint32_t(kvmb::kPfKeys)};
-        if (enc(&maps[1 + i], dt, 3, const_cast<void*>(kv[i]->data), dims, strides, box, estr,
+        if (enc(&maps[i], dt, 3, const_cast<void*>(kv[i]->data), dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return KVM_ERR_CUDA;
     }
+    p.q = static_cast<const uint8_t*>(q);
+    p.q_row = q_row_stride;
+    p.q_head = q_head_stride;
     p.q_heads = d->q_heads;
     p.kv_heads = d->kv_heads;
     p.width = d->width;
@@ -2163,6 +2157,40 @@ int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, 
     p.out_head = out_head_stride;
     p.status = c->status;
     DeviceGuard guard(c->device);
+    // Key-range split: one CTA per SM, so the (row tile, head) pairs run in waves of num_sms;
+    // cutting each pair's key tiles into S chunks (whole capture pages each) fills the last
+    // wave at the price of a merge pass over S partial rows. S minimises the modelled time
+    // (waves x (tiles per chunk x ~1.1 us + ~6 us per CTA) + merge bytes at ~6 TB/s);
+    // KVM_PREFILL_SPLITS overrides it (tests use it to reach the merge on small problems).
+    p.granule = d->samples && d->page_tokens > uint32_t(kvmb::kPfKeys) ? d->page_tokens / kvmb::kPfKeys : 1;
+    const uint64_t pairs = uint64_t(p.q_tiles) * d->q_heads;
+    const uint64_t tiles = (keys + kvmb::kPfKeys - 1) / kvmb::kPfKeys;
+    const uint64_t row_bytes_f32 = uint64_t(d->width) * d->q_heads * (uint64_t(d->head_dim) * 4 + 8);
+    uint32_t splits = 1;
+    double best = 0;
+    for (uint32_t sp = 1; sp <= 16; ++sp) {
+        const uint64_t chunk = ((tiles + sp - 1) / sp + p.granule - 1) / p.granule * p.granule;
+        if (sp > 1 && (sp - 1) * chunk >= tiles) break;  // an empty chunk: no finer split helps
+        const uint64_t waves = (pairs * sp + c->num_sms - 1) / c->num_sms;
+        const double t = double(waves) * (double(chunk) * 1.1 + 6.0) +
+                         (sp > 1 ? 4.0 + double(sp + 1) * double(row_bytes_f32) / 6e6 : 0.0);
+        if (sp == 1 || t < best) best = t, splits = sp;
+    }
+    if (const char* e = std::getenv("KVM_PREFILL_SPLITS")) {
+        const long v = std::strtol(e, nullptr, 10);
+        if (v >= 1 && v <= 64) splits = uint32_t(v);
+    }
+    p.splits = splits;
+    if (splits > 1) {
+        const size_t rows = size_t(splits) * d->width * d->q_heads;
+        const size_t ml_off = (rows * d->head_dim * 4 + 255) / 256 * 256;
+        if (ensure_ws(c, ml_off + rows * 8) != KVM_OK) {
+            p.splits = 1;  // a bound workspace too small for the partial rows
+        } else {
+            p.part_o = static_cast<float*>(c->ws);
+            p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(c->ws) + ml_off);
+        }
+    }
     return kvmb::launch_prefill(c, maps, p, d->head_dim, d->type == KVM_BF16, static_cast<cudaStream_t>(stream));
 }
 

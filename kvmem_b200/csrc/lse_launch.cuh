@@ -169,7 +169,7 @@ int launch_lse_tc(kvm_ctx* c, const CUtensorMap& map, const LseParams& p, int ka
                   cudaStream_t s);
 
 // Causal prompt attention with page-LSE capture (prefill_attn.cu): maps =
-// the 3-D TMA tensor maps of Q, K and V built by the caller; head_dim 128 or
+// the 3-D TMA tensor maps of K and V built by the caller; head_dim 128 or
 // 256; fp16 (bf16 = false) or bf16 operands.
 struct PrefillParams;
 int launch_prefill(kvm_ctx* c, const CUtensorMap* maps, const PrefillParams& p, uint32_t head_dim, bool bf16,

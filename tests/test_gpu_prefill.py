@@ -7,7 +7,8 @@ backends/patches/ninfer-blackwell-prefill-page-lse.patch:24-31: base / width / s
 (0, 99, {0,31,32,62,63,64,94,98}), (47, 137, 64 rows 2i), (1003, 1024, {5,20,...,1023}) and
 (36864, 1024, 32 rows 32i+31), at its admission shape D 256, 24 query / 4 KV heads), in bf16
 (the engine's FP8 KV codec is not part of the reference), plus fp16 at D 128 over page sizes 16 to
-256, large-logit needles that make rows rescale their accumulator mid-history, and argument errors.
+256, large-logit needles that make rows rescale their accumulator mid-history, key-range splits
+merged by the second pass, and argument errors.
 
 Tolerances: attention rows, relative L2 <= 1e-2 (bf16) / 3e-3 (fp16) and max |err| <= 2e-2 of the
 row's largest |value| (P and the output are rounded to 16 bits); page LSE within 2e-4 + 1e-5 |lse|
@@ -136,6 +137,18 @@ def test_bf16_d128_and_fp16_d256(ctx):
 def test_attention_only_and_single_row(ctx):
     run(ctx, base=500, width=77, samples=[], hq=8, hkv=2, dim=128, dtype=torch.bfloat16)
     run(ctx, base=0, width=1, samples=[0], hq=4, hkv=1, dim=256, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("splits", [2, 3, 5])
+def test_key_range_split_merge(ctx, monkeypatch, splits):
+    """Each row tile's keys cut into chunks merged by the second pass (forced with
+    KVM_PREFILL_SPLITS): chunks of whole 256-token capture pages, empty trailing chunks and
+    rows that see no key of a chunk (base 0) all give the unsplit result."""
+    monkeypatch.setenv("KVM_PREFILL_SPLITS", str(splits))
+    run(ctx, base=1003, width=300, samples=[5, 20, 63, 85, 196, 299], check=list(range(0, 300, 13)), needles=6)
+    run(ctx, base=700, width=150, samples=[0, 77, 149], hq=8, hkv=2, dim=128, dtype=torch.float16, pt=256,
+        needles=3, seed=splits)
+    run(ctx, base=0, width=260, samples=[0, 1, 200], hq=8, hkv=2, dim=128, dtype=torch.bfloat16, pt=32)
 
 
 def test_argument_errors(ctx):
