@@ -72,6 +72,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU baseline and the reference GPU timings")
     ap.add_argument("--no-c5", action="store_true", help="skip the config-5 sharded-selection key")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill page-LSE capture key")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="time only the prefill page-LSE capture (one GPU) and print its key; for ncu captures")
+    ap.add_argument("--prefill-base", type=int, default=36864,
+                    help="cached tokens before the 1024-row prompt chunk of the prefill case")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the page scorer (no host history, no stage-in); for ncu captures")
@@ -560,6 +565,7 @@ def run_ours(args, world, rank, local):
     del cache_k, cache_v, h
     torch.cuda.empty_cache()
     c5 = None if args.no_c5 else sharded_selection(args, workload_named("c5"), world, rank, local)
+    prefill = None if args.no_prefill else prefill_capture(dev, args.prefill_base)
     line = {
         "metric": METRIC, "value": token_layers / (ms_step * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -608,8 +614,90 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
         "reference_gpu": ref_gpu,
         "c5_sharded": c5,
+        "prefill_page_lse": prefill,
     }
     print(json.dumps(line), flush=True)
+
+
+def prefill_capture(dev, base=36864):
+    """Prefill page statistics, the reference's own long case (base 36864 cached tokens, a
+    1024-row prompt chunk, 24 query / 4 KV heads, head_dim 256, 32 sampled rows 32i+31, pages of
+    64 tokens; docs/benchmarks/ninfer-sm120-prefill-page-lse-20261114.json:43-49), bf16 instead
+    of the engine's FP8 cache:
+      fused     kvm_prefill_attention with capture (attention output + page LSE in one pass);
+      separate  the same attention without capture, then kvm_score_pages over the 32 sampled rows
+                with causal visibility as a -inf bias (the second Q.K^T pass the fusion removes);
+    plus the tcgen05 attention's FLOP rate (4 * heads * head_dim * visible keys summed over rows)
+    against the measured bf16 peak, and flash_attn's causal forward on the same tensors for
+    context (a library kernel, not part of this repository). CUDA events, median of 10 after 3
+    warm-up calls; K + V are 155 MB, above L2. `base` other than 36864 (--prefill-base) gives a
+    smaller case of the same shape for ncu captures."""
+    import torch
+
+    import kvmem_b200 as K
+    try:
+        torch.cuda.synchronize()
+        ctx = K.RecallContext(dev.index or 0)
+        width, hq, hkv, dim = 1024, 24, 4, 256
+        T = base + width
+        g = torch.Generator(device=dev).manual_seed(11)
+        q = torch.randn(width, hq, dim, device=dev, generator=g).bfloat16()
+        k = torch.randn(T, hkv, dim, device=dev, generator=g).bfloat16()
+        v = torch.randn(T, hkv, dim, device=dev, generator=g).bfloat16()
+        samples = [32 * i + 31 for i in range(32)]
+        out = torch.empty_like(q)
+        lse = torch.empty(len(samples), hq, T // 64, device=dev)
+        qs = q[samples].contiguous().view(1, len(samples), hq, dim)
+        pos = torch.tensor([base + r for r in samples], device=dev)
+        mask = torch.where(torch.arange(T, device=dev)[None, :] <= pos[:, None], 0.0, float("-inf")).float()
+        sdesc = K.RecallContext.make_desc(layers=1, q_heads=hq, kv_heads=hkv, head_dim=dim, tokens=T,
+                                          page_tokens=64, mask=mask)
+        sq = K.RecallContext.make_query(qs, len(samples))
+        sk = K.RecallContext.make_kcache(k, K.BF16, kv_heads=hkv, head_dim=dim, capacity_tokens=T)
+
+        def med(fn, it=10):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ts = []
+            for _ in range(it):
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            return statistics.median(ts)
+
+        fused = med(lambda: ctx.prefill_attention(q, k, v, base=base, sample_rows=samples, out=out, page_lse=lse))
+        attn = med(lambda: ctx.prefill_attention(q, k, v, base=base, out=out))
+        stats = med(lambda: ctx.score_pages(sdesc, sq, sk, want_mean=False))
+        ctx.check_status("prefill_capture")
+        flops = 4.0 * hq * dim * sum(base + i + 1 for i in range(width))
+        peak, src = tensor_peak()
+        res = {"config": {"base": base, "width": width, "q_heads": hq, "kv_heads": hkv, "head_dim": dim,
+                          "samples": len(samples), "page_tokens": 64, "dtype": "bf16"},
+               "fused_ms": fused, "attention_only_ms": attn, "separate_ms": attn + stats,
+               "separate_stats_ms": stats, "capture_cost_ms": fused - attn,
+               "attention_tflops": flops / attn / 1e9, "fused_tflops": flops / fused / 1e9,
+               "frac_of_bf16_peak": flops / fused / 1e9 / peak, "peak_tflops": peak, "peak_source": src,
+               "kernel": "prefill_attn_kernel (+prefill_combine_kernel)",
+               "reference_published": {"separate_ms": 31.8095, "fused_ms": 9.74842,
+                                       "hardware": "RTX PRO 6000 Blackwell (sm_120a), FP8 KV",
+                                       "source": "docs/benchmarks/ninfer-sm120-prefill-page-lse-20261114.json"}}
+        try:
+            from flash_attn import flash_attn_func
+            qq, kk, vv = q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0)
+            res["flash_attn_ms"] = med(lambda: flash_attn_func(qq, kk, vv, causal=True))
+        except Exception as e:  # library missing or not built for this GPU: context only
+            res["flash_attn_ms"] = None
+            res["flash_attn_error"] = repr(e)[:120]
+        ctx.close()
+        del q, k, v, out, lse, mask
+        torch.cuda.empty_cache()
+        return res
+    except Exception as e:
+        return {"error": repr(e)[:300]}
 
 
 def workload_named(name):
@@ -1388,6 +1476,11 @@ def main():
     args = parse()
     world, rank, local = dist_setup(args)
     ClockSampler.init_nvml()
+    if args.prefill_only:
+        import torch
+        print(json.dumps({"prefill_page_lse": prefill_capture(torch.device("cuda", local), args.prefill_base)}),
+              flush=True)
+        return
     try:
         if args.impl == "reference":
             run_reference(args, world, rank, local)
