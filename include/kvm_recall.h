@@ -707,7 +707,10 @@ int kvm_ipc_close(int device, void* dev_ptr);
  * unused), capacity_tokens >= base + width; out: device, like q. page_lse:
  * device f32 [samples][q_heads][pages] (pages >= ceil((base + width) /
  * page_tokens)), or NULL with samples = 0 (attention only). sample_rows: host,
- * strictly ascending, < width, at most KVM_PREFILL_MAX_SAMPLES. head_dim 128 or
+ * strictly ascending, < width, at most KVM_PREFILL_MAX_SAMPLES (the engine's
+ * first capture took 64 rows in its launch parameters; its dynamic-sample form,
+ * ninfer-prefill-page-lse-dynamic-samples.patch:22-35, takes as many as the
+ * scratch holds, from device memory, as this one does). head_dim 128 or
  * 256; page_tokens 16, 32 or a multiple of 64; all base pointers and strides
  * 16-byte aligned. kvm_page_mass_from_lse(desc = {layers 1, q_heads, kv_heads,
  * page_tokens, tokens = pages * page_tokens, groups 1}, rows = samples) turns
@@ -715,7 +718,7 @@ int kvm_ipc_close(int device, void* dev_ptr);
  * over pages, mean over heads). Long histories split each row tile's keys
  * into chunks merged by a second pass whose partial rows live in the context's
  * scoring workspace (as kvm_score_pages's LSE does). Asynchronous on `stream`. */
-#define KVM_PREFILL_MAX_SAMPLES 64
+#define KVM_PREFILL_MAX_SAMPLES 4096
 typedef struct kvm_prefill_desc {
     uint32_t q_heads, kv_heads, head_dim;
     int32_t type;         /* KVM_F16 or KVM_BF16: q, k, v and out */

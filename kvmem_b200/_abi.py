@@ -119,7 +119,7 @@ class PrefillDesc(C.Structure):
                 ("sample_rows", C.POINTER(C.c_uint32))]
 
 
-PREFILL_MAX_SAMPLES = 64
+PREFILL_MAX_SAMPLES = 4096
 
 SIGNATURES = {
     "kvm_ctx_create": ([_i, C.POINTER(C.c_void_p)], _i),

@@ -2116,11 +2116,9 @@ int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, 
         if (!page_lse || !d->sample_rows || !d->page_tokens) return KVM_ERR_INVALID_ARGUMENT;
         if (d->page_tokens != 16 && d->page_tokens != 32 && d->page_tokens % kvmb::kPfKeys) return KVM_ERR_UNSUPPORTED;
         if (uint64_t(d->pages) * d->page_tokens < keys) return KVM_ERR_LENGTH;
-        for (uint32_t i = 0; i < d->samples; ++i) {
+        for (uint32_t i = 0; i < d->samples; ++i)
             if (d->sample_rows[i] >= d->width || (i && d->sample_rows[i] <= d->sample_rows[i - 1]))
                 return KVM_ERR_INVALID_ARGUMENT;
-            p.rows[i] = d->sample_rows[i];
-        }
         p.lse = page_lse;
         p.pages = d->pages;
         p.page_tokens = d->page_tokens;
@@ -2191,7 +2189,16 @@ int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, 
             p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(c->ws) + ml_off);
         }
     }
-    return kvmb::launch_prefill(c, maps, p, d->head_dim, d->type == KVM_BF16, static_cast<cudaStream_t>(stream));
+    auto s = static_cast<cudaStream_t>(stream);
+    if (d->samples) {
+        // The sampled rows as a device table (the context's per-call table buffer, reused
+        // once the kernels that read it are done).
+        KVM_TRY(ensure_aux(c, size_t(d->samples) * 4));
+        KVM_CUDA(cudaMemcpyAsync(c->aux, d->sample_rows, size_t(d->samples) * 4, cudaMemcpyHostToDevice, s));
+        p.rows = static_cast<const uint32_t*>(c->aux);
+    }
+    KVM_TRY(kvmb::launch_prefill(c, maps, p, d->head_dim, d->type == KVM_BF16, s));
+    return d->samples ? aux_release(c, s) : KVM_OK;
 }
 
 }  // extern "C"

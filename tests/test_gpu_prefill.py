@@ -151,6 +151,15 @@ def test_key_range_split_merge(ctx, monkeypatch, splits):
     run(ctx, base=0, width=260, samples=[0, 1, 200], hq=8, hkv=2, dim=128, dtype=torch.bfloat16, pt=32)
 
 
+def test_more_samples_than_the_first_capture_took(ctx):
+    """Every row of a 260-row chunk sampled (the dynamic-sample capture, rows from device memory),
+    then a second call with a different list: each matches the oracle."""
+    run(ctx, base=300, width=260, samples=list(range(260)), hq=8, hkv=2, dim=128, dtype=torch.bfloat16,
+        check=[0, 100, 259])
+    run(ctx, base=41, width=200, samples=list(range(1, 200, 3)), hq=8, hkv=2, dim=128, dtype=torch.float16,
+        check=[1, 199], seed=5)
+
+
 def test_argument_errors(ctx):
     import kvmem_b200 as K
     q, k, v = (x.to(DEV) for x in make(1, 64, 64, 8, 2, 128, torch.bfloat16))
@@ -164,8 +173,8 @@ def test_argument_errors(ctx):
         ctx.prefill_attention(q, k, v, base=64, sample_rows=[1], page_tokens=48)
     with pytest.raises(K.KvmError):  # the cache holds fewer keys than base + width
         ctx.prefill_attention(q, k[:100], v[:100], base=64, sample_rows=[1])
-    with pytest.raises(K.KvmError):  # more samples than one capture takes
-        ctx.prefill_attention(q, k, v, base=64, sample_rows=list(range(64)) + [0])
+    with pytest.raises(K.KvmError):  # a repeated sample row
+        ctx.prefill_attention(q, k, v, base=64, sample_rows=list(range(64)) + [63])
     with pytest.raises(K.KvmError):  # head_dim 64 is not served
         q64, k64, v64 = (x.to(DEV) for x in make(1, 64, 64, 8, 2, 64, torch.bfloat16))
         ctx.prefill_attention(q64, k64, v64, base=64)
