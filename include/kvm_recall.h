@@ -710,7 +710,9 @@ int kvm_ipc_close(int device, void* dev_ptr);
  * strictly ascending, < width, at most KVM_PREFILL_MAX_SAMPLES (the engine's
  * first capture took 64 rows in its launch parameters; its dynamic-sample form,
  * ninfer-prefill-page-lse-dynamic-samples.patch:22-35, takes as many as the
- * scratch holds, from device memory, as this one does). head_dim 128 or
+ * scratch holds, from device memory, as this one does above 64 rows: that
+ * table is staged from the host array, which waits for the stream's earlier
+ * work; up to 64 rows travel in the launch and need no copy). head_dim 128 or
  * 256; page_tokens 16, 32 or a multiple of 64; all base pointers and strides
  * 16-byte aligned. kvm_page_mass_from_lse(desc = {layers 1, q_heads, kv_heads,
  * page_tokens, tokens = pages * page_tokens, groups 1}, rows = samples) turns

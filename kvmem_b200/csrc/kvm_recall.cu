@@ -2190,15 +2190,19 @@ int kvm_prefill_attention(kvm_ctx* c, const kvm_prefill_desc* d, const void* q, 
         }
     }
     auto s = static_cast<cudaStream_t>(stream);
-    if (d->samples) {
-        // The sampled rows as a device table (the context's per-call table buffer, reused
-        // once the kernels that read it are done).
+    const bool table = d->samples > uint32_t(kvmb::kPfInlineSamples);
+    if (table) {
+        // More rows than the launch parameters carry: a device table in the context's per-call
+        // table buffer, reused once the kernels that read it are done.
         KVM_TRY(ensure_aux(c, size_t(d->samples) * 4));
         KVM_CUDA(cudaMemcpyAsync(c->aux, d->sample_rows, size_t(d->samples) * 4, cudaMemcpyHostToDevice, s));
         p.rows = static_cast<const uint32_t*>(c->aux);
+    } else {
+        p.rows = nullptr;
+        for (uint32_t i = 0; i < d->samples; ++i) p.rows_inline[i] = d->sample_rows[i];
     }
     KVM_TRY(kvmb::launch_prefill(c, maps, p, d->head_dim, d->type == KVM_BF16, s));
-    return d->samples ? aux_release(c, s) : KVM_OK;
+    return table ? aux_release(c, s) : KVM_OK;
 }
 
 }  // extern "C"

@@ -48,6 +48,7 @@ namespace kvmb {
 constexpr int kPfRows = 128;         // prompt rows per CTA (M)
 constexpr int kPfKeys = 64;          // keys per tile
 constexpr int kPfMaxSamples = 4096;  // sampled rows per call (the reference's scratch decides; 64 by default)
+constexpr int kPfInlineSamples = 64; // up to this many travel in the launch parameters
 constexpr int kPfThreads = 256;      // warp 0: K loads, 1: MMA, 2: V loads, 3: idle, 4-7: softmax
 constexpr float kPfRescale = 8.f;    // lazy rescale threshold (log2 units)
 
@@ -68,7 +69,10 @@ struct PrefillParams {
     uint32_t splits, granule;
     float* part_o;
     float2* part_ml;
-    const uint32_t* rows;  // device: sampled prompt rows, ascending
+    // Sampled prompt rows, ascending: in rows_inline when samples <= kPfInlineSamples
+    // (no copy, no synchronisation), else in the device table `rows`.
+    const uint32_t* rows;
+    uint32_t rows_inline[kPfInlineSamples];
     DeviceStatus* status;
 };
 
@@ -343,10 +347,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             uint32_t lo = 0, hi = P.samples;
             while (lo < hi) {
                 const uint32_t mid = (lo + hi) >> 1;
-                if (__ldg(P.rows + mid) < r) lo = mid + 1;
+                if ((P.rows ? __ldg(P.rows + mid) : P.rows_inline[mid]) < r) lo = mid + 1;
                 else hi = mid;
             }
-            if (lo < P.samples && __ldg(P.rows + lo) == r) slot = int(lo);
+            if (lo < P.samples && (P.rows ? __ldg(P.rows + lo) : P.rows_inline[lo]) == r) slot = int(lo);
         }
         float* lse_row = slot >= 0 ? P.lse + (size_t(slot) * P.q_heads + h) * P.pages : nullptr;
         const uint32_t pt = P.page_tokens;
